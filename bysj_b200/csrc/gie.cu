@@ -1,0 +1,472 @@
+// GIE zonal scatter, forward and backward, for sm_100a.
+//
+//   out[n, 0, :]   = 0
+//   out[n, r+1, c] = inv[n] * sum_{e in seg(n)} zonal[e, r] * radial[e, slot[r], c]
+//
+// Contract of the reference's csrc/gie.cpp:68-228 (normalise after the
+// destination sum).  The reference scatters with one float atomicAdd per
+// (edge, row, channel) and scales in a second pass; here the edges are read
+// in destination (CSR) order, one merge-path partition per warp, each lane
+// owning a slice of the node's [rows, channels] block in registers, and the
+// normalisation is folded into the single store.  No atomics: repeated runs
+// are bit-identical.  The backward writes the per-edge gradients directly
+// (each edge reads only its own node's upstream row) and reduces the
+// inverse-degree gradient per segment from the same unnormalised sums.
+#include "launch.cuh"
+
+namespace bysj {
+namespace {
+
+struct GieArgs {
+  const float* zonal;    // [E, R]
+  const float* radial;   // [E, NR, C]
+  const int64_t* order;
+  const int64_t* slot;   // [R]
+  const float* inv;      // [N]
+  const float* grad;     // backward: [N, R+1, C]
+  const int64_t* dst;    // backward: [E]
+  float* out;            // forward: [N, R+1, C] | backward: grad_inv [N]
+  float* grad_zonal;     // [E, R]
+  float* grad_radial;    // [E, NR, C]
+  int64_t rows, n_radial, channels;
+  int64_t lv;            // R*C/VEC
+  MergePath mp;
+  SplitSlots ss;
+};
+
+template <int VEC>
+__device__ __forceinline__ void ld_l1(const float* p, float (&v)[VEC]) {
+  if constexpr (VEC == 4) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) v[i] = __ldg(p + i);
+  }
+}
+
+// Per-lane geometry of vector k: output row r, radial offset slot*C + c.
+template <int VEC, int NV>
+struct LaneMap {
+  int64_t j[NV];     // vector index (clamped into range)
+  bool ok[NV];
+  int r[NV];
+  int64_t roff[NV];  // slot[r] * C + c
+  int64_t ooff[NV];  // (r + 1) * C + c inside the node block
+  __device__ __forceinline__ void init(const GieArgs& a, int64_t jt, int lane) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int64_t jj = jt + lane + k * kWarp;
+      ok[k] = jj < a.lv;
+      j[k] = ok[k] ? jj : a.lv - 1;
+      const int64_t x = j[k] * VEC;
+      r[k] = static_cast<int>(x / a.channels);
+      const int64_t c = x - r[k] * a.channels;
+      roff[k] = __ldg(a.slot + r[k]) * a.channels + c;
+      ooff[k] = (r[k] + 1) * a.channels + c;
+    }
+  }
+};
+
+template <int VEC, int NV>
+__device__ __forceinline__ void gie_accumulate(const GieArgs& a, const LaneMap<VEC, NV>& L,
+                                               int64_t lo, int64_t hi,
+                                               float (&acc)[NV][VEC]) {
+  for (int64_t s = lo; s < hi; ++s) {
+    const int64_t e = a.order ? __ldg(a.order + s) : s;
+    const float* zr = a.zonal + e * a.rows;
+    const float* rr = a.radial + e * a.n_radial * a.channels;
+    float z[NV];
+    float rv[NV][VEC];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      z[k] = __ldg(zr + L.r[k]);
+      ld_l1<VEC>(rr + L.roff[k], rv[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[k][i] = fmaf(z[k], rv[k][i], acc[k][i]);
+  }
+}
+
+template <int VEC, int NV>
+__global__ void __launch_bounds__(kBlock, 2) gie_fwd_kernel(GieArgs a) {
+  constexpr int TV = kWarp * NV;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int tile = blockIdx.y;
+  const int64_t jt = static_cast<int64_t>(tile) * TV;
+  const int64_t block = (a.rows + 1) * a.channels;
+  LaneMap<VEC, NV> L;
+  L.init(a, jt, lane);
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    float acc[NV][VEC];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[k][i] = 0.0f;
+    gie_accumulate<VEC, NV>(a, L, cur.lo, cur.hi, acc);
+    float* on = a.out + n * block;
+    if (cur.kind == kWhole) {
+      const float inv = __ldg(a.inv + n);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        if (!L.ok[k]) continue;
+        float v[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) v[i] = acc[k][i] * inv;
+        store_f32<VEC>(on + L.ooff[k], v);
+      }
+      if (tile == 0)
+        for (int64_t c = lane; c < a.channels; c += kWarp) on[c] = 0.0f;
+      continue;
+    }
+    float* mine = a.ss.slot(p, cur.kind);
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+      if (L.ok[k]) store_cg<VEC>(mine + L.j[k] * VEC, acc[k]);
+    const int64_t first = a.mp.part_of_first_edge(n);
+    const int64_t last = a.mp.part_of_end(n);
+    if (!arrive_last(a.ss, first, last, tile)) continue;
+    const float inv = __ldg(a.inv + n);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      if (!L.ok[k]) continue;
+      float sum[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) sum[i] = 0.0f;
+      for (int64_t q = first; q <= last; ++q) {
+        float part[VEC];
+        load_cg<VEC>(a.ss.slot(q, q == last ? kHead : kTail) + L.j[k] * VEC, part);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) sum[i] += part[i];
+      }
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) sum[i] *= inv;
+      store_f32<VEC>(on + L.ooff[k], sum);
+    }
+    if (tile == 0)
+      for (int64_t c = lane; c < a.channels; c += kWarp) on[c] = 0.0f;
+  }
+}
+
+// Backward.  Per edge, with gi = g[n] * inv[n] (g rows are re-read from L1):
+//   grad_zonal[e, r]     = sum_c gi[r, c] * radial[e, slot r, c]
+//   grad_radial[e, s, c] = sum_{r: slot r = s} gi[r, c] * zonal[e, r]
+// and per segment grad_inv[n] = <g[n], pre[n]>, where pre is the
+// unnormalised forward sum accumulated exactly as the forward does (sum over
+// the edges first, then one dot product), so cancellation inside the sum is
+// resolved before the upstream weight is applied.
+template <int VEC, int NV>
+__global__ void __launch_bounds__(kBlock, 2) gie_bwd_kernel(GieArgs a) {
+  constexpr int TV = kWarp * NV;
+  extern __shared__ float s_dot[];  // [warps][TV]
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  float* sdot = s_dot + (threadIdx.x >> 5) * TV;
+  const int lane = lane_id();
+  const int64_t block = (a.rows + 1) * a.channels;
+  const int64_t vpr = a.channels / VEC;  // vectors per output row
+  const int64_t radial_row = a.n_radial * a.channels;
+  LaneMap<VEC, NV> L;
+  L.init(a, 0, lane);
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const float inv = __ldg(a.inv + n);
+    const float* gn = a.grad + n * block;
+    float acc[NV][VEC];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[k][i] = 0.0f;
+    for (int64_t s = cur.lo; s < cur.hi; ++s) {
+      const int64_t e = a.order ? __ldg(a.order + s) : s;
+      const float* zr = a.zonal + e * a.rows;
+      const float* rr = a.radial + e * radial_row;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        float rv[VEC], g[VEC];
+        ld_l1<VEC>(rr + L.roff[k], rv);
+        ld_l1<VEC>(gn + L.ooff[k], g);
+        const float z = __ldg(zr + L.r[k]);
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          d = fmaf(g[i] * inv, rv[i], d);
+          acc[k][i] = fmaf(z, rv[i], acc[k][i]);
+        }
+        if (L.ok[k]) sdot[lane + k * kWarp] = d;
+      }
+      __syncwarp();
+      for (int64_t r = lane; r < a.rows; r += kWarp) {
+        float sum = 0.0f;
+        for (int64_t v = 0; v < vpr; ++v) sum += sdot[r * vpr + v];
+        a.grad_zonal[e * a.rows + r] = sum;
+      }
+      for (int64_t v = lane; v < radial_row / VEC; v += kWarp) {
+        const int64_t x = v * VEC;
+        const int64_t sl = x / a.channels;
+        const int64_t c = x - sl * a.channels;
+        float gr[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) gr[i] = 0.0f;
+        for (int64_t r = 0; r < a.rows; ++r) {
+          if (__ldg(a.slot + r) != sl) continue;
+          const float z = __ldg(zr + r);
+          float g[VEC];
+          ld_l1<VEC>(gn + (r + 1) * a.channels + c, g);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) gr[i] = fmaf(g[i] * inv, z, gr[i]);
+        }
+        store_f32<VEC>(a.grad_radial + e * radial_row + x, gr);
+      }
+      __syncwarp();
+    }
+    if (cur.kind != kWhole) {
+      float* mine = a.ss.slot(p, cur.kind);
+#pragma unroll
+      for (int k = 0; k < NV; ++k)
+        if (L.ok[k]) store_cg<VEC>(mine + L.j[k] * VEC, acc[k]);
+      const int64_t first = a.mp.part_of_first_edge(n);
+      const int64_t last = a.mp.part_of_end(n);
+      if (!arrive_last(a.ss, first, last, 0)) continue;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) acc[k][i] = 0.0f;
+        if (!L.ok[k]) continue;
+        for (int64_t q = first; q <= last; ++q) {
+          float part[VEC];
+          load_cg<VEC>(a.ss.slot(q, q == last ? kHead : kTail) + L.j[k] * VEC, part);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) acc[k][i] += part[i];
+        }
+      }
+    }
+    float dot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      if (!L.ok[k]) continue;
+      float g[VEC];
+      ld_l1<VEC>(gn + L.ooff[k], g);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) dot = fmaf(g[i], acc[k][i], dot);
+    }
+    dot = xor_sum(dot, 1);
+    if (lane == 0) a.out[n] = dot;
+  }
+}
+
+using GieKernel = void (*)(GieArgs);
+
+struct GieConfig {
+  GieKernel kernel = nullptr;
+  int vec = 1, nv = 1;
+  int64_t lv = 0, tiles = 1;
+};
+
+template <int VEC>
+GieConfig gie_pick(int64_t lv, bool backward) {
+  GieConfig c;
+  c.vec = VEC;
+  c.lv = lv;
+  if (lv > 128) { c.nv = 8; c.kernel = backward ? gie_bwd_kernel<VEC, 8> : gie_fwd_kernel<VEC, 8>; }
+  else if (lv > 64) { c.nv = 4; c.kernel = backward ? gie_bwd_kernel<VEC, 4> : gie_fwd_kernel<VEC, 4>; }
+  else if (lv > 32) { c.nv = 2; c.kernel = backward ? gie_bwd_kernel<VEC, 2> : gie_fwd_kernel<VEC, 2>; }
+  else { c.nv = 1; c.kernel = backward ? gie_bwd_kernel<VEC, 1> : gie_fwd_kernel<VEC, 1>; }
+  c.tiles = (lv + kWarp * c.nv - 1) / (kWarp * c.nv);
+  return c;
+}
+
+struct GieLayout {
+  GieConfig cfg;
+  PartitionPlan plan;
+  size_t bytes = 0;
+  SplitSlots ss{};
+};
+
+GieLayout gie_layout(bool vec_ok, int64_t n_edges, int64_t n_nodes,
+                     int64_t rows, int64_t channels, bool backward, void* ws) {
+  GieLayout L;
+  const int64_t cells = rows * channels;
+  L.cfg = (vec_ok && channels % 4 == 0) ? gie_pick<4>(cells / 4, backward)
+                                        : gie_pick<1>(cells, backward);
+  const DeviceInfo& dev = current_device_info();
+  const size_t smem = backward ? sizeof(float) * kBlock * L.cfg.nv : 0;
+  const int64_t resident =
+      static_cast<int64_t>(dev.sm_count) *
+      resident_blocks(reinterpret_cast<const void*>(L.cfg.kernel), smem) *
+      kWarpsPerBlock;
+  int64_t warps = resident / L.cfg.tiles;
+  if (warps < 1) warps = 1;
+  L.plan = plan_partitions(n_edges, n_nodes, warps, 16);
+  const int64_t stride = (cells + 7) / 8 * 8;
+  Carver carve(ws);
+  float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * stride);
+  int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts) * L.cfg.tiles);
+  L.bytes = carve.need;
+  L.ss = SplitSlots{slots, tickets, stride, static_cast<int>(L.cfg.tiles)};
+  return L;
+}
+
+int gie_check(int64_t n_edges, int64_t n_nodes, int64_t rows, int64_t n_radial,
+              int64_t channels) {
+  if (n_edges < 0 || n_nodes < 0 || rows < 0 || n_radial < 0 || channels < 0)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter: invalid sizes");
+  if (rows > 0 && n_radial == 0)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "zonal scatter: radial slots are required for non-scalar rows");
+  if (n_edges > 0 && n_nodes == 0)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter: edges require nodes");
+  return BYSJ_OK;
+}
+
+}  // namespace
+}  // namespace bysj
+
+using namespace bysj;
+
+extern "C" {
+
+size_t bysj_gie_zonal_scatter_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                             int64_t n_rows, int64_t channels) {
+  if (n_edges < 0 || n_nodes <= 0 || n_rows <= 0 || channels <= 0) return 0;
+  const size_t a = gie_layout(true, n_edges, n_nodes, n_rows, channels, false, nullptr).bytes;
+  const size_t b = gie_layout(false, n_edges, n_nodes, n_rows, channels, false, nullptr).bytes;
+  return a > b ? a : b;
+}
+
+int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
+                                   const int64_t* offsets,
+                                   const int64_t* order,
+                                   const int64_t* radial_slot,
+                                   const float* inv_sqrt_deg, int64_t n_edges,
+                                   int64_t n_nodes, int64_t n_rows,
+                                   int64_t n_radial, int64_t channels,
+                                   float* out, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  clear_error();
+  int st = gie_check(n_edges, n_nodes, n_rows, n_radial, channels);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t block = (n_rows + 1) * channels;
+  if (n_nodes == 0 || block == 0) return BYSJ_OK;
+  if (out == nullptr || inv_sqrt_deg == nullptr)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter: NULL out/inv_sqrt_deg");
+  if (n_rows == 0 || channels == 0)
+    return cuda_check(cudaMemsetAsync(out, 0, sizeof(float) * n_nodes * block, s),
+                      "zonal scatter: zero output");
+  if (offsets == nullptr || radial_slot == nullptr ||
+      (n_edges > 0 && (zonal == nullptr || radial == nullptr)))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter: NULL pointer");
+  const bool vec_ok = aligned16(radial) && aligned16(out);
+  GieLayout L = gie_layout(vec_ok, n_edges, n_nodes, n_rows, channels, false, workspace);
+  if (workspace == nullptr || workspace_bytes < L.bytes)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "zonal scatter: workspace of %zu bytes needed, %zu given",
+                L.bytes, workspace_bytes);
+  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0,
+                                  sizeof(int) * L.plan.parts * L.cfg.tiles, s),
+                  "zonal scatter: ticket reset");
+  if (st) return st;
+  GieArgs a{};
+  a.zonal = zonal;
+  a.radial = radial;
+  a.order = order;
+  a.slot = radial_slot;
+  a.inv = inv_sqrt_deg;
+  a.out = out;
+  a.rows = n_rows;
+  a.n_radial = n_radial;
+  a.channels = channels;
+  a.lv = L.cfg.lv;
+  a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
+  a.ss = L.ss;
+  dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
+  L.cfg.kernel<<<grid, kBlock, 0, s>>>(a);
+  return launch_check("gie_fwd_kernel");
+}
+
+size_t bysj_gie_zonal_scatter_backward_workspace_size(int64_t n_edges,
+                                                      int64_t n_nodes,
+                                                      int64_t n_rows,
+                                                      int64_t channels) {
+  if (n_edges < 0 || n_nodes <= 0 || n_rows <= 0 || channels <= 0) return 0;
+  const size_t a = gie_layout(true, n_edges, n_nodes, n_rows, channels, true, nullptr).bytes;
+  const size_t b = gie_layout(false, n_edges, n_nodes, n_rows, channels, true, nullptr).bytes;
+  return a > b ? a : b;
+}
+
+int bysj_gie_zonal_scatter_backward(
+    const float* grad_out, const float* zonal, const float* radial,
+    const int64_t* dst, const int64_t* offsets, const int64_t* order,
+    const int64_t* radial_slot, const float* inv_sqrt_deg, int64_t n_edges,
+    int64_t n_nodes, int64_t n_rows, int64_t n_radial, int64_t channels,
+    float* grad_zonal, float* grad_radial, float* grad_inv, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  clear_error();
+  (void)dst;
+  int st = gie_check(n_edges, n_nodes, n_rows, n_radial, channels);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_nodes == 0) return BYSJ_OK;
+  if (grad_inv == nullptr || inv_sqrt_deg == nullptr)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter backward: NULL grad_inv");
+  if (n_rows == 0 || channels == 0 || n_edges == 0) {
+    st = cuda_check(cudaMemsetAsync(grad_inv, 0, sizeof(float) * n_nodes, s),
+                    "zonal scatter backward: zero grad_inv");
+    if (st) return st;
+    if (n_edges > 0 && grad_zonal && n_rows > 0)
+      st = cuda_check(cudaMemsetAsync(grad_zonal, 0, sizeof(float) * n_edges * n_rows, s),
+                      "zonal scatter backward: zero grad_zonal");
+    if (!st && n_edges > 0 && grad_radial && n_radial > 0 && channels > 0)
+      st = cuda_check(cudaMemsetAsync(grad_radial, 0,
+                                      sizeof(float) * n_edges * n_radial * channels, s),
+                      "zonal scatter backward: zero grad_radial");
+    return st;
+  }
+  if (offsets == nullptr || radial_slot == nullptr || zonal == nullptr ||
+      radial == nullptr || grad_out == nullptr || grad_zonal == nullptr ||
+      grad_radial == nullptr)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter backward: NULL pointer");
+  const bool vec_ok = aligned16(radial) && aligned16(grad_out) &&
+                      aligned16(grad_radial) && channels % 4 == 0;
+  GieLayout L = gie_layout(vec_ok, n_edges, n_nodes, n_rows, channels, true, workspace);
+  if (L.cfg.tiles != 1)
+    return fail(BYSJ_ERR_UNSUPPORTED,
+                "zonal scatter backward: rows*channels = %lld exceeds %d",
+                (long long)(n_rows * channels), kWarp * 8 * L.cfg.vec);
+  if (workspace == nullptr || workspace_bytes < L.bytes)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "zonal scatter backward: workspace of %zu bytes needed, %zu given",
+                L.bytes, workspace_bytes);
+  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts, s),
+                  "zonal scatter backward: ticket reset");
+  if (st) return st;
+  GieArgs a{};
+  a.zonal = zonal;
+  a.radial = radial;
+  a.order = order;
+  a.slot = radial_slot;
+  a.inv = inv_sqrt_deg;
+  a.grad = grad_out;
+  a.out = grad_inv;
+  a.grad_zonal = grad_zonal;
+  a.grad_radial = grad_radial;
+  a.rows = n_rows;
+  a.n_radial = n_radial;
+  a.channels = channels;
+  a.lv = L.cfg.lv;
+  a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
+  a.ss = L.ss;
+  const size_t smem = sizeof(float) * kBlock * L.cfg.nv;
+  L.cfg.kernel<<<L.plan.blocks, kBlock, smem, s>>>(a);
+  return launch_check("gie_bwd_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,566 @@
+// Gated destination-segmented softmax, forward and backward, for sm_100a.
+//
+// Mathematics (reference csrc/segment_softmax.cpp:16-32), per segment n and
+// channel c, with l_e = logit[e,c] + 2 ln env[e] for env[e] > 0:
+//   m = max(null[n,c], max_e l_e),  D = exp(null - m) + sum_e exp(l_e - m)
+//   alpha[e,c] = exp(l_e - m) / D,  null_alpha[n,c] = exp(null - m) / D
+// backward, from the stored weights:
+//   S = sum_e alpha*g + null_alpha*g0
+//   grad_logit = alpha (g - S), grad_null = null_alpha (g0 - S)
+//   grad_env[e] = (sum_c grad_logit[e,c]) * 2 / env[e]   (0 if env <= 0)
+//
+// Work split: merge-path partitions, one per warp.  A narrow channel count
+// packs G = 32 / next_pow2(C) edges side by side in a warp.  Whole segments
+// run max / sum / write back to back while the segment's rows are still in
+// L1.  For a segment cut by partition boundaries, the pieces publish their
+// partial statistics, the last piece to finish combines them in partition
+// order into a final-statistics slot, and a second, equally partitioned
+// kernel writes the per-edge outputs of those segments.
+#include "launch.cuh"
+
+namespace bysj {
+namespace {
+
+struct SmxArgs {
+  // forward inputs / backward "alpha" and "grad_alpha"
+  const float* x;        // forward: logit   | backward: alpha
+  const float* y;        // forward: unused  | backward: grad_alpha
+  const float* env;
+  const float* xn;       // forward: null_logit | backward: null_alpha
+  const float* yn;       // backward: grad_null_alpha
+  const int64_t* order;
+  float* out;            // forward: alpha  | backward: grad_logit
+  float* out_null;       // forward: null_alpha | backward: grad_null_logit
+  float* out_env;        // backward: grad_env (NULL: computed elsewhere)
+  int64_t channels;
+  int64_t cpad;          // channels rounded up to a multiple of 4
+  MergePath mp;
+  SplitSlots ss;         // partial statistics  [parts][2][2*cpad]
+  float* final_stats;    // combined statistics [parts][2*cpad]
+};
+
+template <int NC, int G>
+struct SmxShape {
+  static constexpr int LPG = kWarp / G;  // channel lanes per group
+  static constexpr int TC = LPG * NC;    // channels per tile
+};
+
+template <int NC, int G>
+__device__ __forceinline__ int64_t lane_channel(int lane, int tile, int k) {
+  using S = SmxShape<NC, G>;
+  return static_cast<int64_t>(tile) * S::TC + lane % S::LPG + k * S::LPG;
+}
+
+// ---- forward --------------------------------------------------------------
+
+template <int NC, int G>
+__device__ __forceinline__ void smx_fwd_write(const SmxArgs& a, int64_t lo,
+                                              int64_t hi, int g,
+                                              const int64_t (&ch)[NC],
+                                              const bool (&ok)[NC],
+                                              const float (&m)[NC],
+                                              const float (&inv)[NC]) {
+  const int64_t C = a.channels;
+  for (int64_t s = lo + g; s < hi; s += G) {
+    const int64_t e = a.order ? __ldg(a.order + s) : s;
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+      if (ok[k]) {
+        const float l = gated_logit(__ldg(a.x + e * C + ch[k]), a.env, e);
+        a.out[e * C + ch[k]] = shifted_exp(l, m[k]) * inv[k];
+      }
+  }
+}
+
+template <int NC, int G>
+__global__ void __launch_bounds__(kBlock) segment_softmax_fwd_kernel(SmxArgs a) {
+  using S = SmxShape<NC, G>;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int tile = blockIdx.y;
+  const int g = lane / S::LPG;
+  const int64_t C = a.channels;
+  int64_t ch[NC];
+  bool ok[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    ch[k] = lane_channel<NC, G>(lane, tile, k);
+    ok[k] = ch[k] < C;
+  }
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const bool whole = cur.kind == kWhole;
+    float m[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) m[k] = -INFINITY;
+    for (int64_t s = cur.lo + g; s < cur.hi; s += G) {
+      const int64_t e = a.order ? __ldg(a.order + s) : s;
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (ok[k]) m[k] = fmaxf(m[k], gated_logit(__ldg(a.x + e * C + ch[k]), a.env, e));
+    }
+    float nl[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      m[k] = xor_max(m[k], S::LPG);
+      nl[k] = (whole && ok[k] && a.xn) ? __ldg(a.xn + n * C + ch[k]) : -INFINITY;
+      m[k] = fmaxf(m[k], nl[k]);
+    }
+    float d[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) d[k] = 0.0f;
+    for (int64_t s = cur.lo + g; s < cur.hi; s += G) {
+      const int64_t e = a.order ? __ldg(a.order + s) : s;
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (ok[k])
+          d[k] += shifted_exp(gated_logit(__ldg(a.x + e * C + ch[k]), a.env, e), m[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < NC; ++k) d[k] = xor_sum(d[k], S::LPG);
+
+    if (whole) {
+      float inv[NC];
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        const float w0 = shifted_exp(nl[k], m[k]);
+        const float total = d[k] + w0;
+        inv[k] = total > 0.0f ? 1.0f / total : 0.0f;
+        if (g == 0 && ok[k] && a.out_null) a.out_null[n * C + ch[k]] = w0 * inv[k];
+      }
+      smx_fwd_write<NC, G>(a, cur.lo, cur.hi, g, ch, ok, m, inv);
+      continue;
+    }
+    float* mine = a.ss.slot(p, cur.kind);
+    if (g == 0) {
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (ok[k]) {
+          __stcg(mine + ch[k], m[k]);
+          __stcg(mine + a.cpad + ch[k], d[k]);
+        }
+    }
+    const int64_t first = a.mp.part_of_first_edge(n);
+    const int64_t last = a.mp.part_of_end(n);
+    if (!arrive_last(a.ss, first, last, tile)) continue;
+    if (g == 0) {
+      float* fin = a.final_stats + last * 2 * a.cpad;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        if (!ok[k]) continue;
+        const float n0 = a.xn ? __ldg(a.xn + n * C + ch[k]) : -INFINITY;
+        float mm = n0;
+        for (int64_t q = first; q <= last; ++q)
+          mm = fmaxf(mm, __ldcg(a.ss.slot(q, q == last ? kHead : kTail) + ch[k]));
+        float total = shifted_exp(n0, mm);
+        for (int64_t q = first; q <= last; ++q) {
+          const float* sq = a.ss.slot(q, q == last ? kHead : kTail);
+          total += shifted_exp(__ldcg(sq + ch[k]), mm) * __ldcg(sq + a.cpad + ch[k]);
+        }
+        const float inv = total > 0.0f ? 1.0f / total : 0.0f;
+        if (a.out_null) a.out_null[n * C + ch[k]] = shifted_exp(n0, mm) * inv;
+        __stcg(fin + ch[k], mm);
+        __stcg(fin + a.cpad + ch[k], inv);
+      }
+    }
+  }
+}
+
+// Writes alpha for the edges of split segments once their statistics are final.
+template <int NC, int G>
+__global__ void __launch_bounds__(kBlock) segment_softmax_fwd_split_kernel(SmxArgs a) {
+  using S = SmxShape<NC, G>;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int tile = blockIdx.y;
+  const int g = lane / S::LPG;
+  int64_t ch[NC];
+  bool ok[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    ch[k] = lane_channel<NC, G>(lane, tile, k);
+    ok[k] = ch[k] < a.channels;
+  }
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    if (cur.kind == kWhole) continue;
+    const int64_t last = a.mp.part_of_end(cur.node);
+    const float* fin = a.final_stats + last * 2 * a.cpad;
+    float m[NC], inv[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      m[k] = ok[k] ? __ldcg(fin + ch[k]) : 0.0f;
+      inv[k] = ok[k] ? __ldcg(fin + a.cpad + ch[k]) : 0.0f;
+    }
+    smx_fwd_write<NC, G>(a, cur.lo, cur.hi, g, ch, ok, m, inv);
+  }
+}
+
+// ---- backward -------------------------------------------------------------
+
+// grad_logit for slots [lo, hi) given the final S; also grad_env when one
+// warp covers all channels (out_env != NULL).
+template <int NC, int G>
+__device__ __forceinline__ void smx_bwd_write(const SmxArgs& a, int64_t lo,
+                                              int64_t hi, int g,
+                                              const int64_t (&ch)[NC],
+                                              const bool (&ok)[NC],
+                                              const float (&S)[NC]) {
+  using Sh = SmxShape<NC, G>;
+  const int64_t C = a.channels;
+  // Lanes of one group handle the same edge, so the trip count is uniform
+  // within a group; groups may differ by one iteration, hence the explicit
+  // group-level mask for the channel reduction.
+  const int64_t count = hi - lo;
+  const int64_t iters = (count + G - 1) / G;
+  for (int64_t t = 0; t < iters; ++t) {
+    const int64_t s = lo + g + t * G;
+    const bool live = s < hi;
+    float rowsum = 0.0f;
+    int64_t e = 0;
+    if (live) {
+      e = a.order ? __ldg(a.order + s) : s;
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (ok[k]) {
+          const int64_t idx = e * C + ch[k];
+          const float gl = __ldg(a.x + idx) * (__ldg(a.y + idx) - S[k]);
+          a.out[idx] = gl;
+          rowsum += gl;
+        }
+    }
+    if (a.out_env) {
+      rowsum = group_sum(rowsum, Sh::LPG);
+      if (live && lane_id() % Sh::LPG == 0) {
+        const float env = a.env ? __ldg(a.env + e) : 1.0f;
+        a.out_env[e] = env > 0.0f ? rowsum * 2.0f / env : 0.0f;
+      }
+    }
+  }
+}
+
+template <int NC, int G>
+__global__ void __launch_bounds__(kBlock) segment_softmax_bwd_kernel(SmxArgs a) {
+  using S = SmxShape<NC, G>;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int tile = blockIdx.y;
+  const int g = lane / S::LPG;
+  const int64_t C = a.channels;
+  int64_t ch[NC];
+  bool ok[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    ch[k] = lane_channel<NC, G>(lane, tile, k);
+    ok[k] = ch[k] < C;
+  }
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const bool whole = cur.kind == kWhole;
+    float sum[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) sum[k] = 0.0f;
+    for (int64_t s = cur.lo + g; s < cur.hi; s += G) {
+      const int64_t e = a.order ? __ldg(a.order + s) : s;
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (ok[k]) {
+          const int64_t idx = e * C + ch[k];
+          sum[k] = fmaf(__ldg(a.x + idx), __ldg(a.y + idx), sum[k]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < NC; ++k) sum[k] = xor_sum(sum[k], S::LPG);
+    if (whole) {
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (a.xn && ok[k]) {
+          const float a0 = __ldg(a.xn + n * C + ch[k]);
+          const float g0 = __ldg(a.yn + n * C + ch[k]);
+          sum[k] = fmaf(a0, g0, sum[k]);
+          if (g == 0) a.out_null[n * C + ch[k]] = a0 * (g0 - sum[k]);
+        }
+      smx_bwd_write<NC, G>(a, cur.lo, cur.hi, g, ch, ok, sum);
+      continue;
+    }
+    float* mine = a.ss.slot(p, cur.kind);
+    if (g == 0) {
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        if (ok[k]) __stcg(mine + ch[k], sum[k]);
+    }
+    const int64_t first = a.mp.part_of_first_edge(n);
+    const int64_t last = a.mp.part_of_end(n);
+    if (!arrive_last(a.ss, first, last, tile)) continue;
+    if (g == 0) {
+      float* fin = a.final_stats + last * 2 * a.cpad;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        if (!ok[k]) continue;
+        float total = 0.0f;
+        for (int64_t q = first; q <= last; ++q)
+          total += __ldcg(a.ss.slot(q, q == last ? kHead : kTail) + ch[k]);
+        if (a.xn) {
+          const float a0 = __ldg(a.xn + n * C + ch[k]);
+          const float g0 = __ldg(a.yn + n * C + ch[k]);
+          total = fmaf(a0, g0, total);
+          a.out_null[n * C + ch[k]] = a0 * (g0 - total);
+        }
+        __stcg(fin + ch[k], total);
+      }
+    }
+  }
+}
+
+template <int NC, int G>
+__global__ void __launch_bounds__(kBlock) segment_softmax_bwd_split_kernel(SmxArgs a) {
+  using S = SmxShape<NC, G>;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int tile = blockIdx.y;
+  const int g = lane / S::LPG;
+  int64_t ch[NC];
+  bool ok[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    ch[k] = lane_channel<NC, G>(lane, tile, k);
+    ok[k] = ch[k] < a.channels;
+  }
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    if (cur.kind == kWhole) continue;
+    const int64_t last = a.mp.part_of_end(cur.node);
+    const float* fin = a.final_stats + last * 2 * a.cpad;
+    float sum[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) sum[k] = ok[k] ? __ldcg(fin + ch[k]) : 0.0f;
+    smx_bwd_write<NC, G>(a, cur.lo, cur.hi, g, ch, ok, sum);
+  }
+}
+
+// grad_env for channel counts wider than one warp tile.
+__global__ void __launch_bounds__(kBlock)
+    segment_softmax_env_kernel(const float* __restrict__ grad_logit,
+                               const float* __restrict__ env,
+                               float* __restrict__ grad_env, int64_t n_edges,
+                               int64_t channels) {
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
+  for (int64_t e = global_warp(); e < n_edges; e += warps) {
+    float sum = 0.0f;
+    for (int64_t c = lane_id(); c < channels; c += kWarp)
+      sum += __ldg(grad_logit + e * channels + c);
+    sum = xor_sum(sum, 1);
+    if (lane_id() == 0) {
+      const float g = env ? __ldg(env + e) : 1.0f;
+      grad_env[e] = g > 0.0f ? sum * 2.0f / g : 0.0f;
+    }
+  }
+}
+
+// ---- host -----------------------------------------------------------------
+
+using SmxKernel = void (*)(SmxArgs);
+struct SmxConfig {
+  SmxKernel main = nullptr, split = nullptr;
+  int64_t tc = 0, tiles = 1;
+};
+
+template <int NC, int G>
+SmxConfig smx_make(bool backward) {
+  SmxConfig c;
+  c.main = backward ? segment_softmax_bwd_kernel<NC, G> : segment_softmax_fwd_kernel<NC, G>;
+  c.split = backward ? segment_softmax_bwd_split_kernel<NC, G>
+                     : segment_softmax_fwd_split_kernel<NC, G>;
+  c.tc = SmxShape<NC, G>::TC;
+  return c;
+}
+
+SmxConfig smx_config(int64_t channels, bool backward) {
+  SmxConfig c;
+  if (channels > 128) c = smx_make<8, 1>(backward);
+  else if (channels > 64) c = smx_make<4, 1>(backward);
+  else if (channels > 32) c = smx_make<2, 1>(backward);
+  else {
+    switch (next_pow2(channels)) {
+      case 32: c = smx_make<1, 1>(backward); break;
+      case 16: c = smx_make<1, 2>(backward); break;
+      case 8: c = smx_make<1, 4>(backward); break;
+      case 4: c = smx_make<1, 8>(backward); break;
+      case 2: c = smx_make<1, 16>(backward); break;
+      default: c = smx_make<1, 32>(backward); break;
+    }
+  }
+  c.tiles = (channels + c.tc - 1) / c.tc;
+  return c;
+}
+
+struct SmxLayout {
+  SmxConfig cfg;
+  PartitionPlan plan;
+  int64_t cpad = 0;
+  size_t bytes = 0;
+  SplitSlots ss{};
+  float* final_stats = nullptr;
+};
+
+SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
+                     bool backward, void* ws) {
+  SmxLayout L;
+  L.cfg = smx_config(channels, backward);
+  const DeviceInfo& dev = current_device_info();
+  const int64_t resident =
+      static_cast<int64_t>(dev.sm_count) *
+      resident_blocks(reinterpret_cast<const void*>(L.cfg.main)) *
+      kWarpsPerBlock;
+  int64_t warps = resident / L.cfg.tiles;
+  if (warps < 1) warps = 1;
+  L.plan = plan_partitions(n_edges, n_nodes, warps, 32);
+  L.cpad = (channels + 3) / 4 * 4;
+  Carver carve(ws);
+  float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * 2 * L.cpad);
+  int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts) * L.cfg.tiles);
+  L.final_stats = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * L.cpad);
+  L.bytes = carve.need;
+  L.ss = SplitSlots{slots, tickets, 2 * L.cpad, static_cast<int>(L.cfg.tiles)};
+  return L;
+}
+
+int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
+            const int64_t* offsets, cudaStream_t s, const char* name) {
+  int st = cuda_check(
+      cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts * L.cfg.tiles, s),
+      "segment softmax: ticket reset");
+  if (st) return st;
+  a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
+  a.ss = L.ss;
+  a.final_stats = L.final_stats;
+  a.cpad = L.cpad;
+  dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
+  L.cfg.main<<<grid, kBlock, 0, s>>>(a);
+  st = launch_check(name);
+  if (st) return st;
+  L.cfg.split<<<grid, kBlock, 0, s>>>(a);
+  return launch_check(name);
+}
+
+int smx_check(int64_t n_edges, int64_t n_nodes, int64_t channels,
+              const int64_t* offsets) {
+  if (n_edges < 0 || n_nodes < 0 || channels <= 0)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment softmax: invalid sizes");
+  if (n_nodes > 0 && offsets == nullptr)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment softmax: offsets is NULL");
+  return BYSJ_OK;
+}
+
+}  // namespace
+}  // namespace bysj
+
+using namespace bysj;
+
+extern "C" {
+
+size_t bysj_segment_softmax_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                           int64_t channels) {
+  if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
+  return smx_layout(n_edges, n_nodes, channels, false, nullptr).bytes;
+}
+
+int bysj_segment_softmax_forward(const float* logit, const float* env,
+                                 const int64_t* offsets, int64_t n_edges,
+                                 int64_t n_nodes, int64_t channels,
+                                 const float* null_logit,
+                                 const int64_t* order, float* alpha,
+                                 float* null_alpha, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  clear_error();
+  int st = smx_check(n_edges, n_nodes, channels, offsets);
+  if (st) return st;
+  if ((null_logit == nullptr) != (null_alpha == nullptr))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "segment softmax: null_logit and null_alpha go together");
+  if (n_nodes == 0) return BYSJ_OK;
+  if (n_edges > 0 && (logit == nullptr || alpha == nullptr))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment softmax: NULL logit/alpha");
+  SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace);
+  if (workspace == nullptr || workspace_bytes < L.bytes)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "segment softmax: workspace of %zu bytes needed, %zu given",
+                L.bytes, workspace_bytes);
+  SmxArgs a{};
+  a.x = logit;
+  a.env = env;
+  a.xn = null_logit;
+  a.order = order;
+  a.out = alpha;
+  a.out_null = null_alpha;
+  a.channels = channels;
+  return smx_run(a, L, n_edges, n_nodes, offsets,
+                 static_cast<cudaStream_t>(stream), "segment_softmax_fwd");
+}
+
+size_t bysj_segment_softmax_backward_workspace_size(int64_t n_edges,
+                                                    int64_t n_nodes,
+                                                    int64_t channels) {
+  if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
+  return smx_layout(n_edges, n_nodes, channels, true, nullptr).bytes;
+}
+
+int bysj_segment_softmax_backward(const float* alpha, const float* grad_alpha,
+                                  const float* env, const int64_t* offsets,
+                                  int64_t n_edges, int64_t n_nodes,
+                                  int64_t channels, const float* null_alpha,
+                                  const float* grad_null_alpha,
+                                  const int64_t* order, float* grad_logit,
+                                  float* grad_null_logit, float* grad_env,
+                                  void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  clear_error();
+  int st = smx_check(n_edges, n_nodes, channels, offsets);
+  if (st) return st;
+  const int nulls = (null_alpha != nullptr) + (grad_null_alpha != nullptr) +
+                    (grad_null_logit != nullptr);
+  if (nulls != 0 && nulls != 3)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "segment softmax backward: null_alpha, grad_null_alpha and "
+                "grad_null_logit go together");
+  if (n_nodes == 0) return BYSJ_OK;
+  if (n_edges > 0 && (alpha == nullptr || grad_alpha == nullptr ||
+                      grad_logit == nullptr))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "segment softmax backward: NULL alpha/grad_alpha/grad_logit");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SmxLayout L = smx_layout(n_edges, n_nodes, channels, true, workspace);
+  if (workspace == nullptr || workspace_bytes < L.bytes)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "segment softmax backward: workspace of %zu bytes needed, %zu "
+                "given",
+                L.bytes, workspace_bytes);
+  const bool env_in_warp = L.cfg.tiles == 1;
+  SmxArgs a{};
+  a.x = alpha;
+  a.y = grad_alpha;
+  a.env = env;
+  a.xn = null_alpha;
+  a.yn = grad_null_alpha;
+  a.order = order;
+  a.out = grad_logit;
+  a.out_null = grad_null_logit;
+  a.out_env = env_in_warp ? grad_env : nullptr;
+  a.channels = channels;
+  st = smx_run(a, L, n_edges, n_nodes, offsets, s, "segment_softmax_bwd");
+  if (st || env_in_warp || grad_env == nullptr || n_edges == 0) return st;
+  const DeviceInfo& dev = current_device_info();
+  int64_t blocks = (n_edges + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  if (blocks > dev.sm_count * 8) blocks = dev.sm_count * 8;
+  segment_softmax_env_kernel<<<static_cast<unsigned>(blocks), kBlock, 0, s>>>(
+      grad_logit, env, grad_env, n_edges, channels);
+  return launch_check("segment_softmax_env_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,110 @@
+"""GIE zonal scatter on B200.
+
+Python face of the reference's ``python/kernels/gie.py`` (validation and
+autograd contract, lines 11-93).  ``dst`` may be in any order: the extension
+derives the destination CSR view on the device (boundary kernel for sorted
+input, histogram + stable sort otherwise) and then runs the atomic-free
+segmented kernel, which normalises after the destination sum.
+"""
+from __future__ import annotations
+
+import torch
+
+from .native import _extension, require_dcu
+
+
+def _validate(zonal, radial, dst, radial_slot, inv_sqrt_deg):
+    named = (
+        ("zonal", zonal),
+        ("radial", radial),
+        ("dst", dst),
+        ("radial_slot", radial_slot),
+        ("inv_sqrt_deg", inv_sqrt_deg),
+    )
+    for name, tensor in named:
+        if not isinstance(tensor, torch.Tensor):
+            raise TypeError(f"GIE {name} must be a tensor")
+    if any(t.dtype != torch.float32 for t in (zonal, radial, inv_sqrt_deg)):
+        raise TypeError("GIE value tensors must be float32")
+    if dst.dtype != torch.int64 or radial_slot.dtype != torch.int64:
+        raise TypeError("GIE dst and radial_slot must be int64")
+    if zonal.ndim != 2:
+        raise ValueError("GIE zonal must have shape (n_edges, n_rows)")
+    if radial.ndim != 3 or radial.shape[0] != zonal.shape[0]:
+        raise ValueError("GIE radial must have shape (n_edges, n_radial, channels)")
+    n_edges, n_rows = zonal.shape
+    if tuple(dst.shape) != (n_edges,):
+        raise ValueError("GIE dst must have shape (n_edges,)")
+    if tuple(radial_slot.shape) != (n_rows,):
+        raise ValueError("GIE radial_slot must have shape (n_rows,)")
+    if inv_sqrt_deg.ndim not in (1, 3) or (
+        inv_sqrt_deg.ndim == 3 and tuple(inv_sqrt_deg.shape[1:]) != (1, 1)
+    ):
+        raise ValueError("GIE inv_sqrt_deg must have shape (n_nodes,) or (n_nodes, 1, 1)")
+    if n_rows and radial.shape[1] == 0:
+        raise ValueError("GIE radial must contain slots when zonal rows are present")
+    if n_edges and inv_sqrt_deg.shape[0] == 0:
+        raise ValueError("GIE degree normalization must contain destination nodes")
+    tensors = (zonal, radial, dst, radial_slot, inv_sqrt_deg)
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("GIE inputs must be contiguous")
+    if len({t.device for t in tensors}) != 1:
+        raise ValueError("all GIE inputs must share a device")
+
+
+class _GIEZonalScatterFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, zonal, radial, dst, radial_slot, inv_sqrt_deg):
+        output = _extension("gie_zonal_scatter_forward").gie_zonal_scatter_forward(
+            zonal, radial, dst, radial_slot, inv_sqrt_deg
+        )
+        ctx.save_for_backward(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+        return output
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        zonal, radial, dst, radial_slot, inv_sqrt_deg = ctx.saved_tensors
+        grad_zonal, grad_radial, grad_inv = _extension(
+            "gie_zonal_scatter_backward"
+        ).gie_zonal_scatter_backward(
+            grad_output.contiguous(), zonal, radial, dst, radial_slot, inv_sqrt_deg
+        )
+        needs = ctx.needs_input_grad
+        return (
+            grad_zonal if needs[0] else None,
+            grad_radial if needs[1] else None,
+            None,
+            None,
+            grad_inv if needs[4] else None,
+        )
+
+
+def zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg):
+    """DPA4 geometric-initial-embedding zonal scatter on a B200.
+
+    ``out[n, r+1, c] = inv[n] * sum_{dst[e]=n} zonal[e, r] * radial[e,
+    radial_slot[r], c]``; row zero is reserved (zero).  Value tensors are
+    contiguous float32, indices contiguous int64 and in range.  Gradients are
+    defined for zonal, radial and the inverse degree, not for the indices.
+    """
+    _validate(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+    require_dcu(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+    return _GIEZonalScatterFunction.apply(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+
+
+def gie_zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg):
+    """Alias naming the DPA4 stage this primitive belongs to."""
+    return zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+
+
+def gie_available() -> bool:
+    """Whether this process can run both GIE entry points."""
+    try:
+        require_dcu()
+        extension = _extension("gie_zonal_scatter_forward")
+        return hasattr(extension, "gie_zonal_scatter_backward")
+    except (ImportError, OSError, RuntimeError):
+        return False
+
+
+__all__ = ["gie_available", "gie_zonal_scatter", "zonal_scatter"]

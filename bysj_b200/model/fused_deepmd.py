@@ -1,0 +1,417 @@
+"""Bind the B200 segmented operators into a loaded DeepMD DPA4 model.
+
+Same seam as the reference's ``python/model/fused_deepmd.py`` (lines
+58-470): two DeepMD dispatch points are rebound, and every call keeps a
+per-call fallback to DeepMD's own implementation.
+
+``segment_envelope_gated_softmax`` (module attribute in DeepMD's
+``sezm_nn.attention`` / ``sezm_nn.so2`` / ``sezm_nn``)
+    replaced by ``ops.segment_softmax`` with the null logit
+    ``log(softplus(z_bias) + eps)`` and the envelope folded into the logit.
+``SO2Convolution.forward_envelope`` (per block instance)
+    replaced by one ``ops.segment_sum`` with ``edge_scale = env * src_gate``
+    and ``node_scale = inv_sqrt_deg``.
+
+A call falls back -- counted in ``FusedStats`` and warned about once -- when a
+precondition fails (training mode, a source-weighted softmax, non-contiguous
+or non-fp32 or non-CUDA tensors, shape mismatch) or when the fused operator
+raises.  The destination CSR view (offsets, stable order) is built on the
+device with the operator bundle's ``segment_offsets`` and kept in a small LRU
+keyed by the ``dst`` storage.
+"""
+from __future__ import annotations
+
+import warnings
+from dataclasses import dataclass, field
+from types import MethodType
+from typing import Any, Iterable
+
+import torch
+import torch.nn.functional as F
+
+_CSR_CAPACITY = 4
+# Host tests drive the seams with CPU tensors and a stand-in operator bundle;
+# on a real install this guard keeps CPU tensors away from the CUDA kernels.
+_ACCEPT_ANY_DEVICE = False
+_SOFTMAX_NAME = "segment_envelope_gated_softmax"
+_BLOCK_PREFIX = "block:"
+
+
+@dataclass
+class FusedStats:
+    """Hit / fallback counters of the installed seams."""
+
+    softmax_hits: int = 0
+    softmax_fallbacks: int = 0
+    envelope_hits: int = 0
+    envelope_fallbacks: int = 0
+    bound_softmax: bool = False
+    bound_envelope: bool = False
+    blocks: int = 0
+    last_error: str | None = None
+
+    def as_dict(self) -> dict[str, Any]:
+        return {
+            "softmax_hits": self.softmax_hits,
+            "softmax_fallbacks": self.softmax_fallbacks,
+            "envelope_hits": self.envelope_hits,
+            "envelope_fallbacks": self.envelope_fallbacks,
+            "bound_softmax": self.bound_softmax,
+            "bound_envelope": self.bound_envelope,
+            "blocks": self.blocks,
+            "last_error": self.last_error,
+        }
+
+
+def _usable_tensor(value: Any, *, dtype: torch.dtype = torch.float32) -> bool:
+    if not isinstance(value, torch.Tensor):
+        return False
+    on_device = value.is_cuda or _ACCEPT_ANY_DEVICE
+    return on_device and value.dtype == dtype and value.is_contiguous()
+
+
+def _load_ops() -> Any:
+    """The fused operator bundle, or ``None`` when it cannot run here."""
+    try:
+        from .. import kernels
+    except ImportError:
+        return None
+    if not kernels.segment_available():
+        return None
+    return kernels
+
+
+class _CsrView:
+    """Destination CSR view ``(offsets, order)`` cached by the dst storage."""
+
+    def __init__(self, builder=None, capacity: int = _CSR_CAPACITY) -> None:
+        self._builder = builder
+        self._capacity = capacity
+        self._cache: dict[tuple[int, int, int], tuple[torch.Tensor, torch.Tensor]] = {}
+        self._lru: list[tuple[int, int, int]] = []
+
+    def _offsets(self, dst: torch.Tensor, n_nodes: int) -> torch.Tensor:
+        builder = self._builder
+        if builder is None:
+            from ..kernels.segment import segment_offsets as builder
+        return builder(dst, n_nodes)
+
+    def get(self, dst: torch.Tensor, n_nodes: int) -> tuple[torch.Tensor, torch.Tensor]:
+        key = (int(dst.data_ptr()), int(dst.numel()), int(n_nodes))
+        hit = self._cache.get(key)
+        if hit is not None:
+            return hit
+        view = (self._offsets(dst, n_nodes), torch.argsort(dst, stable=True))
+        self._cache[key] = view
+        self._lru.append(key)
+        while len(self._lru) > self._capacity:
+            self._cache.pop(self._lru.pop(0), None)
+        return view
+
+
+@dataclass
+class _Session:
+    ops: Any
+    stats: FusedStats
+    reference_softmax: Any
+    csr: _CsrView = field(default_factory=_CsrView)
+    warned: bool = False
+
+    # -- softmax seam ---------------------------------------------------------
+    def softmax(self, logits, edge_env, dst, n_nodes, z_bias_raw, eps, src_weight=None):
+        stats = self.stats
+
+        def stock(weight=None):
+            stats.softmax_fallbacks += 1
+            return self.reference_softmax(logits, edge_env, dst, n_nodes, z_bias_raw, eps, weight)
+
+        if src_weight is not None:
+            return stock(src_weight)
+        shaped = (
+            _usable_tensor(logits)
+            and logits.ndim == 3
+            and logits.shape[0] > 0
+            and _usable_tensor(edge_env)
+            and isinstance(dst, torch.Tensor)
+            and dst.dtype == torch.int64
+            and dst.ndim == 1
+            and n_nodes > 0
+        )
+        if not shaped:
+            return stock()
+        n_edges, n_focus, n_head = logits.shape
+        channels = n_focus * n_head
+        bias = z_bias_raw.to(dtype=torch.float32).reshape(-1)
+        if bias.numel() != channels or edge_env.numel() != n_edges:
+            return stock()
+        try:
+            offsets, order = self.csr.get(dst, n_nodes)
+            null = torch.log(F.softplus(bias) + float(eps))
+            null = null.reshape(1, channels).expand(n_nodes, channels).contiguous()
+            result = self.ops.segment_softmax(
+                logits.reshape(n_edges, channels),
+                edge_env.reshape(n_edges),
+                offsets,
+                null,
+                order=order,
+            )
+            # (alpha, null_alpha) when a null logit is given; accept a bare
+            # tensor too so the seam does not depend on that arity.
+            alpha = result[0] if isinstance(result, tuple) else result
+        except Exception as error:  # noqa: BLE001 - fall back, never break inference
+            self._record(error)
+            return stock()
+        stats.softmax_hits += 1
+        return alpha.reshape(n_edges, n_focus, n_head)
+
+    # -- envelope seam --------------------------------------------------------
+    def envelope(self, original, block, x, edge_cache, radial_feat):
+        stats = self.stats
+
+        def stock():
+            stats.envelope_fallbacks += 1
+            return original(block, x, edge_cache, radial_feat)
+
+        dst = getattr(edge_cache, "dst", None)
+        edge_env = getattr(edge_cache, "edge_env", None)
+        inverse = getattr(edge_cache, "inv_sqrt_deg", None)
+        gate = getattr(edge_cache, "edge_src_gate", None)
+        ready = (
+            not bool(getattr(block, "training", False))
+            and _usable_tensor(x)
+            and _usable_tensor(edge_env)
+            and _usable_tensor(inverse)
+            and isinstance(dst, torch.Tensor)
+            and dst.dtype == torch.int64
+            and dst.ndim == 1
+            and dst.numel() > 0
+            and (gate is None or _usable_tensor(gate))
+        )
+        if not ready:
+            return stock()
+        n_node, n_edges = x.shape[0], dst.shape[0]
+        if (
+            x.ndim != 3
+            or inverse.numel() != n_node
+            or edge_env.numel() != n_edges
+            or not _usable_tensor(dst, dtype=torch.int64)
+        ):
+            return stock()
+        try:
+            message, _ = block.edge_message(x, edge_cache, radial_feat)
+            if not _usable_tensor(message) or message.shape[0] != n_edges:
+                raise ValueError("edge message is not a contiguous fp32 (E, ...) tensor")
+            weight = edge_env.reshape(-1)
+            if gate is not None:
+                weight = weight * gate.reshape(-1).to(dtype=torch.float32)
+            offsets, order = self.csr.get(dst, n_node)
+            out = self.ops.segment_sum(
+                message.reshape(n_edges, -1),
+                dst,
+                offsets,
+                weight.contiguous(),
+                inverse.reshape(-1).contiguous(),
+                order=order,
+            )
+        except Exception as error:  # noqa: BLE001 - fall back, never break inference
+            self._record(error)
+            return stock()
+        stats.envelope_hits += 1
+        return out.reshape(x.shape)
+
+    def _record(self, error: Exception) -> None:
+        self.stats.last_error = f"{type(error).__name__}: {error}"
+        if not self.warned:
+            self.warned = True
+            warnings.warn(
+                "fused DeepMD dispatch fell back to the reference path: " + self.stats.last_error,
+                RuntimeWarning,
+                stacklevel=3,
+            )
+
+
+_SESSION: _Session | None = None
+# "<module>.segment_envelope_gated_softmax" -> (module, original callable)
+# "block:<id>"                               -> (block, original bound method)
+_SAVED: dict[str, Any] = {}
+
+
+def _softmax_namespaces() -> list[Any]:
+    """DeepMD modules whose ``segment_envelope_gated_softmax`` is rebound."""
+    import deepmd.pt.model.descriptor.sezm_nn.attention as attention_module
+    import deepmd.pt.model.descriptor.sezm_nn.so2 as so2_module
+
+    found = [attention_module, so2_module]
+    try:
+        import deepmd.pt.model.descriptor.sezm_nn as package
+    except ImportError:  # pragma: no cover - the package exists with its modules
+        return found
+    found.append(package)
+    return found
+
+
+def _blocks(model: Any) -> list[Any]:
+    """SO(2) convolution blocks that carry the aggregation seams."""
+    return [
+        module
+        for module in model.modules()
+        if callable(getattr(module, "edge_message", None))
+        and callable(getattr(module, "forward_envelope", None))
+        and hasattr(module, "_segment_softmax_fn")
+    ]
+
+
+def _module_root(model: Any) -> tuple[Any | None, str]:
+    """The ``nn.Module`` tree behind a ``DeepPot`` / ``DeepEval`` wrapper.
+
+    ``DeepPot`` is not a module: the legacy ``pt`` backend keeps its tree at
+    ``deep_eval.dp``, ``pt_expt`` at ``deep_eval._dpmodel``; a module may also
+    be passed directly.
+    """
+    if callable(getattr(model, "modules", None)):
+        return model, "model"
+    deep_eval = getattr(model, "deep_eval", None)
+    if deep_eval is None:
+        return None, ""
+    for attribute in ("_dpmodel", "dp", "model"):
+        candidate = getattr(deep_eval, attribute, None)
+        if candidate is not None and callable(getattr(candidate, "modules", None)):
+            return candidate, f"deep_eval.{attribute}"
+    if callable(getattr(deep_eval, "modules", None)):
+        return deep_eval, "deep_eval"
+    return None, ""
+
+
+def describe_module(module: Any, *, max_depth: int = 2, max_rows: int = 40) -> list[str]:
+    """Printable lines: the module tree (to ``max_depth``) and the patch targets."""
+    root, path = _module_root(module)
+    if root is None:
+        return [
+            f"module: {type(module).__name__} (no nn.Module tree found -- expected a "
+            "module, or a DeepPot/DeepEval wrapper with deep_eval.dp / deep_eval._dpmodel)",
+            "patch targets: 0 (nothing can be bound)",
+        ]
+    named = list(root.named_modules()) if hasattr(root, "named_modules") else []
+    via = "" if path == "model" else f" -> {path}"
+    lines = [f"module: {type(module).__name__}{via} ({type(root).__name__}, {len(named)} submodules)"]
+    for name, child in named[:max_rows]:
+        depth = name.count(".") + 1 if name else 0
+        if depth <= max_depth:
+            lines.append(f"  {'  ' * depth}{name or '<root>'}  {type(child).__name__}")
+    if len(named) > max_rows:
+        lines.append(f"  ... {len(named) - max_rows} more submodules")
+    targets = _blocks(root)
+    lines.append(f"patch targets: {len(targets)} SO(2) block(s)")
+    for index, block in enumerate(targets):
+        lines.append(
+            f"  [{index}] {type(block).__name__}  "
+            f"n_atten_head={getattr(block, 'n_atten_head', '?')}  "
+            "seams: forward_envelope -> segment_sum, attention softmax -> segment_softmax"
+        )
+    return lines
+
+
+def _say(verbose: bool, text: str) -> None:
+    if verbose:
+        print(f"[deepmd_patch] {text}", flush=True)
+
+
+def deepmd_patch(module: Any, *, ops: Any = None, softmax: bool = True, envelope: bool = True,
+                 blocks: Iterable[Any] | None = None, namespaces: Iterable[Any] | None = None,
+                 verbose: bool = True) -> FusedStats:
+    """Bind the fused operators on ``module`` (a ``DeepPot`` or an ``nn.Module``).
+
+    ``ops`` is an operator bundle with ``segment_softmax`` and ``segment_sum``
+    (and optionally ``segment_offsets`` for the CSR view); it defaults to
+    :mod:`bysj_b200.kernels`, and the install is a logged no-op when the
+    extension cannot run on this host.  ``namespaces`` overrides the DeepMD
+    modules that carry the softmax name.  Installing twice keeps one patch.
+    """
+    global _SESSION
+    stats = FusedStats()
+    if verbose:
+        for line in describe_module(module):
+            _say(True, line)
+    uninstall(module)
+    root, path = _module_root(module)
+    if blocks is not None:
+        targets = list(blocks)
+    else:
+        targets = [] if root is None else list(_blocks(root))
+    if root is not None and path != "model":
+        _say(verbose, f"resolved module tree: {path} ({type(root).__name__})")
+    stats.blocks = len(targets)
+    if ops is None:
+        ops = _load_ops()
+    _say(verbose, f"operators: {'bysj_b200.kernels' if ops is not None else 'unavailable'}; "
+                  f"softmax={softmax} envelope={envelope}")
+    if ops is None:
+        _say(verbose, "no fused extension on this host -> nothing replaced")
+        return stats
+
+    spaces: list[Any] = []
+    reference = None
+    if softmax:
+        spaces = list(namespaces) if namespaces is not None else _softmax_namespaces()
+        if not spaces:
+            raise ValueError("deepmd_patch requires one module namespace to patch")
+        reference = getattr(spaces[0], _SOFTMAX_NAME)
+    builder = getattr(ops, "segment_offsets", None)
+    _SESSION = _Session(ops=ops, stats=stats, reference_softmax=reference,
+                        csr=_CsrView(builder))
+
+    if softmax:
+        def bound_softmax(logits, edge_env, dst, n_nodes, z_bias_raw, eps, src_weight=None):
+            session = _SESSION
+            if session is None:  # uninstalled between calls
+                return reference(logits, edge_env, dst, n_nodes, z_bias_raw, eps, src_weight)
+            return session.softmax(logits, edge_env, dst, n_nodes, z_bias_raw, eps, src_weight)
+
+        for space in spaces:
+            if not hasattr(space, _SOFTMAX_NAME):
+                continue
+            _SAVED[f"{space.__name__}.{_SOFTMAX_NAME}"] = (space, getattr(space, _SOFTMAX_NAME))
+            setattr(space, _SOFTMAX_NAME, bound_softmax)
+            _say(verbose, f"replace {space.__name__}.{_SOFTMAX_NAME} -> "
+                          "bysj_b200.model.fused_deepmd.bound_softmax")
+        stats.bound_softmax = True
+
+    if envelope:
+        for block in targets:
+            original = block.forward_envelope
+            _SAVED[f"{_BLOCK_PREFIX}{id(block)}"] = (block, original)
+
+            def patched(self, x, edge_cache, radial_feat, _original=original):
+                session = _SESSION
+                if session is None:
+                    return _original(self, x, edge_cache, radial_feat)
+                return session.envelope(_original, self, x, edge_cache, radial_feat)
+
+            block.forward_envelope = MethodType(patched, block)
+        stats.bound_envelope = bool(targets)
+        _say(verbose, f"replace SO2Convolution.forward_envelope on {len(targets)} block(s) -> "
+                      "bysj_b200.model.fused_deepmd.patched")
+    _say(verbose, f"installed: softmax={stats.bound_softmax} envelope={stats.bound_envelope} "
+                  f"blocks={stats.blocks}")
+    return stats
+
+
+def uninstall(module: Any = None) -> None:
+    """Restore every rebound name; safe to call when nothing is installed."""
+    global _SESSION
+    for key, (owner, original) in list(_SAVED.items()):
+        if key.startswith(_BLOCK_PREFIX):
+            # Drop the instance attribute so the class method shows through.
+            owner.__dict__.pop("forward_envelope", None)
+        else:
+            setattr(owner, key.rsplit(".", 1)[-1], original)
+    _SAVED.clear()
+    _SESSION = None
+
+
+def status(stats: FusedStats | None) -> dict[str, Any]:
+    """Counters of a patch (empty when it never ran)."""
+    return {} if stats is None else stats.as_dict()
+
+
+__all__ = ["FusedStats", "deepmd_patch", "describe_module", "status", "uninstall"]

@@ -1,0 +1,288 @@
+/*
+ * bysj_b200.h -- C ABI of the B200 (sm_100a) segmented-operator library.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream (passed as `void*`, i.e. a `cudaStream_t`; NULL is the legacy default
+ * stream), launches its kernels asynchronously on that stream and returns a
+ * `bysj_status`.  Nothing here allocates device memory: outputs and scratch
+ * ("workspace") are owned by the caller.  Each operator that needs scratch has
+ * a `*_workspace_size` query; pass a buffer of at least that many bytes,
+ * 256-byte aligned.  Inputs are borrowed and never written.
+ *
+ * Layout contract shared by the segmented operators: the edge list is grouped
+ * by destination node ("segment").  `offsets[n_nodes + 1]` is the exclusive
+ * prefix sum of the per-node edge counts; the edges of node n are the slots
+ * offsets[n] .. offsets[n+1]-1.  When `order` is non-NULL, slot s refers to
+ * edge order[s]; otherwise slot s is edge s.  Index values are trusted to be in
+ * range (the Python layer validates shapes and dtypes before calling).
+ *
+ * All reductions are deterministic: for fixed inputs, sizes and device, two
+ * calls produce bit-identical outputs (no floating-point atomics; partial
+ * results of a segment split across warps are combined in a fixed order).
+ *
+ * Reference interfaces replaced (lipengfei1409/bysj):
+ *   csrc/ops.h:8-45        (declarations of the HIP operators)
+ *   csrc/bindings.cpp:6-29 (the nine Python-visible entry points)
+ *   python/kernels/segment.py:46-71 (segment_offsets / group_by_source)
+ */
+#ifndef BYSJ_B200_H
+#define BYSJ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BYSJ_API __attribute__((visibility("default")))
+#else
+#define BYSJ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum bysj_status {
+  BYSJ_OK = 0,
+  BYSJ_ERR_INVALID_ARGUMENT = 1, /* bad size, NULL pointer, misalignment    */
+  BYSJ_ERR_WORKSPACE = 2,        /* workspace missing or too small           */
+  BYSJ_ERR_UNSUPPORTED = 3,      /* shape outside what the kernels support   */
+  BYSJ_ERR_CUDA = 4,             /* a CUDA runtime call failed               */
+  BYSJ_ERR_LAUNCH = 5,           /* a kernel launch failed                   */
+  BYSJ_ERR_TOO_LARGE = 6         /* size beyond a fixed capacity             */
+} bysj_status;
+
+typedef enum bysj_dtype {
+  BYSJ_F32 = 0,
+  BYSJ_BF16 = 1
+} bysj_dtype;
+
+/* Flags written to the device word `flags` by the segment_offsets kernels. */
+#define BYSJ_FLAG_OUT_OF_RANGE 1u /* some dst < 0 or dst >= n_nodes       */
+#define BYSJ_FLAG_UNSORTED 2u     /* dst is not non-decreasing           */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+BYSJ_API int bysj_version(void);
+/* Static description of a status code. */
+BYSJ_API const char* bysj_status_string(int status);
+/* Detail of the last failure on the calling host thread ("" if none). */
+BYSJ_API const char* bysj_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * segment_offsets
+ * Replaces python/kernels/segment.py:46-57 (bincount + cumsum over dst).
+ * ------------------------------------------------------------------------ */
+
+/* Fast path for a destination-sorted edge list: one pass, no atomics.
+ * Writes offsets[0..n_nodes] and ORs BYSJ_FLAG_* into *flags (a device
+ * uint32 that the caller zeroes).  If the flags come back non-zero the
+ * offsets are meaningless: use bysj_segment_offsets_histogram instead
+ * (unsorted input) or report the range error. */
+BYSJ_API int bysj_segment_offsets_sorted(const int64_t* dst, int64_t n_edges,
+                                int64_t n_nodes, int64_t* offsets,
+                                uint32_t* flags, void* stream);
+
+/* General path (any order): histogram with integer atomics, then an
+ * exclusive scan.  Integer results are exact; out-of-range dst values are
+ * skipped and flagged. */
+BYSJ_API size_t bysj_segment_offsets_workspace_size(int64_t n_nodes);
+BYSJ_API int bysj_segment_offsets_histogram(const int64_t* dst, int64_t n_edges,
+                                   int64_t n_nodes, int64_t* offsets,
+                                   uint32_t* flags, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * segment_sum
+ * Replaces csrc/segment_sum.cpp:214-317 (segment_sum_forward_hip /
+ * segment_sum_backward_hip).
+ *   out[n, c] = node_scale[n] * sum_{slot in seg(n)} edge_scale[e] * src[e, c]
+ * src is [n_edges, channels] in `src_dtype`; out is float32 [n_nodes, channels].
+ * edge_scale [n_edges], node_scale [n_nodes] and order [n_edges] may be NULL.
+ * ------------------------------------------------------------------------ */
+BYSJ_API size_t bysj_segment_sum_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                       int64_t channels, int src_dtype);
+BYSJ_API int bysj_segment_sum_forward(const void* src, int src_dtype, int64_t n_edges,
+                             int64_t channels, const int64_t* offsets,
+                             int64_t n_nodes, const float* edge_scale,
+                             const float* node_scale, const int64_t* order,
+                             float* out, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* grad_src[e, c] = grad_out[dst[e], c] * edge_scale[e] * node_scale[dst[e]]
+ * grad_node_scale[n] = sum_c grad_out[n, c] * sum_{e in n} edge_scale[e] src[e, c]
+ * grad_node_scale may be NULL (not wanted); it requires node_scale != NULL. */
+BYSJ_API size_t bysj_segment_sum_backward_workspace_size(int64_t n_edges,
+                                                int64_t n_nodes,
+                                                int64_t channels,
+                                                int src_dtype);
+BYSJ_API int bysj_segment_sum_backward(const float* grad_out, const void* src,
+                              int src_dtype, const int64_t* dst,
+                              const int64_t* offsets, int64_t n_edges,
+                              int64_t n_nodes, int64_t channels,
+                              const float* edge_scale, const float* node_scale,
+                              const int64_t* order, float* grad_src,
+                              float* grad_node_scale, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * segment_softmax
+ * Replaces csrc/segment_softmax.cpp:235-343.  Per segment and channel:
+ *   l_e = logit[e,c] + 2 ln env[e] for env[e] > 0 (other edges carry no mass)
+ *   m = max(null_logit[n,c], max_e l_e);  D = exp(null - m) + sum_e exp(l_e - m)
+ *   alpha[e,c] = exp(l_e - m) / D;  null_alpha[n,c] = exp(null - m) / D
+ * A segment whose maximum is -inf gets all-zero weights.
+ * null_logit / null_alpha may both be NULL.
+ * ------------------------------------------------------------------------ */
+BYSJ_API size_t bysj_segment_softmax_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                           int64_t channels);
+BYSJ_API int bysj_segment_softmax_forward(const float* logit, const float* env,
+                                 const int64_t* offsets, int64_t n_edges,
+                                 int64_t n_nodes, int64_t channels,
+                                 const float* null_logit,
+                                 const int64_t* order, float* alpha,
+                                 float* null_alpha, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* S = sum_e alpha*grad_alpha + null_alpha*grad_null_alpha
+ * grad_logit = alpha (grad_alpha - S);  grad_null_logit = null_alpha (grad_null_alpha - S)
+ * grad_env[e] = 2 / env[e] * sum_c grad_logit[e, c]  (0 where env[e] <= 0)
+ * null_alpha, grad_null_alpha and grad_null_logit are all NULL or all set. */
+BYSJ_API size_t bysj_segment_softmax_backward_workspace_size(int64_t n_edges,
+                                                    int64_t n_nodes,
+                                                    int64_t channels);
+BYSJ_API int bysj_segment_softmax_backward(const float* alpha, const float* grad_alpha,
+                                  const float* env, const int64_t* offsets,
+                                  int64_t n_edges, int64_t n_nodes,
+                                  int64_t channels, const float* null_alpha,
+                                  const float* grad_null_alpha,
+                                  const int64_t* order, float* grad_logit,
+                                  float* grad_null_logit, float* grad_env,
+                                  void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+/* ------------------------------------------------------------------------
+ * segment_attention: fused gated segment softmax + weighted segment sum.
+ * No single counterpart in the reference; it is the composition
+ * python/reference/segment.py:63-118 (softmax) followed by :39-60 (sum).
+ *   alpha[e,h] as in segment_softmax over logit [n_edges, heads]
+ *   out[n, h, s, k] = sum_e alpha[e,h] * value[e, s, h*(channels/heads) + k]
+ * value is [n_edges, components, channels] in `value_dtype`; out is float32
+ * [n_nodes, heads, components, channels/heads].  env [n_edges] and
+ * null_logit [n_nodes, heads] may be NULL.  heads must divide channels.
+ * ------------------------------------------------------------------------ */
+BYSJ_API size_t bysj_segment_attention_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                             int64_t heads,
+                                             int64_t components,
+                                             int64_t channels,
+                                             int value_dtype);
+BYSJ_API int bysj_segment_attention_forward(const float* logit, const void* value,
+                                   int value_dtype, const float* env,
+                                   const float* null_logit,
+                                   const int64_t* offsets,
+                                   const int64_t* order, int64_t n_edges,
+                                   int64_t n_nodes, int64_t heads,
+                                   int64_t components, int64_t channels,
+                                   float* out, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * force_assembly
+ * Replaces csrc/force_assembly.cpp:106-146.
+ *   force[k]  = sum_{dst(e)=k} g_e - sum_{src(e)=k} g_e        (fp64 accumulate)
+ *   virial[k] = - sum_{src(e)=k} g_e (x) v_e  (row-major 3x3)
+ * grad_edge, edge_vec: float32 [n_edges, 3]; dst_offsets / src_offsets
+ * [n_nodes + 1]; src_order [n_edges] groups the edges by source atom.
+ * force [n_nodes, 3], virial [n_nodes, 9] (virial may be NULL).
+ * ------------------------------------------------------------------------ */
+BYSJ_API int bysj_force_assembly(const float* grad_edge, const float* edge_vec,
+                        const int64_t* dst_offsets, const int64_t* src_offsets,
+                        const int64_t* src_order, int64_t n_edges,
+                        int64_t n_nodes, float* force, float* virial,
+                        void* stream);
+
+/* Source-side half of force_assembly for a destination-range partition of a
+ * larger graph: partial[k, 0:3] = -sum_{src(e)=k} g_e and
+ * partial[k, 3:12] = -sum_{src(e)=k} g_e (x) v_e for every k in [0, n_nodes),
+ * where the edges given here are only this partition's; the destination side
+ * force[k] += sum_{dst(e)=k} g_e is added by bysj_force_assembly_dst_add for
+ * the local atoms [node_begin, node_begin + n_local) after the partials of all
+ * partitions have been summed (reduce-scattered).  No reference counterpart:
+ * this is the multi-GPU decomposition of csrc/force_assembly.cpp:64-96. */
+BYSJ_API int bysj_force_assembly_src_partial(const float* grad_edge,
+                                    const float* edge_vec,
+                                    const int64_t* src_offsets,
+                                    const int64_t* src_order, int64_t n_edges,
+                                    int64_t n_nodes, float* partial,
+                                    void* stream);
+BYSJ_API int bysj_force_assembly_dst_add(const float* grad_edge,
+                                const int64_t* dst_offsets, int64_t n_local,
+                                const float* summed_partial, float* force,
+                                float* virial, void* stream);
+
+/* ------------------------------------------------------------------------
+ * rmsnorm (last axis)
+ * Replaces csrc/rmsnorm.cpp:99-157.
+ *   inv_rms[r] = rsqrt(mean_c x[r,c]^2 + eps);  y[r,c] = x[r,c] inv_rms[r] w[c]
+ * x / y: [rows, width] in `dtype` (y has the dtype of x); inv_rms float32.
+ * scale: NULL (no scale), float32 [width] (scale_rows == 1) or the
+ * per-degree form float32 [scale_rows, width] with scale_rows = L + 1, where
+ * row r of x is component i = r mod (L+1)^2 and uses weight row floor(sqrt(i)).
+ * ------------------------------------------------------------------------ */
+BYSJ_API int bysj_rmsnorm_forward(const void* x, int dtype, int64_t rows, int64_t width,
+                         const float* scale, int64_t scale_rows, float eps,
+                         void* y, float* inv_rms, void* stream);
+
+/* gx = inv*gw - x*inv^3*mean(x*gw), gw = grad_out*w;
+ * grad_scale[l, c] = sum over rows r using weight row l of grad_out*x*inv.
+ * grad_scale may be NULL.  Deterministic two-stage reduction (no atomics). */
+BYSJ_API size_t bysj_rmsnorm_backward_workspace_size(int64_t rows, int64_t width,
+                                            int64_t scale_rows);
+BYSJ_API int bysj_rmsnorm_backward(const float* grad_out, const float* x,
+                          const float* scale, int64_t scale_rows,
+                          const float* inv_rms, int64_t rows, int64_t width,
+                          float* grad_x, float* grad_scale, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * GIE zonal scatter (CSR form)
+ * Replaces csrc/gie.cpp:148-228.  With the edges grouped by destination
+ * (offsets / order as above):
+ *   out[n, 0, :] = 0
+ *   out[n, r+1, c] = inv_sqrt_deg[n] * sum_{e in n} zonal[e, r] *
+ *                    radial[e, radial_slot[r], c]      (normalise after sum)
+ * zonal [n_edges, n_rows], radial [n_edges, n_radial, channels],
+ * radial_slot int64 [n_rows], inv_sqrt_deg [n_nodes], out [n_nodes, n_rows+1,
+ * channels].
+ * ------------------------------------------------------------------------ */
+BYSJ_API size_t bysj_gie_zonal_scatter_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                             int64_t n_rows, int64_t channels);
+BYSJ_API int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
+                                   const int64_t* offsets,
+                                   const int64_t* order,
+                                   const int64_t* radial_slot,
+                                   const float* inv_sqrt_deg, int64_t n_edges,
+                                   int64_t n_nodes, int64_t n_rows,
+                                   int64_t n_radial, int64_t channels,
+                                   float* out, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* grad_zonal[e, r]     = inv[dst e] * sum_c g[dst e, r+1, c] radial[e, slot r, c]
+ * grad_radial[e, s, c] = inv[dst e] * sum_{r: slot r = s} g[dst e, r+1, c] zonal[e, r]
+ * grad_inv[n]          = sum_{r,c} g[n, r+1, c] * sum_{e in n} zonal[e,r] radial[e, slot r, c]
+ * dst [n_edges] is the destination of each edge (natural order). */
+BYSJ_API size_t bysj_gie_zonal_scatter_backward_workspace_size(int64_t n_edges,
+                                                      int64_t n_nodes,
+                                                      int64_t n_rows,
+                                                      int64_t channels);
+BYSJ_API int bysj_gie_zonal_scatter_backward(
+    const float* grad_out, const float* zonal, const float* radial,
+    const int64_t* dst, const int64_t* offsets, const int64_t* order,
+    const int64_t* radial_slot, const float* inv_sqrt_deg, int64_t n_edges,
+    int64_t n_nodes, int64_t n_rows, int64_t n_radial, int64_t channels,
+    float* grad_zonal, float* grad_radial, float* grad_inv, void* workspace,
+    size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* BYSJ_B200_H */

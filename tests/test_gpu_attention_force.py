@@ -1,0 +1,144 @@
+"""GPU parity of the fused segment attention and of force_assembly (B200)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import truth
+from reference import force_assembly_reference, segment_attention_reference
+
+pytestmark = pytest.mark.gpu
+
+from bysj_b200 import kernels as K  # noqa: E402
+from bysj_b200 import workloads as W  # noqa: E402
+from test_gpu_segment import budget, graph, skewed_sizes  # noqa: E402
+
+
+# ---- segment_attention -------------------------------------------------------------
+
+def test_attention_golden(cuda):
+    g = golden("segment_attention")
+    out = K.segment_attention(torch.from_numpy(g["logit"]).cuda(),
+                              torch.from_numpy(g["value"]).cuda(),
+                              torch.from_numpy(g["offsets"]).cuda())
+    np.testing.assert_allclose(out.cpu().numpy(), g["out"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("heads,comps,channels", [(8, 16, 64), (8, 4, 16), (4, 3, 12),
+                                                  (2, 5, 6), (1, 2, 3), (16, 2, 32)])
+def test_attention_matches_oracle_with_env_and_null(cuda, heads, comps, channels):
+    sizes = [3, 0, 5, 1, 12, 2, 7]
+    dst, off = graph(sizes)
+    e = dst.numel()
+    gen = torch.Generator().manual_seed(heads * 100 + channels)
+    logit = torch.randn(e, heads, generator=gen) * 2
+    value = torch.randn(e, comps, channels, generator=gen)
+    env = torch.where(torch.rand(e, generator=gen) < 0.2, torch.tensor(0.0),
+                      torch.rand(e, generator=gen) + 0.05)
+    null = torch.randn(len(sizes), heads, generator=gen)
+    got = K.segment_attention(logit.cuda(), value.cuda(), off, env.cuda(), null.cuda())
+    want = segment_attention_reference(logit, value, dst.cpu(), off.cpu(), env, null)
+    torch.testing.assert_close(got.cpu(), want, rtol=1e-5, atol=1e-6)
+    plain = K.segment_attention(logit.cuda(), value.cuda(), off)
+    want_plain = segment_attention_reference(logit, value, dst.cpu(), off.cpu())
+    torch.testing.assert_close(plain.cpu(), want_plain, rtol=1e-5, atol=1e-6)
+
+
+def test_attention_c1_fp32_bf16_and_determinism(cuda):
+    g = W.c1_box(device="cuda")
+    off = K.segment_offsets(g.dst, g.n_atoms)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    logit = torch.randn(g.n_edges, 8, device="cuda", generator=gen) * 2
+    value = torch.randn(g.n_edges, 16, 64, device="cuda", generator=gen)
+    out = K.segment_attention(logit, value, off)
+    want = truth.segment_attention(logit.cpu().numpy(), value.cpu().numpy(),
+                                   g.dst.cpu().numpy(), g.n_atoms)
+    np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5, atol=budget(want))
+    fp32_oracle = segment_attention_reference(logit.cpu(), value.cpu(), g.dst.cpu(), off.cpu())
+    torch.testing.assert_close(out.cpu(), fp32_oracle, rtol=1e-5, atol=1e-6)
+    assert torch.equal(out, K.segment_attention(logit, value, off))
+    vb = value.to(torch.bfloat16)
+    out16 = K.segment_attention(logit, vb, off)
+    want16 = truth.segment_attention(logit.cpu().numpy(), vb.float().cpu().numpy(),
+                                     g.dst.cpu().numpy(), g.n_atoms)
+    np.testing.assert_allclose(out16.cpu().numpy(), want16, rtol=1e-2, atol=1e-3)
+
+
+def test_attention_skewed_split_segments_and_order(cuda):
+    sizes = skewed_sizes(3, nodes=150, giant=4000)
+    dst, off = graph(sizes)
+    e = dst.numel()
+    gen = torch.Generator().manual_seed(4)
+    logit = torch.randn(e, 8, generator=gen) * 2
+    value = torch.randn(e, 4, 32, generator=gen)
+    env = torch.rand(e, generator=gen) + 0.05
+    null = torch.randn(sizes.numel(), 8, generator=gen)
+    got = K.segment_attention(logit.cuda(), value.cuda(), off, env.cuda(), null.cuda())
+    want = truth.segment_attention(logit.numpy(), value.numpy(), dst.cpu().numpy(),
+                                   sizes.numel(), env.numpy(), null.numpy())
+    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-5, atol=budget(want))
+    assert torch.equal(got, K.segment_attention(logit.cuda(), value.cuda(), off, env.cuda(),
+                                                null.cuda()))
+    perm = torch.randperm(e, generator=gen)
+    lp, vp, ep = torch.empty_like(logit), torch.empty_like(value), torch.empty_like(env)
+    lp[perm], vp[perm], ep[perm] = logit, value, env
+    got_p = K.segment_attention(lp.cuda(), vp.cuda(), off, ep.cuda(), null.cuda(),
+                                order=perm.cuda())
+    np.testing.assert_allclose(got_p.cpu().numpy(), want, rtol=1e-5, atol=budget(want))
+
+
+def test_attention_all_masked_segment_is_zero(cuda):
+    dst, off = graph([2, 3])
+    logit = torch.randn(5, 2, device="cuda")
+    value = torch.randn(5, 2, 4, device="cuda")
+    env = torch.tensor([0.0, -1.0, 0.5, 0.2, 0.9], device="cuda")
+    out = K.segment_attention(logit, value, off, env)
+    assert out[0].count_nonzero() == 0
+
+
+# ---- force_assembly --------------------------------------------------------------------
+
+def test_force_golden(cuda):
+    g = golden("force_assembly")
+    to = lambda k: torch.from_numpy(g[k]).cuda()  # noqa: E731
+    force, virial = K.force_assembly(to("grad_edge"), to("edge_vec"), to("src"), to("dst"),
+                                     to("dst_offsets"), to("src_offsets"), to("src_order"))
+    np.testing.assert_allclose(force.cpu().numpy(), g["force"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(virial.cpu().numpy(), g["virial"], rtol=1e-5, atol=1e-6)
+
+
+def test_force_c1_matches_oracle_and_conserves_momentum(cuda):
+    g = W.c1_box(device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    grad = torch.randn(g.n_edges, 3, device="cuda", generator=gen) * 0.1
+    off = K.segment_offsets(g.dst, g.n_atoms)
+    force, virial = K.force_assembly(grad, g.unit, g.src, g.dst, off)
+    order, soff = K.group_by_source(g.src, g.n_atoms)
+    wf, wv = force_assembly_reference(grad.cpu(), g.unit.cpu(), g.src.cpu(), g.dst.cpu(),
+                                      off.cpu(), soff.cpu())
+    torch.testing.assert_close(force.cpu(), wf, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(virial.cpu(), wv, rtol=1e-5, atol=1e-6)
+    tf, tv = truth.force_assembly(grad.cpu().numpy(), g.unit.cpu().numpy(), g.src.cpu().numpy(),
+                                  g.dst.cpu().numpy(), g.n_atoms)
+    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(force.double().sum(0).cpu(), torch.zeros(3, dtype=torch.float64),
+                               atol=1e-4, rtol=0)
+    f2, v2 = K.force_assembly(grad, g.unit, g.src, g.dst, off, soff, order)
+    assert torch.equal(force, f2) and torch.equal(virial, v2)
+
+
+def test_force_skewed_and_empty_atom(cuda):
+    sizes = skewed_sizes(6, nodes=120, giant=3000)
+    dst, off = graph(sizes)
+    e = dst.numel()
+    gen = torch.Generator().manual_seed(6)
+    src = torch.randint(0, sizes.numel(), (e,), generator=gen)
+    src[src == 7] = 8  # atom 7 has no source edges
+    grad, vec = torch.randn(e, 3, generator=gen), torch.randn(e, 3, generator=gen)
+    force, virial = K.force_assembly(grad.cuda(), vec.cuda(), src.cuda(), dst, off)
+    tf, tv = truth.force_assembly(grad.numpy(), vec.numpy(), src.numpy(), dst.cpu().numpy(),
+                                  sizes.numel())
+    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=1e-6, atol=1e-5)
+    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=1e-6, atol=1e-5)
