@@ -170,7 +170,7 @@ class _Session:
 
         def stock():
             stats.envelope_fallbacks += 1
-            return original(block, x, edge_cache, radial_feat)
+            return original(x, edge_cache, radial_feat)  # bound to `block` already
 
         dst = getattr(edge_cache, "dst", None)
         edge_env = getattr(edge_cache, "edge_env", None)
@@ -382,9 +382,10 @@ def deepmd_patch(module: Any, *, ops: Any = None, softmax: bool = True, envelope
             _SAVED[f"{_BLOCK_PREFIX}{id(block)}"] = (block, original)
 
             def patched(self, x, edge_cache, radial_feat, _original=original):
+                # `_original` is the block's bound method captured at install.
                 session = _SESSION
                 if session is None:
-                    return _original(self, x, edge_cache, radial_feat)
+                    return _original(x, edge_cache, radial_feat)
                 return session.envelope(_original, self, x, edge_cache, radial_feat)
 
             block.forward_envelope = MethodType(patched, block)
