@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 segmented-operator path (one JSON line on rank 0).
 
-Headline workload ("C3"): fused attention aggregation on
+Headline workload ("C3", the fused-attention configuration): aggregation on
 a 24576-atom water-like periodic box (density 0.1 / A^3, rcut 6 A, ~2.22 M
 dst-sorted edges); logits fp32 [E, 8] drawn N(0, 2) (variance 2), values
 fp32 [E, 16, 64] drawn N(0, 1).  One step = ``segment_offsets`` (device
@@ -436,12 +436,14 @@ def run_ours(args, dist):
     clocks.start()
     dist.barrier()
     torch.cuda.synchronize()
+    torch.cuda.profiler.start()  # ncu --profile-from-start off captures from here
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for i in range(args.steps):
         step(pairs[i])
     end.record()
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     dist.barrier()
     clock_info = clocks.stop()
     step_s = start.elapsed_time(end) / 1e3 / args.steps
@@ -507,7 +509,9 @@ def run_ours(args, dist):
     ops = cpu = None
     if dist.world == 1 and not args.no_ops and not args.profile_small:
         value32 = value if value.dtype == torch.float32 else value.float()
+        torch.cuda.profiler.start()
         ops = measure_ops(g, logit, value32, device, peak)
+        torch.cuda.profiler.stop()
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu and not args.profile_small:
         cpu = cpu_sample_rate(g, logit, value)
 
