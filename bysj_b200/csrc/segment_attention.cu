@@ -16,6 +16,8 @@
 // each piece keeps its local maximum m_q, denominator d_q and unnormalised
 // sum; the last piece to finish rescales them by exp(m_q - m) in partition
 // order, so results are deterministic.
+#include <mutex>
+
 #include "launch.cuh"
 
 namespace bysj {
@@ -423,3 +425,147 @@ int bysj_segment_attention_forward(const float* logit, const void* value,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot hand this library a workspace: a plugin hook that only
+// receives input/output pointers and a stream (a molecular-dynamics engine's
+// pair-style callback, a serving runtime that forbids allocation after its
+// warm-up so its memory footprint stays fixed), or code on a hot path where
+// cudaMalloc would synchronise the whole device.  For them the split-segment
+// scratch of the fused attention lives in one file-scope device array of
+// BYSJ_ATTENTION_NOALLOC_SCRATCH_BYTES (16 MiB), which every GPU that loads
+// this library keeps until the process exits.
+// ---------------------------------------------------------------------------
+
+static __device__ __align__(256) unsigned char
+    bysj_attention_noalloc_scratch[BYSJ_ATTENTION_NOALLOC_SCRATCH_BYTES];
+
+namespace bysj {
+namespace {
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[64] = {};
+
+// Device address of the scratch array for the current device.  In host code
+// the array's name is only a host-side handle, so the address is looked up
+// once per device (with that device current) and cached.
+int noalloc_scratch_address(void** address) {
+  int device = 0;
+  int st = cuda_check(cudaGetDevice(&device), "segment attention (no-alloc): current device");
+  if (st) return st;
+  if (device < 0 || device >= 64)
+    return fail(BYSJ_ERR_UNSUPPORTED, "segment attention (no-alloc): device %d", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[device] == nullptr) {
+    void* ptr = nullptr;
+    st = cuda_check(cudaGetSymbolAddress(&ptr, bysj_attention_noalloc_scratch),
+                    "segment attention (no-alloc): scratch address");
+    if (st) return st;
+    g_noalloc_address[device] = ptr;
+  }
+  *address = g_noalloc_address[device];
+  return BYSJ_OK;
+}
+
+// Same tiling as attn_layout, with the partition count capped so that the
+// split slots and tickets fit in the fixed scratch array.
+int noalloc_layout(bool vec_ok, int dtype, int64_t n_edges, int64_t n_nodes,
+                   int64_t heads, int64_t comps, int64_t channels, void* base,
+                   AttnLayout* L, SplitSlots* ss) {
+  const int64_t row = comps * channels;
+  L->cfg = attn_config(vec_ok, dtype, channels, channels / heads, row);
+  L->stats_off = (row + 7) / 8 * 8;
+  L->stride = L->stats_off + 2 * kMaxHeads;
+  const size_t slack = 2 * 256;  // alignment of the two carved regions
+  const size_t per_part = 2 * sizeof(float) * static_cast<size_t>(L->stride) +
+                          sizeof(int) * static_cast<size_t>(L->cfg.tiles);
+  const size_t capacity = BYSJ_ATTENTION_NOALLOC_SCRATCH_BYTES;
+  if (per_part + slack > capacity)
+    return fail(BYSJ_ERR_TOO_LARGE,
+                "segment attention (no-alloc): a value row of %lld elements needs %zu "
+                "bytes of scratch per partition; the fixed scratch holds %zu bytes "
+                "(use bysj_segment_attention_forward with a workspace)",
+                (long long)row, per_part, capacity);
+  const int64_t cap = static_cast<int64_t>((capacity - slack) / per_part);
+  const DeviceInfo& dev = current_device_info();
+  int64_t warps = static_cast<int64_t>(dev.sm_count) *
+                  resident_blocks(reinterpret_cast<const void*>(L->cfg.kernel)) *
+                  kWarpsPerBlock / L->cfg.tiles;
+  if (warps > cap) warps = cap;
+  if (warps < 1) warps = 1;
+  L->plan = plan_partitions(n_edges, n_nodes, warps, 16);
+  Carver carve(base);
+  float* slots = carve.take<float>(static_cast<size_t>(L->plan.parts) * 2 * L->stride);
+  int* tickets = carve.take<int>(static_cast<size_t>(L->plan.parts) * L->cfg.tiles);
+  L->bytes = carve.need;
+  if (L->bytes > capacity)
+    return fail(BYSJ_ERR_TOO_LARGE, "segment attention (no-alloc): scratch plan overflow");
+  *ss = SplitSlots{slots, tickets, L->stride, static_cast<int>(L->cfg.tiles)};
+  return BYSJ_OK;
+}
+
+}  // namespace
+}  // namespace bysj
+
+extern "C" int bysj_segment_attention_forward_noalloc(
+    const float* logit, const void* value, int value_dtype, const float* env,
+    const float* null_logit, const int64_t* offsets, const int64_t* order, int64_t n_edges,
+    int64_t n_nodes, int64_t heads, int64_t components, int64_t channels, float* out,
+    void* stream) {
+  clear_error();
+  if (n_edges < 0 || n_nodes < 0 || heads <= 0 || components <= 0 || channels <= 0)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment attention (no-alloc): invalid sizes");
+  if (heads > kMaxHeads)
+    return fail(BYSJ_ERR_UNSUPPORTED,
+                "segment attention (no-alloc): at most %d heads are supported", kMaxHeads);
+  if (channels % heads != 0)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "segment attention (no-alloc): heads must divide channels");
+  if (value_dtype != BYSJ_F32 && value_dtype != BYSJ_BF16)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment attention (no-alloc): unknown dtype");
+  const bool vec_ok = aligned16(value) && aligned16(out);
+  AttnLayout L;
+  SplitSlots ss{};
+  // Size check first, so an oversized row is rejected whatever the counts.
+  int st = noalloc_layout(vec_ok, value_dtype, n_edges, n_nodes, heads, components, channels,
+                          nullptr, &L, &ss);
+  if (st) return st;
+  if (n_nodes == 0) return BYSJ_OK;
+  if (offsets == nullptr || out == nullptr ||
+      (n_edges > 0 && (logit == nullptr || value == nullptr)))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment attention (no-alloc): NULL pointer");
+  void* base = nullptr;
+  st = noalloc_scratch_address(&base);
+  if (st) return st;
+  st = noalloc_layout(vec_ok, value_dtype, n_edges, n_nodes, heads, components, channels, base,
+                      &L, &ss);
+  if (st) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents; only the tickets must
+  // start at zero (partial slots are always written before they are read).
+  st = cuda_check(cudaMemsetAsync(ss.tickets, 0, sizeof(int) * L.plan.parts * L.cfg.tiles, s),
+                  "segment attention (no-alloc): ticket reset");
+  if (st) return st;
+  AttnArgs a;
+  a.logit = logit;
+  a.value = value;
+  a.env = env;
+  a.null_logit = null_logit;
+  a.order = order;
+  a.out = out;
+  a.heads = static_cast<int>(heads);
+  a.hp = static_cast<int>(next_pow2(heads));
+  a.comps = components;
+  a.channels = channels;
+  a.dh = channels / heads;
+  a.row = components * channels;
+  a.lv = L.cfg.lv;
+  a.stats_off = L.stats_off;
+  a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
+  a.ss = ss;
+  dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
+  L.cfg.kernel<<<grid, kBlock, 0, s>>>(a);
+  return launch_check("segment_attention_kernel (no-alloc)");
+}

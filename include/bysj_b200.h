@@ -184,6 +184,31 @@ BYSJ_API int bysj_segment_attention_forward(const float* logit, const void* valu
                                    float* out, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of bysj_segment_attention_forward.  It has no
+ * counterpart in the reference.  It is for callers that cannot allocate device
+ * memory or hand over a workspace: a plugin hook that only sees its inputs,
+ * outputs and a stream, a serving runtime whose memory footprint is frozen
+ * after warm-up, or a hot path where cudaMalloc would synchronise the device.
+ * Same arguments and results (within fp32 rounding: segments may be split at
+ * different points) as the workspace form, minus the workspace.
+ *
+ * Scratch: one file-scope device array of BYSJ_ATTENTION_NOALLOC_SCRATCH_BYTES
+ * per GPU, held from library load until process exit.  The partition count is
+ * capped so the split-segment slots fit; a value row (components * channels)
+ * too wide for even one partition is rejected with BYSJ_ERR_TOO_LARGE.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All calls
+ * on a device share the array and it keeps the last call's contents (each
+ * call zeroes, on its own stream, the counters that must start at zero):
+ * calls that overlap on the GPU, e.g. on two streams at once, race and must
+ * be serialised by the caller. */
+#define BYSJ_ATTENTION_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+BYSJ_API int bysj_segment_attention_forward_noalloc(
+    const float* logit, const void* value, int value_dtype, const float* env,
+    const float* null_logit, const int64_t* offsets, const int64_t* order,
+    int64_t n_edges, int64_t n_nodes, int64_t heads, int64_t components,
+    int64_t channels, float* out, void* stream);
+
 /* ------------------------------------------------------------------------
  * force_assembly
  * Replaces csrc/force_assembly.cpp:106-146.
