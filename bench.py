@@ -60,6 +60,15 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile-small", action="store_true",
                    help="tiny frame for ncu captures (not a bench number)")
+    p.add_argument("--only", choices=sorted(OPS),
+                   help="time one operator on its own (per-op line only, no headline)")
+    p.add_argument("--atoms", type=int, default=24576,
+                   help="atoms of the synthetic box used by --only")
+    p.add_argument("--mode", choices=("frames", "partition"), default="frames",
+                   help="frames: one C3 frame per rank (default); partition: one large box "
+                        "split by destination-atom ranges, force partials reduce-scattered")
+    p.add_argument("--partition-atoms", type=int, default=500_000,
+                   help="atoms of the box used by --mode partition")
     return p.parse_args()
 
 
@@ -80,7 +89,12 @@ class Dist:
 
             import torch.distributed as dist
 
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            kwargs = {}
+            if backend == "nccl":
+                device = torch.device("cuda", self.local)
+                torch.cuda.set_device(device)
+                kwargs["device_id"] = device
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kwargs)
             self.pg = dist
 
     def barrier(self):
@@ -287,75 +301,158 @@ def op_line(name, alg_bytes, seconds, peak, edges=None, extra=None):
     return name, line
 
 
-def measure_ops(g, logit, value32, device, peak, iters=10):
+def _op_offsets(ctx):
     from bysj_b200 import _C
-    from bysj_b200 import kernels as K
-    from bysj_b200 import workloads as W
 
-    flush = Flusher(device)
-    e, n = g.n_edges, g.n_atoms
-    out = {}
-    flags = torch.zeros(1, dtype=torch.int32, device=device)
-    offsets = _C.segment_offsets_device(g.dst, n, flags)
-
-    t = time_launches(lambda: _C.segment_offsets_device(g.dst, n, flags), iters, flush)
-    k, v = op_line("segment_offsets", 8 * e + 8 * (n + 1), t, peak, e,
+    g, n, e = ctx["g"], ctx["g"].n_atoms, ctx["g"].n_edges
+    flags = ctx["flags"]
+    t = time_launches(lambda: _C.segment_offsets_device(g.dst, n, flags), ctx["iters"],
+                      ctx["flush"])
+    return op_line("segment_offsets", 8 * e + 8 * (n + 1), t, ctx["peak"], e,
                    {"note": "2 launches (check + boundary), L2 flushed"})
-    out[k] = v
 
-    vb = value32.to(torch.bfloat16)
-    t = time_launches(lambda: _C.segment_attention_forward(logit, vb, offsets), iters)
-    k, v = op_line("segment_attention_bf16", attention_bytes(e, n, 2), t, peak, e)
-    out[k] = v
-    del vb
 
-    env = torch.ones(e, device=device)
-    t = time_launches(lambda: _C.segment_softmax_forward(logit, env, offsets), iters, flush)
-    k, v = op_line("segment_softmax_h8", e * (32 + 4 + 32) + 8 * (n + 1), t, peak, e,
+def _op_attention_bf16(ctx):
+    from bysj_b200 import _C
+
+    e, n = ctx["g"].n_edges, ctx["g"].n_atoms
+    vb = ctx["value32"]().to(torch.bfloat16)
+    t = time_launches(lambda: _C.segment_attention_forward(ctx["logit"](), vb, ctx["offsets"]),
+                      ctx["iters"])
+    return op_line("segment_attention_bf16", attention_bytes(e, n, 2), t, ctx["peak"], e)
+
+
+def _op_softmax(ctx):
+    from bysj_b200 import _C
+
+    e, n = ctx["g"].n_edges, ctx["g"].n_atoms
+    env = torch.ones(e, device=ctx["device"])
+    logit = ctx["logit"]()
+    t = time_launches(lambda: _C.segment_softmax_forward(logit, env, ctx["offsets"]),
+                      ctx["iters"], ctx["flush"])
+    return op_line("segment_softmax_h8", e * (32 + 4 + 32) + 8 * (n + 1), t, ctx["peak"], e,
                    {"note": "standalone alpha output, L2 flushed"})
-    out[k] = v
 
-    src = value32.reshape(e, -1)
+
+def _op_segment_sum(ctx):
+    from bysj_b200 import _C
+
+    e, n = ctx["g"].n_edges, ctx["g"].n_atoms
+    device = ctx["device"]
+    src = ctx["value32"]().reshape(e, -1)
     ws = torch.rand(e, device=device) + 0.5
     ns = torch.rand(n, device=device) + 0.5
-    t = time_launches(lambda: _C.segment_sum_forward(src, offsets, ws, ns), iters)
-    k, v = op_line("segment_sum_c1024", e * (4096 + 4) + n * (4096 + 4) + 8 * (n + 1), t, peak, e)
-    out[k] = v
+    t = time_launches(lambda: _C.segment_sum_forward(src, ctx["offsets"], ws, ns), ctx["iters"])
+    return op_line("segment_sum_c1024", e * (4096 + 4) + n * (4096 + 4) + 8 * (n + 1), t,
+                   ctx["peak"], e)
 
-    gen = torch.Generator(device=device).manual_seed(99)
-    grad = torch.randn(e, 3, device=device, generator=gen) * 0.1
-    order, soff = K.group_by_source(g.src, n)
-    fa = lambda: _C.force_assembly(grad, g.unit, offsets, soff, order)  # noqa: E731
+
+def _op_force(ctx, shuffled=False):
+    from bysj_b200 import _C
+    from bysj_b200 import kernels as K
+
+    g, e, n = ctx["g"], ctx["g"].n_edges, ctx["g"].n_atoms
+    gen = torch.Generator(device=ctx["device"]).manual_seed(99)
+    grad = torch.randn(e, 3, device=ctx["device"], generator=gen) * 0.1
+    src, unit, offsets, name = g.src, g.unit, ctx["offsets"], "force_assembly"
+    if shuffled:
+        # the same system with atoms numbered in random order: neighbours' rows
+        # are scattered over the whole array (worst case for the source gather)
+        label = torch.randperm(n, device=ctx["device"], generator=gen)
+        dst, src = label[g.dst], label[src]
+        perm = torch.argsort(dst * n + src)
+        dst, src, unit = dst[perm].contiguous(), src[perm].contiguous(), unit[perm].contiguous()
+        offsets = _C.segment_offsets_device(dst, n, ctx["flags"])
+        name = "force_assembly_random_order"
+    order, soff = K.group_by_source(src, n)
+    fa = lambda: _C.force_assembly(grad, unit, offsets, soff, order)  # noqa: E731
     fa_bytes = e * (12 + 12 + 8) + n * (16 + 12 + 36)
-    t_cold = time_launches(fa, iters, flush)
-    t_warm = time_launches(fa, iters)
-    k, v = op_line("force_assembly", fa_bytes, t_cold, peak, e,
-                   {"note": "L2 flushed before each launch (cold)",
-                    "warm_us": t_warm * 1e6,
-                    "warm_frac": round(fa_bytes / t_warm / 1e9 / peak, 4)})
-    out[k] = v
+    t_cold = time_launches(fa, ctx["iters"], ctx["flush"])
+    t_warm = time_launches(fa, ctx["iters"])
+    return op_line(name, fa_bytes, t_cold, ctx["peak"], e,
+                   {"note": "L2 flushed before each launch (cold)", "warm_us": t_warm * 1e6,
+                    "warm_frac": round(fa_bytes / t_warm / 1e9 / ctx["peak"], 4)})
 
+
+def _op_zonal(ctx):
+    from bysj_b200 import _C
+    from bysj_b200 import workloads as W
+
+    g, e, n = ctx["g"], ctx["g"].n_edges, ctx["g"].n_atoms
+    device = ctx["device"]
+    gen = torch.Generator(device=device).manual_seed(98)
     zonal = W.real_sph_zonal(g.unit)
     radial = torch.randn(e, 4, 64, device=device, generator=gen)
     slot = W.degree_slots().to(device)
     inv = torch.rsqrt(torch.bincount(g.dst, minlength=n).float() + 1.0)
-    t = time_launches(lambda: _C.gie_zonal_scatter_forward(zonal, radial, g.dst, slot, inv), iters)
-    k, v = op_line("zonal_scatter", e * (60 + 8 + 256 * 3) + n * (4096 + 4), t, peak, e,
+    t = time_launches(lambda: _C.gie_zonal_scatter_forward(zonal, radial, g.dst, slot, inv),
+                      ctx["iters"])
+    return op_line("zonal_scatter", e * (60 + 8 + 256 * 3) + n * (4096 + 4), t, ctx["peak"], e,
                    {"note": "includes device CSR view of dst (sync for the range flag)"})
-    out[k] = v
-    del radial, zonal
 
-    x = torch.randn(n, 16, 128, device=device, generator=gen)
+
+def _op_rmsnorm(ctx, dtype):
+    from bysj_b200 import _C
+
+    n = ctx["g"].n_atoms
+    device = ctx["device"]
+    gen = torch.Generator(device=device).manual_seed(97)
+    x = torch.randn(n, 16, 128, device=device, generator=gen).to(dtype)
     w = torch.rand(4, 128, device=device, generator=gen) + 0.5
-    t = time_launches(lambda: _C.rmsnorm_forward(x, w, 1e-6), iters, flush)
-    k, v = op_line("rmsnorm_f32", 2 * n * 16 * 128 * 4 + 4 * n * 16 + 2048, t, peak, None,
-                   {"rows": n * 16, "note": "per-degree weights [4,128]"})
-    out[k] = v
-    xb = x.to(torch.bfloat16)
-    t = time_launches(lambda: _C.rmsnorm_forward(xb, w, 1e-6), iters, flush)
-    k, v = op_line("rmsnorm_bf16", 2 * n * 16 * 128 * 2 + 4 * n * 16 + 2048, t, peak, None,
-                   {"rows": n * 16})
-    out[k] = v
+    t = time_launches(lambda: _C.rmsnorm_forward(x, w, 1e-6), ctx["iters"], ctx["flush"])
+    size = 4 if dtype == torch.float32 else 2
+    name = "rmsnorm_f32" if dtype == torch.float32 else "rmsnorm_bf16"
+    return op_line(name, 2 * n * 16 * 128 * size + 4 * n * 16 + 2048, t, ctx["peak"], None,
+                   {"rows": n * 16, "note": "per-degree weights [4,128], L2 flushed"})
+
+
+OPS = {
+    "offsets": _op_offsets,
+    "attention_bf16": _op_attention_bf16,
+    "softmax": _op_softmax,
+    "segment_sum": _op_segment_sum,
+    "force": _op_force,
+    "force_random_order": lambda ctx: _op_force(ctx, shuffled=True),
+    "zonal": _op_zonal,
+    "rmsnorm": lambda ctx: _op_rmsnorm(ctx, torch.float32),
+    "rmsnorm_bf16": lambda ctx: _op_rmsnorm(ctx, torch.bfloat16),
+}
+
+
+def op_context(g, device, peak, logit=None, value32=None, iters=10):
+    """Shared inputs of the per-op lines; logits / values built on demand."""
+    from bysj_b200 import _C
+
+    flags = torch.zeros(1, dtype=torch.int32, device=device)
+    cache = {}
+
+    def lazy(name, make):
+        def get():
+            if name not in cache:
+                cache[name] = make()
+            return cache[name]
+        return get
+
+    gen = torch.Generator(device=device).manual_seed(17)
+    return {
+        "g": g, "device": device, "peak": peak, "iters": iters, "flags": flags,
+        "flush": Flusher(device),
+        "offsets": _C.segment_offsets_device(g.dst, g.n_atoms, flags),
+        "logit": (lambda: logit) if logit is not None else lazy(
+            "logit", lambda: torch.randn(g.n_edges, 8, device=device, generator=gen) * 2 ** 0.5),
+        "value32": (lambda: value32) if value32 is not None else lazy(
+            "value", lambda: torch.randn(g.n_edges, 16, 64, device=device, generator=gen)),
+    }
+
+
+def measure_ops(g, logit, value32, device, peak, iters=10, only=None):
+    ctx = op_context(g, device, peak, logit, value32, iters)
+    out = {}
+    for name, fn in OPS.items():
+        if only is not None and name != only:
+            continue
+        key, line = fn(ctx)
+        out[key] = line
     return out
 
 
@@ -537,15 +634,131 @@ def run_ours(args, dist):
         print(json.dumps(line), flush=True)
 
 
+def run_partition(args, dist):
+    """One large box split by destination-atom ranges over the ranks ("strong").
+
+    Per step and rank: ``force_assembly_src_partial`` over the local edges
+    (all atoms' source sums, written in the padded exchange layout), NCCL
+    reduce-scatter of those partials (asynchronous, on NCCL's stream),
+    ``segment_attention`` over the local edges meanwhile, then the wait and
+    ``force_assembly_dst_add`` for the local atoms.  Values fp32 [E, 16, 32],
+    logits fp32 [E, 8], dE/dr fp32 [E, 3].
+    """
+    from bysj_b200 import _C
+    from bysj_b200 import kernels as K
+    from bysj_b200 import sharding as S
+    from bysj_b200 import workloads as W
+
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    g = W.water_box(args.partition_atoms, density=0.1, seed=args.seed, device=device)
+    n, e_total = g.n_atoms, g.n_edges
+    offsets = K.segment_offsets(g.dst, n)
+    part = S.make_partition(offsets, g.src, dist.rank, dist.world)
+    e = part.n_edges
+    gen = torch.Generator(device=device).manual_seed(args.seed + 31)
+    grad_all = torch.randn(e_total, 3, device=device, generator=gen) * 0.1
+    vec_all = g.edge_vec
+    grad, vec = part.edges(grad_all).contiguous(), part.edges(vec_all).contiguous()
+    gen.manual_seed(args.seed + 1000 * dist.rank + 37)
+    logit = torch.randn(e, 8, device=device, generator=gen) * (2.0 ** 0.5)
+    value = torch.randn(e, 16, 32, device=device, generator=gen)
+    ex = S.ForceExchange(part)
+
+    def step(events=None):
+        ex.start(grad, vec)
+        if events is not None:
+            events[0].record()
+        out = _C.segment_attention_forward(logit, value, part.dst_offsets)
+        if events is not None:
+            events[1].record()
+        return out, ex.finish()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(args.steps)]
+    clocks = ClockSampler(device)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        _, (force, virial) = step(pairs[i])
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clock_info = clocks.stop()
+    step_max = dist.max(start.elapsed_time(end) / 1e3 / args.steps)
+    kernel_s = statistics.mean(a.elapsed_time(b) for a, b in pairs) / 1e3
+
+    # check: this rank's forces against the single-device assembly of the whole box
+    order, soff = K.group_by_source(g.src, n)
+    f_ref, v_ref = _C.force_assembly(grad_all, vec_all, offsets, soff, order)
+    err = max(float((force - part.atoms(f_ref)).abs().max()) if part.n_local else 0.0,
+              float((virial - part.atoms(v_ref)).abs().max()) if part.n_local else 0.0)
+    err = dist.max(err)
+    scale = float(f_ref.abs().max())
+    del f_ref, v_ref, order, soff
+
+    peak, peak_src = measured_peak()
+    alg = e * (32 + 16 * 32 * 4) + part.n_local * 16 * 32 * 4 + 8 * (part.n_local + 1)
+    achieved = alg / kernel_s / 1e9
+    if dist.rank == 0:
+        line = {
+            "metric": f"edges/s (dst-partitioned {n}-atom box: attention + force assembly)",
+            "value": e_total / step_max, "unit": UNIT, "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_max * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C5(b) one box, dst-range partition",
+                       "n_atoms": n, "n_edges": e_total, "edges_rank0": e,
+                       "atoms_rank0": part.n_local, "heads": 8, "components": 16,
+                       "channels": 32, "exchange_rows": part.world * part.chunk,
+                       "parallelism": f"dst-range partition x{dist.world}, NCCL reduce-scatter "
+                                      "of [N, 12] force partials overlapped with attention",
+                       "l2": "inputs larger than L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "segment_attention_kernel (rank 0)",
+                         "kernel_ms": kernel_s * 1e3, "peak_source": peak_src},
+            "check": {"max_abs_err_vs_single_device": err, "max_abs_force": scale},
+            "clocks": clock_info,
+            "gpu_launches": 3 * args.steps * dist.world,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_only(args):
+    """One operator on a box of ``--atoms`` atoms (profiling / tuning aid)."""
+    from bysj_b200 import workloads as W
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = W.water_box(args.atoms, density=0.1, seed=args.seed, device=device)
+    peak, _ = measured_peak()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    ops = measure_ops(g, None, None, device, peak, iters=max(args.steps, 1), only=args.only)
+    torch.cuda.profiler.stop()
+    print(json.dumps({"only": args.only, "atoms": g.n_atoms, "edges": g.n_edges, "ops": ops}),
+          flush=True)
+
+
 def main():
     args = parse_args()
     dist = Dist()
     if args.impl == "reference":
         run_reference(args, dist)
         return
+    if args.only:
+        run_only(args)
+        return
     dist.setup("nccl")
     try:
-        run_ours(args, dist)
+        (run_partition if args.mode == "partition" else run_ours)(args, dist)
     finally:
         dist.close()
 

@@ -57,6 +57,9 @@ struct Carver {
 inline bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
+inline bool aligned8(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 7u) == 0;
+}
 
 // ---------------------------------------------------------------------------
 // Device side: loads.

@@ -7,10 +7,10 @@
 // csrc/force_assembly.cpp:64-96.  The whole working set (grad_edge, edge_vec,
 // src_order: ~73 MB at 2.2 M edges) is small, so the kernel is bound by
 // memory latency rather than bandwidth; it maximises loads in flight: eight
-// lanes cooperate on one atom (four atoms per warp), each lane walking every
-// eighth edge of both CSR lists with independent loads, and the twelve fp64
-// sums are folded with a 3-step butterfly inside the 8-lane group.  The
-// summation order is fixed, so repeated runs are bit-identical.
+// lanes cooperate on one atom (four atoms per warp), each lane taking every
+// eighth edge of both CSR lists and issuing its loads in bursts, and the
+// twelve fp64 sums are folded with a 3-step butterfly inside the 8-lane
+// group.  The summation order is fixed, so repeated runs are bit-identical.
 #include "launch.cuh"
 
 namespace bysj {
@@ -21,8 +21,63 @@ constexpr int kAtomsPerWarp = kWarp / kLanesPerAtom;
 
 enum Mode : int { kAssemble = 0, kSrcPartial = 1 };
 
-template <int MODE>
-__global__ void __launch_bounds__(kBlock)
+// Loads of one lane are issued in bursts so that an atom costs a handful of
+// dependent memory round trips, not one per edge: up to kSlots source slots
+// (src_order) are fetched at once, then their grad/vec rows in batches of
+// kBatch, and the destination rows in batches of kBatch while those are in
+// flight.
+constexpr int kSlots = 12;
+constexpr int kBatch = 6;
+
+// Row e of an [E, 3] float array with two loads: the 8-byte-aligned pair
+// (components 0-1 for even e, 1-2 for odd e) and the remaining single.
+// Needs an 8-byte-aligned base; PAIR = false falls back to three loads.
+template <bool PAIR>
+__device__ __forceinline__ void load_row3(const float* __restrict__ base, int64_t e,
+                                          float (&v)[3]) {
+  const float* p = base + 3 * e;
+  if constexpr (PAIR) {
+    const bool odd = (e & 1) != 0;
+    const float2 pair = __ldg(reinterpret_cast<const float2*>(p + (odd ? 1 : 0)));
+    const float single = __ldg(p + (odd ? 0 : 2));
+    v[0] = odd ? single : pair.x;
+    v[1] = odd ? pair.x : pair.y;
+    v[2] = odd ? pair.y : single;
+  } else {
+    v[0] = __ldg(p);
+    v[1] = __ldg(p + 1);
+    v[2] = __ldg(p + 2);
+  }
+}
+
+template <bool PAIR>
+__device__ __forceinline__ void add_src_rows(const float* __restrict__ grad_edge,
+                                             const float* __restrict__ edge_vec,
+                                             const int64_t (&edge)[kBatch], int count,
+                                             double (&acc)[12]) {
+  float g[kBatch][3], v[kBatch][3];
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+    if (b < count) {
+      load_row3<PAIR>(grad_edge, edge[b], g[b]);
+      load_row3<PAIR>(edge_vec, edge[b], v[b]);
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+    if (b < count) {
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+        acc[r] -= g[b][r];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) acc[3 + r * 3 + c] -= static_cast<double>(g[b][r]) * v[b][c];
+      }
+    }
+  }
+}
+
+template <int MODE, bool PAIR>
+__global__ void __launch_bounds__(kBlock, 2)
     force_assembly_kernel(const float* __restrict__ grad_edge,
                           const float* __restrict__ edge_vec,
                           const int64_t* __restrict__ dst_offsets,
@@ -43,66 +98,67 @@ __global__ void __launch_bounds__(kBlock)
 #pragma unroll
     for (int c = 0; c < 12; ++c) acc[c] = 0.0;
     if (valid) {
+      int64_t d0 = 0, d1 = 0;
       if constexpr (MODE == kAssemble) {
-        const int64_t d0 = __ldg(dst_offsets + atom);
-        const int64_t d1 = __ldg(dst_offsets + atom + 1);
-        int64_t e = d0 + sub;
-        for (; e + kLanesPerAtom < d1; e += 2 * kLanesPerAtom) {
-          const float* g0 = grad_edge + e * 3;
-          const float* g1 = grad_edge + (e + kLanesPerAtom) * 3;
-          const float a0 = __ldg(g0), a1 = __ldg(g0 + 1), a2 = __ldg(g0 + 2);
-          const float b0 = __ldg(g1), b1 = __ldg(g1 + 1), b2 = __ldg(g1 + 2);
-          acc[0] += a0; acc[1] += a1; acc[2] += a2;
-          acc[0] += b0; acc[1] += b1; acc[2] += b2;
-        }
-        if (e < d1) {
-          const float* g0 = grad_edge + e * 3;
-          acc[0] += __ldg(g0); acc[1] += __ldg(g0 + 1); acc[2] += __ldg(g0 + 2);
-        }
+        d0 = __ldg(dst_offsets + atom) + sub;
+        d1 = __ldg(dst_offsets + atom + 1);
       }
-      const int64_t s0 = __ldg(src_offsets + atom);
       const int64_t s1 = __ldg(src_offsets + atom + 1);
-      int64_t s = s0 + sub;
-      for (; s + kLanesPerAtom < s1; s += 2 * kLanesPerAtom) {
-        const int64_t ea = __ldg(src_order + s);
-        const int64_t eb = __ldg(src_order + s + kLanesPerAtom);
-        float ga[3], va[3], gb[3], vb[3];
+      for (int64_t s = __ldg(src_offsets + atom) + sub; s < s1;
+           s += static_cast<int64_t>(kSlots) * kLanesPerAtom) {
+        // Burst 1: this lane's next kSlots source slots.
+        int64_t edge[kSlots];
+        int count = 0;
 #pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          ga[r] = __ldg(grad_edge + ea * 3 + r);
-          va[r] = __ldg(edge_vec + ea * 3 + r);
-          gb[r] = __ldg(grad_edge + eb * 3 + r);
-          vb[r] = __ldg(edge_vec + eb * 3 + r);
+        for (int t = 0; t < kSlots; ++t) {
+          const int64_t slot = s + static_cast<int64_t>(t) * kLanesPerAtom;
+          if (slot < s1) {
+            edge[t] = __ldg(src_order + slot);
+            count = t + 1;
+          }
         }
+        // Destination rows of this round (contiguous), issued before the
+        // gathers are consumed.
+        float dg[kBatch][3];
+        int dcount = 0;
+        if constexpr (MODE == kAssemble) {
 #pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          acc[r] -= ga[r];
-#pragma unroll
-          for (int c = 0; c < 3; ++c)
-            acc[3 + r * 3 + c] -= static_cast<double>(ga[r]) * va[c];
+          for (int b = 0; b < kBatch; ++b) {
+            const int64_t e = d0 + static_cast<int64_t>(b) * kLanesPerAtom;
+            if (e < d1) {
+              load_row3<PAIR>(grad_edge, e, dg[b]);
+              dcount = b + 1;
+            }
+          }
+          d0 += static_cast<int64_t>(kBatch) * kLanesPerAtom;
         }
+        // Bursts 2 and 3: the gathered rows, kBatch slots at a time.
 #pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          acc[r] -= gb[r];
+        for (int h = 0; h < kSlots / kBatch; ++h) {
+          int64_t part[kBatch];
 #pragma unroll
-          for (int c = 0; c < 3; ++c)
-            acc[3 + r * 3 + c] -= static_cast<double>(gb[r]) * vb[c];
+          for (int b = 0; b < kBatch; ++b) part[b] = edge[h * kBatch + b];
+          const int c = count - h * kBatch;
+          if (c > 0) add_src_rows<PAIR>(grad_edge, edge_vec, part, c < kBatch ? c : kBatch, acc);
+        }
+        if constexpr (MODE == kAssemble) {
+#pragma unroll
+          for (int b = 0; b < kBatch; ++b)
+            if (b < dcount) {
+              acc[0] += dg[b][0];
+              acc[1] += dg[b][1];
+              acc[2] += dg[b][2];
+            }
         }
       }
-      if (s < s1) {
-        const int64_t ea = __ldg(src_order + s);
-        float ga[3], va[3];
-#pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          ga[r] = __ldg(grad_edge + ea * 3 + r);
-          va[r] = __ldg(edge_vec + ea * 3 + r);
-        }
-#pragma unroll
-        for (int r = 0; r < 3; ++r) {
-          acc[r] -= ga[r];
-#pragma unroll
-          for (int c = 0; c < 3; ++c)
-            acc[3 + r * 3 + c] -= static_cast<double>(ga[r]) * va[c];
+      // Destination rows left over when an atom has more targets than sources.
+      if constexpr (MODE == kAssemble) {
+        for (; d0 < d1; d0 += kLanesPerAtom) {
+          float row[3];
+          load_row3<PAIR>(grad_edge, d0, row);
+          acc[0] += row[0];
+          acc[1] += row[1];
+          acc[2] += row[2];
         }
       }
     }
@@ -196,9 +252,14 @@ int bysj_force_assembly(const float* grad_edge, const float* edge_vec,
                        src_order == nullptr)))
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "force assembly: NULL pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  force_assembly_kernel<kAssemble><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
-      grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force,
-      virial, nullptr);
+  if (aligned8(grad_edge) && aligned8(edge_vec))
+    force_assembly_kernel<kAssemble, true><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force,
+        virial, nullptr);
+  else
+    force_assembly_kernel<kAssemble, false><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force,
+        virial, nullptr);
   return launch_check("force_assembly_kernel");
 }
 
@@ -217,9 +278,14 @@ int bysj_force_assembly_src_partial(const float* grad_edge,
                        src_order == nullptr)))
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "force partial: NULL pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  force_assembly_kernel<kSrcPartial><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
-      grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr,
-      nullptr, partial);
+  if (aligned8(grad_edge) && aligned8(edge_vec))
+    force_assembly_kernel<kSrcPartial, true><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr,
+        nullptr, partial);
+  else
+    force_assembly_kernel<kSrcPartial, false><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr,
+        nullptr, partial);
   return launch_check("force_assembly_kernel<src partial>");
 }
 

@@ -154,6 +154,120 @@ __global__ void __launch_bounds__(kBlock, 2) gie_fwd_kernel(GieArgs a) {
   }
 }
 
+// Forward for the degree-grouped row layout of DPA4's GIE: rows r = 0..R-1
+// with R = (L+1)^2 - 1, row r has degree l(r) = floor(sqrt(r+1)) and reads
+// radial slot l(r) + slot_base.  A lane owns one 4-channel column quad for
+// all R rows (LPE = C/4 lanes per edge, EG = 32/LPE edges side by side), so
+// per edge it loads each degree's radial quad once (L loads) plus the R zonal
+// coefficients, and the row -> slot choice is resolved at compile time.
+template <int LPE, int L>
+__global__ void __launch_bounds__(kBlock, 2) gie_fwd_degree_kernel(GieArgs a, int64_t slot_base) {
+  constexpr int R = (L + 1) * (L + 1) - 1;
+  constexpr int EG = kWarp / LPE;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int eg = lane / LPE;
+  const int c4 = lane % LPE;
+  const int64_t C = a.channels;
+  const int64_t block = (R + 1) * C;
+  const int64_t radial_row = a.n_radial * C;
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    float acc[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+    int64_t s = cur.lo + eg;
+    for (; s + EG < cur.hi; s += 2 * EG) {
+      float4 rad[2][L];
+      float z[2][R];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t slot = s + u * EG;
+        const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+        const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
+#pragma unroll
+        for (int l = 1; l <= L; ++l)
+          rad[u][l - 1] = __ldg(reinterpret_cast<const float4*>(rr + l * C));
+#pragma unroll
+        for (int r = 0; r < R; ++r) z[u][r] = __ldg(a.zonal + e * R + r);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int l = 1; l <= L; ++l)
+#pragma unroll
+          for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
+            acc[r][0] = fmaf(z[u][r], rad[u][l - 1].x, acc[r][0]);
+            acc[r][1] = fmaf(z[u][r], rad[u][l - 1].y, acc[r][1]);
+            acc[r][2] = fmaf(z[u][r], rad[u][l - 1].z, acc[r][2]);
+            acc[r][3] = fmaf(z[u][r], rad[u][l - 1].w, acc[r][3]);
+          }
+    }
+    if (s < cur.hi) {
+      const int64_t e = a.order ? __ldg(a.order + s) : s;
+      const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
+#pragma unroll
+      for (int l = 1; l <= L; ++l) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(rr + l * C));
+#pragma unroll
+        for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
+          const float z = __ldg(a.zonal + e * R + r);
+          acc[r][0] = fmaf(z, q.x, acc[r][0]);
+          acc[r][1] = fmaf(z, q.y, acc[r][1]);
+          acc[r][2] = fmaf(z, q.z, acc[r][2]);
+          acc[r][3] = fmaf(z, q.w, acc[r][3]);
+        }
+      }
+    }
+    if constexpr (EG > 1) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[r][i] = xor_sum(acc[r][i], LPE);
+    }
+    float* on = a.out + n * block;
+    if (cur.kind == kWhole) {
+      if (eg == 0) {
+        const float inv = __ldg(a.inv + n);
+        reinterpret_cast<float4*>(on)[c4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          reinterpret_cast<float4*>(on + (r + 1) * C)[c4] =
+              make_float4(acc[r][0] * inv, acc[r][1] * inv, acc[r][2] * inv, acc[r][3] * inv);
+      }
+      continue;
+    }
+    float* mine = a.ss.slot(p, cur.kind);
+    if (eg == 0) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) store_cg<4>(mine + r * C + 4 * c4, acc[r]);
+    }
+    const int64_t first = a.mp.part_of_first_edge(n);
+    const int64_t last = a.mp.part_of_end(n);
+    if (!arrive_last(a.ss, first, last, 0)) continue;
+    if (eg == 0) {
+      const float inv = __ldg(a.inv + n);
+      reinterpret_cast<float4*>(on)[c4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int64_t q = first; q <= last; ++q) {
+          float part[4];
+          load_cg<4>(a.ss.slot(q, q == last ? kHead : kTail) + r * C + 4 * c4, part);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sum[i] += part[i];
+        }
+        reinterpret_cast<float4*>(on + (r + 1) * C)[c4] =
+            make_float4(sum[0] * inv, sum[1] * inv, sum[2] * inv, sum[3] * inv);
+      }
+    }
+  }
+}
+
 // Backward.  Per edge, with gi = g[n] * inv[n] (g rows are re-read from L1):
 //   grad_zonal[e, r]     = sum_c gi[r, c] * radial[e, slot r, c]
 //   grad_radial[e, s, c] = sum_{r: slot r = s} gi[r, c] * zonal[e, r]
@@ -314,6 +428,60 @@ GieLayout gie_layout(bool vec_ok, int64_t n_edges, int64_t n_nodes,
   return L;
 }
 
+
+using GieDegreeKernel = void (*)(GieArgs, int64_t);
+
+template <int L>
+GieDegreeKernel gie_degree_pick(int64_t lpe) {
+  switch (lpe) {
+    case 1: return gie_fwd_degree_kernel<1, L>;
+    case 2: return gie_fwd_degree_kernel<2, L>;
+    case 4: return gie_fwd_degree_kernel<4, L>;
+    case 8: return gie_fwd_degree_kernel<8, L>;
+    case 16: return gie_fwd_degree_kernel<16, L>;
+    case 32: return gie_fwd_degree_kernel<32, L>;
+    default: return nullptr;
+  }
+}
+
+GieDegreeKernel gie_degree_kernel(int64_t degrees, int64_t channels) {
+  if (channels % 4 != 0) return nullptr;
+  const int64_t lpe = channels / 4;
+  switch (degrees) {
+    case 1: return gie_degree_pick<1>(lpe);
+    case 2: return gie_degree_pick<2>(lpe);
+    case 3: return gie_degree_pick<3>(lpe);
+    default: return nullptr;
+  }
+}
+
+struct GieDegreeLayout {
+  GieDegreeKernel kernel = nullptr;
+  PartitionPlan plan;
+  size_t bytes = 0;
+  SplitSlots ss{};
+};
+
+GieDegreeLayout gie_degree_layout(int64_t n_edges, int64_t n_nodes, int64_t degrees,
+                                  int64_t channels, void* ws) {
+  GieDegreeLayout L;
+  L.kernel = gie_degree_kernel(degrees, channels);
+  if (L.kernel == nullptr) return L;
+  const int64_t rows = (degrees + 1) * (degrees + 1) - 1;
+  const DeviceInfo& dev = current_device_info();
+  const int64_t resident = static_cast<int64_t>(dev.sm_count) *
+                           resident_blocks(reinterpret_cast<const void*>(L.kernel)) *
+                           kWarpsPerBlock;
+  L.plan = plan_partitions(n_edges, n_nodes, resident, 16);
+  const int64_t stride = (rows * channels + 7) / 8 * 8;
+  Carver carve(ws);
+  float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * stride);
+  int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts));
+  L.bytes = carve.need;
+  L.ss = SplitSlots{slots, tickets, stride, 1};
+  return L;
+}
+
 int gie_check(int64_t n_edges, int64_t n_nodes, int64_t rows, int64_t n_radial,
               int64_t channels) {
   if (n_edges < 0 || n_nodes < 0 || rows < 0 || n_radial < 0 || channels < 0)
@@ -390,6 +558,61 @@ int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
   L.cfg.kernel<<<grid, kBlock, 0, s>>>(a);
   return launch_check("gie_fwd_kernel");
+}
+
+size_t bysj_gie_zonal_scatter_degree_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                                    int64_t degrees, int64_t channels) {
+  if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
+  return gie_degree_layout(n_edges, n_nodes, degrees, channels, nullptr).bytes;
+}
+
+int bysj_gie_zonal_scatter_forward_degree(const float* zonal, const float* radial,
+                                          const int64_t* offsets, const int64_t* order,
+                                          int64_t slot_base, const float* inv_sqrt_deg,
+                                          int64_t n_edges, int64_t n_nodes, int64_t degrees,
+                                          int64_t n_radial, int64_t channels, float* out,
+                                          void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  clear_error();
+  const int64_t rows = (degrees + 1) * (degrees + 1) - 1;
+  int st = gie_check(n_edges, n_nodes, rows, n_radial, channels);
+  if (st) return st;
+  if (degrees < 1 || degrees > 3 || channels % 4 != 0 || channels > 128 ||
+      (channels / 4 & (channels / 4 - 1)) != 0)
+    return fail(BYSJ_ERR_UNSUPPORTED,
+                "zonal scatter (degree rows): needs 1..3 degrees and channels = 4 * 2^k <= 128");
+  // Degree l reads slot slot_base + l, l = 1..degrees.
+  if (slot_base < -1 || slot_base + degrees > n_radial - 1)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter (degree rows): slots out of range");
+  if (n_nodes == 0) return BYSJ_OK;
+  if (out == nullptr || inv_sqrt_deg == nullptr || offsets == nullptr ||
+      (n_edges > 0 && (zonal == nullptr || radial == nullptr)))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter (degree rows): NULL pointer");
+  if (!aligned16(radial) || !aligned16(out))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "zonal scatter (degree rows): radial and out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  GieDegreeLayout L = gie_degree_layout(n_edges, n_nodes, degrees, channels, workspace);
+  if (workspace == nullptr || workspace_bytes < L.bytes)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "zonal scatter (degree rows): workspace of %zu bytes needed, %zu given",
+                L.bytes, workspace_bytes);
+  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts, s),
+                  "zonal scatter (degree rows): ticket reset");
+  if (st) return st;
+  GieArgs a{};
+  a.zonal = zonal;
+  a.radial = radial;
+  a.order = order;
+  a.inv = inv_sqrt_deg;
+  a.out = out;
+  a.rows = rows;
+  a.n_radial = n_radial;
+  a.channels = channels;
+  a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
+  a.ss = L.ss;
+  L.kernel<<<L.plan.blocks, kBlock, 0, s>>>(a, slot_base);
+  return launch_check("gie_fwd_degree_kernel");
 }
 
 size_t bysj_gie_zonal_scatter_backward_workspace_size(int64_t n_edges,

@@ -17,11 +17,17 @@
 namespace bysj {
 namespace {
 
+// Degree l = floor(sqrt(i)) of irreps component i = r mod comps.  Row
+// counts below 2^32 use 32-bit arithmetic (64-bit division is slow).
 __device__ __forceinline__ int64_t degree_of_row(int64_t r, int64_t comps) {
-  const int64_t i = r % comps;
-  int64_t l = static_cast<int64_t>(sqrtf(static_cast<float>(i)));
+  uint32_t i;
+  if (r < (int64_t(1) << 32)) {
+    i = static_cast<uint32_t>(r) % static_cast<uint32_t>(comps);
+  } else {
+    i = static_cast<uint32_t>(r % comps);
+  }
+  uint32_t l = 0;
   while ((l + 1) * (l + 1) <= i) ++l;
-  while (l * l > i) --l;
   return l;
 }
 
@@ -65,10 +71,21 @@ __device__ __forceinline__ void store_row<__nv_bfloat16>(__nv_bfloat16* dst,
 }
 
 // G rows per warp (LPG = 32/G lanes each), NV vectors per lane, R row-blocks
-// loaded before any is reduced.
-template <typename T, int VEC, int NV, int G, int R>
+// loaded before any is reduced.  WMODE: 0 no weight, 1 one weight row,
+// 2 per-degree weight table.  Weights are staged once per CTA in shared
+// memory (at most kMaxSmemWeights floats), so the per-row cost is one
+// shared-memory vector load per vector.
+constexpr int kMaxSmemWeights = 8192;
+
+template <typename T, int VEC, int NV, int G, int R, int WMODE>
 __global__ void __launch_bounds__(kBlock) rmsnorm_fwd_kernel(NormArgs a) {
   constexpr int LPG = kWarp / G;
+  extern __shared__ __align__(16) float s_w[];  // weights, dynamic size
+  if constexpr (WMODE != 0) {
+    const int64_t count = (WMODE == 2 ? a.scale_rows : 1) * a.width;
+    for (int64_t i = threadIdx.x; i < count; i += blockDim.x) s_w[i] = __ldg(a.scale + i);
+    __syncthreads();
+  }
   const int lane = lane_id();
   const int g = lane / LPG;
   const int jl0 = lane % LPG;
@@ -82,6 +99,7 @@ __global__ void __launch_bounds__(kBlock) rmsnorm_fwd_kernel(NormArgs a) {
     const int64_t j = jl0 + k * LPG;
     jl[k] = j < a.lv ? j : a.lv - 1;
   }
+  const bool pow2_comps = (a.comps & (a.comps - 1)) == 0;
   const float inv_width = 1.0f / static_cast<float>(a.width);
   for (int64_t base = global_warp() * G * R; base < a.rows; base += step) {
     RowVec<T, VEC> buf[R][NV];
@@ -98,7 +116,7 @@ __global__ void __launch_bounds__(kBlock) rmsnorm_fwd_kernel(NormArgs a) {
       float ss = 0.0f;
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        if (jl0 + k * LPG < a.lv) {
+        if (jl0 + k * LPG < a.lv) {  // partial tiles: clamped lanes hold duplicates
 #pragma unroll
           for (int i = 0; i < VEC; ++i) {
             const float v = buf[rr][k].get(i);
@@ -110,20 +128,34 @@ __global__ void __launch_bounds__(kBlock) rmsnorm_fwd_kernel(NormArgs a) {
       const float inv = rsqrtf(ss * inv_width + a.eps);
       if (r >= a.rows) continue;
       if (jl0 == 0) a.inv_rms[r] = inv;
-      const float* w = nullptr;
-      if (a.scale) {
-        const int64_t l = a.scale_rows > 1 ? degree_of_row(r, a.comps) : 0;
-        w = a.scale + l * a.width;
+      int wrow = 0;
+      if constexpr (WMODE == 2) {
+        const uint32_t i = pow2_comps ? static_cast<uint32_t>(r) & static_cast<uint32_t>(a.comps - 1)
+                                      : static_cast<uint32_t>(r % a.comps);
+        wrow = (i >= 1) + (i >= 4) + (i >= 9) + (i >= 16) + (i >= 25) + (i >= 36) + (i >= 49);
       }
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         const int64_t j = jl0 + k * LPG;
         if (j < a.lv) {
           float v[VEC];
+          if constexpr (WMODE == 0) {
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) {
-            v[i] = buf[rr][k].get(i) * inv;
-            if (w) v[i] *= __ldg(w + j * VEC + i);
+            for (int i = 0; i < VEC; ++i) v[i] = buf[rr][k].get(i) * inv;
+          } else {
+            const float* w = s_w + wrow * a.width + j * VEC;
+#pragma unroll
+            for (int i = 0; i < VEC; i += (VEC % 4 == 0 ? 4 : 1)) {
+              if constexpr (VEC % 4 == 0) {
+                const float4 t = *reinterpret_cast<const float4*>(w + i);
+                v[i] = buf[rr][k].get(i) * inv * t.x;
+                v[i + 1] = buf[rr][k].get(i + 1) * inv * t.y;
+                v[i + 2] = buf[rr][k].get(i + 2) * inv * t.z;
+                v[i + 3] = buf[rr][k].get(i + 3) * inv * t.w;
+              } else {
+                v[i] = buf[rr][k].get(i) * inv * w[i];
+              }
+            }
           }
           store_row<T>(y + r * a.width + j * VEC, v, VEC);
         }
@@ -239,21 +271,28 @@ __global__ void __launch_bounds__(kBlock)
 
 using NormKernel = void (*)(NormArgs);
 
-template <typename T, int VEC>
-NormKernel norm_pick(int64_t lv, int* g_out) {
+template <typename T, int VEC, int WM>
+NormKernel norm_pick_w(int64_t lv, int* g_out) {
   *g_out = 1;
   if (lv > 256) return nullptr;
-  if (lv > 128) return rmsnorm_fwd_kernel<T, VEC, 8, 1, 1>;
-  if (lv > 64) return rmsnorm_fwd_kernel<T, VEC, 4, 1, 2>;
-  if (lv > 32) return rmsnorm_fwd_kernel<T, VEC, 2, 1, 4>;
+  if (lv > 128) return rmsnorm_fwd_kernel<T, VEC, 8, 1, 1, WM>;
+  if (lv > 64) return rmsnorm_fwd_kernel<T, VEC, 4, 1, 2, WM>;
+  if (lv > 32) return rmsnorm_fwd_kernel<T, VEC, 2, 1, 4, WM>;
   switch (next_pow2(lv)) {
-    case 32: return rmsnorm_fwd_kernel<T, VEC, 1, 1, 4>;
-    case 16: *g_out = 2; return rmsnorm_fwd_kernel<T, VEC, 1, 2, 4>;
-    case 8: *g_out = 4; return rmsnorm_fwd_kernel<T, VEC, 1, 4, 4>;
-    case 4: *g_out = 8; return rmsnorm_fwd_kernel<T, VEC, 1, 8, 4>;
-    case 2: *g_out = 16; return rmsnorm_fwd_kernel<T, VEC, 1, 16, 4>;
-    default: *g_out = 32; return rmsnorm_fwd_kernel<T, VEC, 1, 32, 4>;
+    case 32: return rmsnorm_fwd_kernel<T, VEC, 1, 1, 4, WM>;
+    case 16: *g_out = 2; return rmsnorm_fwd_kernel<T, VEC, 1, 2, 4, WM>;
+    case 8: *g_out = 4; return rmsnorm_fwd_kernel<T, VEC, 1, 4, 4, WM>;
+    case 4: *g_out = 8; return rmsnorm_fwd_kernel<T, VEC, 1, 8, 4, WM>;
+    case 2: *g_out = 16; return rmsnorm_fwd_kernel<T, VEC, 1, 16, 4, WM>;
+    default: *g_out = 32; return rmsnorm_fwd_kernel<T, VEC, 1, 32, 4, WM>;
   }
+}
+
+template <typename T, int VEC>
+NormKernel norm_pick(int64_t lv, int wmode, int* g_out) {
+  if (wmode == 0) return norm_pick_w<T, VEC, 0>(lv, g_out);
+  if (wmode == 1) return norm_pick_w<T, VEC, 1>(lv, g_out);
+  return norm_pick_w<T, VEC, 2>(lv, g_out);
 }
 
 int64_t scale_comps(int64_t scale_rows) { return scale_rows * scale_rows; }
@@ -306,28 +345,42 @@ int bysj_rmsnorm_forward(const void* x, int dtype, int64_t rows, int64_t width,
   a.eps = eps;
   const bool bf16 = dtype == BYSJ_BF16;
   const int vec = bf16 ? 8 : 4;
-  const bool vec_ok = width % vec == 0 && aligned16(x) && aligned16(y);
+  const bool vec_ok = width % vec == 0 && aligned16(x) && aligned16(y) &&
+                      (scale == nullptr || aligned16(scale));
   int g = 1;
   NormKernel k = nullptr;
-  if (vec_ok) {
-    a.lv = width / vec;
-    k = bf16 ? norm_pick<__nv_bfloat16, 8>(a.lv, &g) : norm_pick<float, 4>(a.lv, &g);
-  } else {
-    a.lv = width;
-    k = bf16 ? norm_pick<__nv_bfloat16, 1>(a.lv, &g) : norm_pick<float, 1>(a.lv, &g);
+  // Weights staged in shared memory when they fit; otherwise the two-pass
+  // wide kernel reads them from global memory.
+  const int wmode = scale == nullptr ? 0 : (scale_rows > 1 ? 2 : 1);
+  const bool smem_ok = scale == nullptr || scale_rows * width <= kMaxSmemWeights;
+  const bool table_ok = scale_rows <= 8;  // degree test covers components < 64
+  if (smem_ok && table_ok) {
+    if (vec_ok) {
+      a.lv = width / vec;
+      k = bf16 ? norm_pick<__nv_bfloat16, 8>(a.lv, wmode, &g)
+               : norm_pick<float, 4>(a.lv, wmode, &g);
+    } else {
+      a.lv = width;
+      k = bf16 ? norm_pick<__nv_bfloat16, 1>(a.lv, wmode, &g)
+               : norm_pick<float, 1>(a.lv, wmode, &g);
+    }
   }
   const DeviceInfo& dev = current_device_info();
-  if (k == nullptr) {
+  const bool wide = k == nullptr;
+  if (wide) {
     k = bf16 ? rmsnorm_fwd_wide_kernel<__nv_bfloat16> : rmsnorm_fwd_wide_kernel<float>;
     g = 1;
   }
+  const size_t smem = (wide || wmode == 0)
+                          ? 0
+                          : sizeof(float) * static_cast<size_t>(wmode == 2 ? scale_rows : 1) * width;
   const int64_t resident = static_cast<int64_t>(dev.sm_count) *
-                           resident_blocks(reinterpret_cast<const void*>(k));
+                           resident_blocks(reinterpret_cast<const void*>(k), smem);
   int64_t blocks = (rows + static_cast<int64_t>(kWarpsPerBlock) * g - 1) /
                    (static_cast<int64_t>(kWarpsPerBlock) * g);
   if (blocks > resident) blocks = resident;
   if (blocks < 1) blocks = 1;
-  k<<<static_cast<unsigned>(blocks), kBlock, 0, s>>>(a);
+  k<<<static_cast<unsigned>(blocks), kBlock, smem, s>>>(a);
   return launch_check("rmsnorm_fwd_kernel");
 }
 

@@ -37,7 +37,12 @@ struct SmxArgs {
   MergePath mp;
   SplitSlots ss;         // partial statistics  [parts][2][2*cpad]
   float* final_stats;    // combined statistics [parts][2*cpad]
+  int* big_split;        // set when a split segment is left to the second pass
 };
+
+// Split segments up to this many edges are written by the piece that
+// combines them; longer ones by the second, equally partitioned pass.
+constexpr int64_t kSelfWrite = 4096;
 
 template <int NC, int G>
 struct SmxShape {
@@ -196,6 +201,259 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_fwd_split_kernel(SmxAr
       inv[k] = ok[k] ? __ldcg(fin + a.cpad + ch[k]) : 0.0f;
     }
     smx_fwd_write<NC, G>(a, cur.lo, cur.hi, g, ch, ok, m, inv);
+  }
+}
+
+// ---- forward, quad-vector form (C % 4 == 0, C <= 128) ------------------------
+// Lanes of a warp are (edge group g, channel quad q): LP = pow2(C/4) lanes per
+// edge row, G = 32/LP rows side by side, T rows per lane per chunk.  A chunk
+// of G*T rows is loaded in one burst of 16-byte loads; each lane keeps a
+// running (max, denominator) per channel, rescaled when the max grows, and
+// the G groups are merged with a fixed butterfly.  A segment that fits in
+// one chunk is written straight from registers (one read, one write of the
+// logits); longer segments re-read their rows (from L1/L2) for the write.
+template <int LP>
+struct QuadSmx {
+  static constexpr int G = kWarp / LP;
+  static constexpr int T =
+      LP >= 16 ? 8 : ((128 / G) < 8 ? 8 : ((128 / G) > 16 ? 16 : (128 / G)));
+  static constexpr int CHUNK = G * T;
+};
+
+__device__ __forceinline__ float quad_get(const float4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ void quad_set(float4& v, int i, float x) {
+  if (i == 0) v.x = x; else if (i == 1) v.y = x; else if (i == 2) v.z = x; else v.w = x;
+}
+
+// Loads the gated logits of slots base + g + t*G (t < T) into x (-inf past
+// `hi` and for masked edges).
+template <int LP>
+__device__ __forceinline__ void quad_load(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                          int q, bool qok, float4 (&x)[QuadSmx<LP>::T]) {
+  using Q = QuadSmx<LP>;
+  const int64_t C = a.channels;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    const int64_t s = base + g + static_cast<int64_t>(t) * Q::G;
+    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (qok && s < hi) {
+      const int64_t e = a.order ? __ldg(a.order + s) : s;
+      v = __ldg(reinterpret_cast<const float4*>(a.x + e * C) + q);
+      if (a.env) {
+        const float env = __ldg(a.env + e);
+        if (env > 0.0f) {
+          const float shift = 2.0f * logf(env);
+          v.x += shift; v.y += shift; v.z += shift; v.w += shift;
+        } else {
+          v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
+      }
+    }
+    x[t] = v;
+  }
+}
+
+template <int LP>
+__device__ __forceinline__ void quad_write(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                           int q, bool qok, const float4 (&x)[QuadSmx<LP>::T],
+                                           const float (&m)[4], const float (&inv)[4]) {
+  using Q = QuadSmx<LP>;
+  if (!qok) return;
+  const int64_t C = a.channels;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    const int64_t s = base + g + static_cast<int64_t>(t) * Q::G;
+    if (s >= hi) break;
+    const int64_t e = a.order ? __ldg(a.order + s) : s;
+    float4 o;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) quad_set(o, i, shifted_exp(quad_get(x[t], i), m[i]) * inv[i]);
+    reinterpret_cast<float4*>(a.out + e * C)[q] = o;
+  }
+}
+
+template <int LP, bool kSplitPass>
+__global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t C = a.channels;
+  const bool qok = 4 * q < C;
+  if constexpr (kSplitPass) {
+    if (*reinterpret_cast<volatile int*>(a.big_split) == 0) return;
+  }
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const bool whole = cur.kind == kWhole;
+    float4 x[Q::T];
+    float m[4], inv[4];
+    if constexpr (kSplitPass) {
+      if (whole) continue;
+      if (__ldg(a.mp.offsets + n + 1) - __ldg(a.mp.offsets + n) <= kSelfWrite) continue;
+      const float* fin = a.final_stats + a.mp.part_of_end(n) * 2 * a.cpad;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        m[i] = qok ? __ldcg(fin + 4 * q + i) : 0.0f;
+        inv[i] = qok ? __ldcg(fin + a.cpad + 4 * q + i) : 0.0f;
+      }
+      for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+        quad_load<LP>(a, base, cur.hi, g, q, qok, x);
+        quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
+      }
+      continue;
+    } else {
+      float d[4];
+      const bool one_chunk = cur.hi - cur.lo <= Q::CHUNK;
+      float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (whole && a.xn && qok) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+        nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
+      }
+      if (one_chunk) {
+        // Exact two-step form: maximum first, then each exponential once;
+        // x keeps exp(l - m) for the write.
+        quad_load<LP>(a, cur.lo, cur.hi, g, q, qok, x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float cm = -INFINITY;
+#pragma unroll
+          for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
+          for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
+          m[i] = fmaxf(cm, nl[i]);
+          float acc = 0.0f;
+#pragma unroll
+          for (int t = 0; t < Q::T; ++t) {
+            const float w = shifted_exp(quad_get(x[t], i), m[i]);
+            quad_set(x[t], i, w);
+            acc += w;
+          }
+          for (int st = LP; st < kWarp; st <<= 1) acc += __shfl_xor_sync(kFull, acc, st);
+          d[i] = acc;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
+        for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+          quad_load<LP>(a, base, cur.hi, g, q, qok, x);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float cm = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
+            const float mn = fmaxf(m[i], cm);
+            float acc = d[i] * shifted_exp(m[i], mn);
+#pragma unroll
+            for (int t = 0; t < Q::T; ++t) acc += shifted_exp(quad_get(x[t], i), mn);
+            d[i] = acc;
+            m[i] = mn;
+          }
+        }
+        // Merge the G edge groups (fixed butterfly; every lane ends equal).
+        for (int st = LP; st < kWarp; st <<= 1) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float mo = __shfl_xor_sync(kFull, m[i], st);
+            const float dd = __shfl_xor_sync(kFull, d[i], st);
+            const float mn = fmaxf(m[i], mo);
+            d[i] = d[i] * shifted_exp(m[i], mn) + dd * shifted_exp(mo, mn);
+            m[i] = mn;
+          }
+        }
+      }
+      if (whole) {
+        float w0[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          // one_chunk: m already includes the null logit and x holds
+          // exp(l - m); otherwise rescale the running sum to the final max.
+          const float mm = fmaxf(m[i], nl[i]);
+          w0[i] = shifted_exp(nl[i], mm);
+          const float total = (one_chunk ? d[i] : d[i] * shifted_exp(m[i], mm)) + w0[i];
+          inv[i] = total > 0.0f ? 1.0f / total : 0.0f;
+          m[i] = mm;
+        }
+        if (g == 0 && qok && a.out_null) {
+          reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+              make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
+        }
+        if (one_chunk) {
+          if (qok) {
+#pragma unroll
+            for (int t = 0; t < Q::T; ++t) {
+              const int64_t sl = cur.lo + g + static_cast<int64_t>(t) * Q::G;
+              if (sl >= cur.hi) break;
+              const int64_t e = a.order ? __ldg(a.order + sl) : sl;
+              reinterpret_cast<float4*>(a.out + e * C)[q] =
+                  make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+            }
+          }
+        } else {
+          for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+            quad_load<LP>(a, base, cur.hi, g, q, qok, x);
+            quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
+          }
+        }
+        continue;
+      }
+      // Split segment: publish per-channel (m, d); the last piece combines.
+      float* mine = a.ss.slot(p, cur.kind);
+      if (g == 0 && qok) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          __stcg(mine + 4 * q + i, m[i]);
+          __stcg(mine + a.cpad + 4 * q + i, d[i]);
+        }
+      }
+      const int64_t first = a.mp.part_of_first_edge(n);
+      const int64_t last = a.mp.part_of_end(n);
+      if (!arrive_last(a.ss, first, last, 0)) continue;
+      // Every lane combines its own channel quad (the G copies agree).
+      if (a.xn && qok) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+        nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
+      }
+      float* fin = a.final_stats + last * 2 * a.cpad;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t c = 4 * q + i;
+        float mm = nl[i];
+        float total = 0.0f;
+        if (qok) {
+          for (int64_t qq = first; qq <= last; ++qq)
+            mm = fmaxf(mm, __ldcg(a.ss.slot(qq, qq == last ? kHead : kTail) + c));
+          total = shifted_exp(nl[i], mm);
+          for (int64_t qq = first; qq <= last; ++qq) {
+            const float* sq = a.ss.slot(qq, qq == last ? kHead : kTail);
+            total += shifted_exp(__ldcg(sq + c), mm) * __ldcg(sq + a.cpad + c);
+          }
+        }
+        const float iv = total > 0.0f ? 1.0f / total : 0.0f;
+        m[i] = mm;
+        inv[i] = iv;
+        if (g == 0 && qok) {
+          if (a.out_null) a.out_null[n * C + c] = shifted_exp(nl[i], mm) * iv;
+          __stcg(fin + c, mm);
+          __stcg(fin + a.cpad + c, iv);
+        }
+      }
+      const int64_t seg_lo = __ldg(a.mp.offsets + n);
+      const int64_t seg_hi = __ldg(a.mp.offsets + n + 1);
+      if (seg_hi - seg_lo <= kSelfWrite) {
+        for (int64_t base = seg_lo; base < seg_hi; base += Q::CHUNK) {
+          quad_load<LP>(a, base, seg_hi, g, q, qok, x);
+          quad_write<LP>(a, base, seg_hi, g, q, qok, x, m, inv);
+        }
+      } else if (lane == 0) {
+        atomicExch(a.big_split, 1);
+      }
+    }
   }
 }
 
@@ -381,8 +639,28 @@ SmxConfig smx_make(bool backward) {
   return c;
 }
 
-SmxConfig smx_config(int64_t channels, bool backward) {
+template <int LP>
+SmxConfig quad_make() {
   SmxConfig c;
+  c.main = segment_softmax_quad_kernel<LP, false>;
+  c.split = segment_softmax_quad_kernel<LP, true>;
+  c.tc = 4 * LP;
+  c.tiles = 1;
+  return c;
+}
+
+SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok) {
+  SmxConfig c;
+  if (!backward && quad_ok && channels % 4 == 0 && channels <= 128) {
+    switch (next_pow2(channels / 4)) {
+      case 1: return quad_make<1>();
+      case 2: return quad_make<2>();
+      case 4: return quad_make<4>();
+      case 8: return quad_make<8>();
+      case 16: return quad_make<16>();
+      default: return quad_make<32>();
+    }
+  }
   if (channels > 128) c = smx_make<8, 1>(backward);
   else if (channels > 64) c = smx_make<4, 1>(backward);
   else if (channels > 32) c = smx_make<2, 1>(backward);
@@ -410,9 +688,9 @@ struct SmxLayout {
 };
 
 SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
-                     bool backward, void* ws) {
+                     bool backward, void* ws, bool quad_ok = true) {
   SmxLayout L;
-  L.cfg = smx_config(channels, backward);
+  L.cfg = smx_config(channels, backward, quad_ok);
   const DeviceInfo& dev = current_device_info();
   const int64_t resident =
       static_cast<int64_t>(dev.sm_count) *
@@ -424,7 +702,7 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
   L.cpad = (channels + 3) / 4 * 4;
   Carver carve(ws);
   float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * 2 * L.cpad);
-  int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts) * L.cfg.tiles);
+  int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts) * L.cfg.tiles + 1);
   L.final_stats = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * L.cpad);
   L.bytes = carve.need;
   L.ss = SplitSlots{slots, tickets, 2 * L.cpad, static_cast<int>(L.cfg.tiles)};
@@ -433,13 +711,15 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
 
 int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
             const int64_t* offsets, cudaStream_t s, const char* name) {
+  // Tickets and the big-split flag after them start at zero.
   int st = cuda_check(
-      cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts * L.cfg.tiles, s),
+      cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * (L.plan.parts * L.cfg.tiles + 1), s),
       "segment softmax: ticket reset");
   if (st) return st;
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
   a.final_stats = L.final_stats;
+  a.big_split = L.ss.tickets + L.plan.parts * L.cfg.tiles;
   a.cpad = L.cpad;
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
   L.cfg.main<<<grid, kBlock, 0, s>>>(a);
@@ -468,7 +748,10 @@ extern "C" {
 size_t bysj_segment_softmax_workspace_size(int64_t n_edges, int64_t n_nodes,
                                            int64_t channels) {
   if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
-  return smx_layout(n_edges, n_nodes, channels, false, nullptr).bytes;
+  // Pointer alignment picks the quad-vector or the scalar kernel; size for both.
+  const size_t a = smx_layout(n_edges, n_nodes, channels, false, nullptr, true).bytes;
+  const size_t b = smx_layout(n_edges, n_nodes, channels, false, nullptr, false).bytes;
+  return a > b ? a : b;
 }
 
 int bysj_segment_softmax_forward(const float* logit, const float* env,
@@ -487,7 +770,10 @@ int bysj_segment_softmax_forward(const float* logit, const float* env,
   if (n_nodes == 0) return BYSJ_OK;
   if (n_edges > 0 && (logit == nullptr || alpha == nullptr))
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment softmax: NULL logit/alpha");
-  SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace);
+  const bool quad_ok = aligned16(logit) && aligned16(alpha) &&
+                       (null_logit == nullptr || aligned16(null_logit)) &&
+                       (null_alpha == nullptr || aligned16(null_alpha));
+  SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace, quad_ok);
   if (workspace == nullptr || workspace_bytes < L.bytes)
     return fail(BYSJ_ERR_WORKSPACE,
                 "segment softmax: workspace of %zu bytes needed, %zu given",

@@ -465,6 +465,26 @@ void check_gie(const Tensor& zonal, const Tensor& radial, const Tensor& dst,
               "GIE inv_sqrt_deg must have shape (n_nodes,) or (n_nodes, 1, 1)");
 }
 
+// Number of degrees L when radial_slot is the degree-grouped layout
+// slot[r] = floor(sqrt(r+1)) + base with rows == (L+1)^2 - 1 (L <= 3), else 0.
+// Reads the (tiny) slot table back to the host.
+int64_t degree_layout(const Tensor& radial_slot, int64_t rows, int64_t n_radial) {
+  int64_t degrees = 0;
+  for (int64_t l = 1; l <= 3; ++l)
+    if ((l + 1) * (l + 1) - 1 == rows) degrees = l;
+  if (degrees == 0) return 0;
+  Tensor host = radial_slot.to(torch::kCPU);
+  const int64_t* slot = host.data_ptr<int64_t>();
+  const int64_t base = slot[0] - 1;
+  for (int64_t r = 0; r < rows; ++r) {
+    int64_t l = 0;
+    while ((l + 1) * (l + 1) <= r + 1) ++l;
+    if (slot[r] != l + base) return 0;
+  }
+  if (base < -1 || base + degrees > n_radial - 1) return 0;
+  return degrees;
+}
+
 Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor radial_slot,
                                  Tensor inv_sqrt_deg) {
   check_gie(zonal, radial, dst, radial_slot, inv_sqrt_deg);
@@ -475,6 +495,21 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
   Tensor out = torch::empty({nodes, rows + 1, channels}, zonal.options());
   if (nodes == 0) return out;
   auto [offsets, order] = csr_view(dst, nodes);
+  const int64_t degrees = degree_layout(radial_slot, rows, n_radial);
+  if (degrees > 0 && channels % 4 == 0 && channels <= 128 &&
+      ((channels / 4) & (channels / 4 - 1)) == 0 &&
+      reinterpret_cast<uintptr_t>(radial.data_ptr()) % 16 == 0) {
+    const int64_t base = radial_slot.index({0}).item<int64_t>() - 1;
+    Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_degree_workspace_size(edges, nodes,
+                                                                              degrees, channels));
+    check(bysj_gie_zonal_scatter_forward_degree(
+              zonal.data_ptr<float>(), radial.data_ptr<float>(), offsets.data_ptr<int64_t>(),
+              opt_ptr<int64_t>(order), base, inv_sqrt_deg.data_ptr<float>(), edges, nodes,
+              degrees, n_radial, channels, out.data_ptr<float>(), ws.data_ptr(),
+              static_cast<size_t>(ws.numel()), stream_of(zonal)),
+          "gie_zonal_scatter_forward");
+    return out;
+  }
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_workspace_size(edges, nodes, rows, channels));
   check(bysj_gie_zonal_scatter_forward(
             zonal.data_ptr<float>(), radial.data_ptr<float>(), offsets.data_ptr<int64_t>(),

@@ -290,6 +290,24 @@ BYSJ_API int bysj_gie_zonal_scatter_forward(const float* zonal, const float* rad
                                    float* out, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/* Same operator for the degree-grouped row layout the DPA4 GIE uses: rows
+ * r = 0 .. (degrees+1)^2 - 2, row r has degree l = floor(sqrt(r + 1)) and
+ * reads radial slot l + slot_base (slot_base = 0 for slots 1..L, -1 for
+ * slots 0..L-1), i.e. radial_slot[r] == floor(sqrt(r+1)) + slot_base.  It
+ * needs 1 <= degrees <= 3, channels = 4 * 2^k <= 128 and 16-byte-aligned
+ * radial and out; each lane then loads every degree's radial row once per
+ * edge instead of once per output row. */
+BYSJ_API size_t bysj_gie_zonal_scatter_degree_workspace_size(int64_t n_edges,
+                                                             int64_t n_nodes,
+                                                             int64_t degrees,
+                                                             int64_t channels);
+BYSJ_API int bysj_gie_zonal_scatter_forward_degree(
+    const float* zonal, const float* radial, const int64_t* offsets,
+    const int64_t* order, int64_t slot_base, const float* inv_sqrt_deg,
+    int64_t n_edges, int64_t n_nodes, int64_t degrees, int64_t n_radial,
+    int64_t channels, float* out, void* workspace, size_t workspace_bytes,
+    void* stream);
+
 /* grad_zonal[e, r]     = inv[dst e] * sum_c g[dst e, r+1, c] radial[e, slot r, c]
  * grad_radial[e, s, c] = inv[dst e] * sum_{r: slot r = s} g[dst e, r+1, c] zonal[e, r]
  * grad_inv[n]          = sum_{r,c} g[n, r+1, c] * sum_{e in n} zonal[e,r] radial[e, slot r, c]

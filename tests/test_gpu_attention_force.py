@@ -129,6 +129,22 @@ def test_force_c1_matches_oracle_and_conserves_momentum(cuda):
     assert torch.equal(force, f2) and torch.equal(virial, v2)
 
 
+def test_force_heavy_atoms_use_several_slot_rounds(cuda):
+    # more than 12 slots per lane (8 lanes per atom): the slot loop repeats
+    gen = torch.Generator().manual_seed(21)
+    sizes = torch.randint(80, 400, (64,), generator=gen)
+    dst = torch.repeat_interleave(torch.arange(64), sizes)
+    off = torch.zeros(65, dtype=torch.int64)
+    off[1:] = torch.cumsum(sizes, 0)
+    e = dst.numel()
+    src = torch.randint(0, 64, (e,), generator=gen)
+    grad, vec = torch.randn(e, 3, generator=gen), torch.randn(e, 3, generator=gen)
+    force, virial = K.force_assembly(grad.cuda(), vec.cuda(), src.cuda(), dst.cuda(), off.cuda())
+    tf, tv = truth.force_assembly(grad.numpy(), vec.numpy(), src.numpy(), dst.numpy(), 64)
+    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=1e-6, atol=1e-4)
+    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=1e-6, atol=1e-4)
+
+
 def test_force_skewed_and_empty_atom(cuda):
     sizes = skewed_sizes(6, nodes=120, giant=3000)
     dst, off = graph(sizes)
@@ -142,3 +158,34 @@ def test_force_skewed_and_empty_atom(cuda):
                                   sizes.numel())
     np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=1e-6, atol=1e-5)
     np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("parts", [2, 3])
+def test_force_dst_range_partition_matches_single_device(cuda, parts):
+    # ranks emulated on one GPU: the reduce-scatter becomes a plain sum of the padded partials
+    from bysj_b200 import sharding as S
+
+    g = W.c1_box(device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    grad = torch.randn(g.n_edges, 3, device="cuda", generator=gen)
+    off = K.segment_offsets(g.dst, g.n_atoms)
+    force, virial = K.force_assembly(grad, g.edge_vec, g.src, g.dst, off)
+    plan = [S.make_partition(off, g.src, r, parts) for r in range(parts)]
+    partials = [_C().force_assembly_src_partial(p.edges(grad), p.edges(g.edge_vec),
+                                                p.src_offsets, p.src_order) for p in plan]
+    total = torch.stack(partials).double().sum(0).float()
+    got_f, got_v = [], []
+    for p in plan:
+        f, v = S.force_assembly_partitioned(
+            p.edges(grad), p.edges(g.edge_vec), p,
+            combine=lambda _, q: total[q.rank * q.chunk:(q.rank + 1) * q.chunk])
+        got_f.append(f)
+        got_v.append(v)
+    torch.testing.assert_close(torch.cat(got_f), force, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(torch.cat(got_v), virial, rtol=1e-5, atol=1e-5)
+
+
+def _C():
+    from bysj_b200 import _C as ext
+
+    return ext

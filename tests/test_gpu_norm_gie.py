@@ -166,3 +166,33 @@ def test_gie_c1_geometry_matches_float64(cuda):
     np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5,
                                atol=1e-5 * float(np.abs(want).max()))
     assert torch.equal(out, K.zonal_scatter(zonal, radial, g.dst, slot, inv))
+
+
+@pytest.mark.parametrize("zero_based,channels", [(True, 64), (False, 16), (True, 128), (False, 4)])
+def test_gie_degree_layout_with_split_segments(cuda, zero_based, channels):
+    # Rows grouped by degree (the DPA4 layout) take the degree-specialised
+    # kernel; a skewed graph forces segments split across partitions.
+    gen = torch.Generator().manual_seed(channels)
+    sizes = torch.randint(0, 10, (300,), generator=gen)
+    sizes[50], sizes[-1] = 3000, 1200
+    dst = torch.repeat_interleave(torch.arange(300), sizes)
+    e = dst.numel()
+    zonal = torch.randn(e, 15, generator=gen)
+    radial = torch.randn(e, 4, channels, generator=gen)
+    slot = W.degree_slots(zero_based=zero_based)
+    inv = torch.rand(300, generator=gen) + 0.2
+    out = K.zonal_scatter(zonal.cuda(), radial.cuda(), dst.cuda(), slot.cuda(), inv.cuda())
+    want = truth.zonal_scatter(zonal.numpy(), radial.numpy(), dst.numpy(), slot.numpy(),
+                               inv.numpy())
+    np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5,
+                               atol=1e-5 * float(np.abs(want).max()))
+    assert out[:, 0, :].count_nonzero() == 0
+
+
+def test_rmsnorm_misaligned_scale_view(cuda):
+    x = torch.randn(64, 128, device="cuda")
+    big = torch.randn(129, device="cuda")
+    scale = big[1:]  # contiguous view whose data pointer is 4 bytes past alignment
+    got = K.rmsnorm(x, scale)
+    torch.testing.assert_close(got.cpu(), reference_rmsnorm(x.cpu(), scale.cpu()), rtol=2e-5,
+                               atol=2e-5)
