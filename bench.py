@@ -267,13 +267,20 @@ def cpu_sample_rate(g, logit, value, sample_nodes=2048, repeats=3):
 # ---------------------------------------------------------------------------
 
 class Flusher:
-    """Writes 512 MB between timed launches so a small working set starts cold."""
+    """Evicts a small working set from L2 between timed launches.
+
+    Writes 512 MB (4x the 126 MB L2), then reads another 256 MB so that the
+    lines left in L2 are clean: the next timed kernel starts with none of its
+    inputs cached and pays no write-back of the flush's own dirty lines.
+    """
 
     def __init__(self, device):
         self.buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+        self.clean = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     def __call__(self):
         self.buf.fill_(1.0)
+        self.clean.sum()
 
 
 def time_launches(fn, iters, flush=None):

@@ -238,6 +238,15 @@ __device__ __forceinline__ float shifted_exp(float x, float m) {
   return (x == -INFINITY || m == -INFINITY) ? 0.0f : expf(x - m);
 }
 
+// exp(x - m) by the __expf intrinsic (one ex2 on the transcendental pipe).
+// CUDA documents its error as 2 + floor(|1.173 (x - m)|) ulp; outputs of a
+// softmax matter to an absolute 1e-6 only for x - m >= -14, where that is at
+// most 18 ulp (~1.1e-6 relative), well inside rtol 1e-5.  For kernels whose
+// time goes to the exponentials rather than to HBM.
+__device__ __forceinline__ float shifted_exp_fast(float x, float m) {
+  return (x == -INFINITY || m == -INFINITY) ? 0.0f : __expf(x - m);
+}
+
 // ---------------------------------------------------------------------------
 // Merge-path partition of a CSR segment list.
 //

@@ -4,80 +4,124 @@
 //   W_k = - sum_{src(e)=k} g_e (x) v_e          (row-major 3x3)
 //
 // Contract and fp64 accumulation follow the reference's
-// csrc/force_assembly.cpp:64-96.  The whole working set (grad_edge, edge_vec,
-// src_order: ~73 MB at 2.2 M edges) is small, so the kernel is bound by
-// memory latency rather than bandwidth; it maximises loads in flight: eight
-// lanes cooperate on one atom (four atoms per warp), each lane taking every
-// eighth edge of both CSR lists and issuing its loads in bursts, and the
-// twelve fp64 sums are folded with a 3-step butterfly inside the 8-lane
-// group.  The summation order is fixed, so repeated runs are bit-identical.
+// csrc/force_assembly.cpp:64-96 (products double(g) * v, summed in double).
+//
+// The working set (grad_edge, edge_vec, src_order: ~73 MB at 2.2 M edges) is
+// small and the source side is a gather: the rows g_e, v_e of the edges
+// leaving atom k lie in ~90 different destination segments, each in its own
+// cache line.  What limits the kernel is therefore the number of L1 requests
+// per gathered row and the number of dependent round trips per atom, not
+// DRAM bandwidth.  Layout: one warp per atom, lanes 3T + r form ten
+// "triplets" T = 0..9 with component r = 0..2, lanes 30-31 idle.  A triplet
+// takes every tenth edge; its three lanes load the three components of the
+// same 12-byte row with one warp instruction (one request per row and array),
+// exchange the edge vector's components by shuffle, and each lane accumulates
+// its row r of the virial (g_r v_c, c = 0..2) and force component r in fp64.
+// All K source slots, their gathers and K destination rows of a lane are
+// issued as one burst, so a typical atom (<= 10 K edges per side) costs three
+// dependent round trips: offsets, src_order, rows.  The ten triplets' sums
+// are folded through shared memory in triplet order, so repeated runs are
+// bit-identical.
 #include "launch.cuh"
 
 namespace bysj {
 namespace {
 
+constexpr int kTriplets = 10;          // lanes 0..29 in use
+constexpr int kSlotsPerLane = 6;       // K: edges per triplet per burst (even)
+constexpr int kForceMinBlocks = 4;
+constexpr int kChunk = kTriplets * kSlotsPerLane;
+
+// Lanes per atom and atoms per warp of the destination-add kernel below.
 constexpr int kLanesPerAtom = 8;
 constexpr int kAtomsPerWarp = kWarp / kLanesPerAtom;
 
 enum Mode : int { kAssemble = 0, kSrcPartial = 1 };
 
-// Loads of one lane are issued in bursts so that an atom costs a handful of
-// dependent memory round trips, not one per edge: up to kSlots source slots
-// (src_order) are fetched at once, then their grad/vec rows in batches of
-// kBatch, and the destination rows in batches of kBatch while those are in
-// flight.
-constexpr int kSlots = 12;
-constexpr int kBatch = 6;
+// Edge bounds of one atom on both sides.
+template <typename I>
+struct AtomSpan {
+  I s0 = 0, s1 = 0, d0 = 0, d1 = 0;
+};
 
-// Row e of an [E, 3] float array with two loads: the 8-byte-aligned pair
-// (components 0-1 for even e, 1-2 for odd e) and the remaining single.
-// Needs an 8-byte-aligned base; PAIR = false falls back to three loads.
-template <bool PAIR>
-__device__ __forceinline__ void load_row3(const float* __restrict__ base, int64_t e,
-                                          float (&v)[3]) {
-  const float* p = base + 3 * e;
-  if constexpr (PAIR) {
-    const bool odd = (e & 1) != 0;
-    const float2 pair = __ldg(reinterpret_cast<const float2*>(p + (odd ? 1 : 0)));
-    const float single = __ldg(p + (odd ? 0 : 2));
-    v[0] = odd ? single : pair.x;
-    v[1] = odd ? pair.x : pair.y;
-    v[2] = odd ? pair.y : single;
-  } else {
-    v[0] = __ldg(p);
-    v[1] = __ldg(p + 1);
-    v[2] = __ldg(p + 2);
+template <int MODE, typename I>
+__device__ __forceinline__ AtomSpan<I> atom_span(const int64_t* __restrict__ dst_offsets,
+                                                 const int64_t* __restrict__ src_offsets,
+                                                 int64_t atom, int64_t n_nodes) {
+  AtomSpan<I> a;
+  if (atom < n_nodes) {
+    a.s0 = static_cast<I>(__ldg(src_offsets + atom));
+    a.s1 = static_cast<I>(__ldg(src_offsets + atom + 1));
+    if constexpr (MODE == kAssemble) {
+      a.d0 = static_cast<I>(__ldg(dst_offsets + atom));
+      a.d1 = static_cast<I>(__ldg(dst_offsets + atom + 1));
+    }
+  }
+  return a;
+}
+
+// Accumulates slots [base, base + 10 K) of both sides of one atom: triplet T
+// takes slots base + T + 10 k, k < K.
+template <int MODE, typename I, int K>
+__device__ __forceinline__ void force_chunk(const float* __restrict__ grad_edge,
+                                            const float* __restrict__ edge_vec,
+                                            const int64_t* __restrict__ src_order,
+                                            const AtomSpan<I>& cur, I base, bool active,
+                                            int T, int r, int src_lane, double& af,
+                                            double& aw0, double& aw1, double& aw2) {
+  const I ns = cur.s1 - cur.s0;
+  const I nd = cur.d1 - cur.d0;
+  const I first = base + T;
+  I edge[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const I j = first + k * kTriplets;
+    edge[k] = (active && j < ns) ? static_cast<I>(__ldg(src_order + (cur.s0 + j))) : I(-1);
+  }
+  float dg[K];
+  if constexpr (MODE == kAssemble) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const I j = first + k * kTriplets;
+      dg[k] = (active && j < nd) ? __ldg(grad_edge + (3 * (cur.d0 + j) + r)) : 0.0f;
+    }
+  }
+  float gr[K], vr[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    gr[k] = 0.0f;
+    vr[k] = 0.0f;
+    if (edge[k] >= 0) {
+      const I at = 3 * edge[k] + r;
+      gr[k] = __ldg(grad_edge + at);
+      vr[k] = __ldg(edge_vec + at);
+    }
+  }
+  if constexpr (MODE == kAssemble) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) af += static_cast<double>(dg[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float v0 = __shfl_sync(kFull, vr[k], src_lane);
+    const float v1 = __shfl_sync(kFull, vr[k], src_lane + 1);
+    const float v2 = __shfl_sync(kFull, vr[k], src_lane + 2);
+    if (edge[k] >= 0) {
+      const double g = static_cast<double>(gr[k]);
+      af -= g;
+      aw0 -= g * static_cast<double>(v0);
+      aw1 -= g * static_cast<double>(v1);
+      aw2 -= g * static_cast<double>(v2);
+    }
   }
 }
 
-template <bool PAIR>
-__device__ __forceinline__ void add_src_rows(const float* __restrict__ grad_edge,
-                                             const float* __restrict__ edge_vec,
-                                             const int64_t (&edge)[kBatch], int count,
-                                             double (&acc)[12]) {
-  float g[kBatch][3], v[kBatch][3];
-#pragma unroll
-  for (int b = 0; b < kBatch; ++b) {
-    if (b < count) {
-      load_row3<PAIR>(grad_edge, edge[b], g[b]);
-      load_row3<PAIR>(edge_vec, edge[b], v[b]);
-    }
-  }
-#pragma unroll
-  for (int b = 0; b < kBatch; ++b) {
-    if (b < count) {
-#pragma unroll
-      for (int r = 0; r < 3; ++r) {
-        acc[r] -= g[b][r];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) acc[3 + r * 3 + c] -= static_cast<double>(g[b][r]) * v[b][c];
-      }
-    }
-  }
-}
-
-template <int MODE, bool PAIR>
-__global__ void __launch_bounds__(kBlock, 2)
+// I: index type of edge arithmetic -- int32_t when 3 * n_edges fits, else
+// int64_t (the host picks).  The next atom's offsets are loaded while the
+// current atom's rows are in flight.  Chunks of 60, 30 or 10 slots per side
+// are picked by what is left, so a ~90-edge atom runs 60 + 30.
+template <int MODE, typename I>
+__global__ void __launch_bounds__(kBlock, kForceMinBlocks)
     force_assembly_kernel(const float* __restrict__ grad_edge,
                           const float* __restrict__ edge_vec,
                           const int64_t* __restrict__ dst_offsets,
@@ -86,102 +130,65 @@ __global__ void __launch_bounds__(kBlock, 2)
                           int64_t n_nodes, float* __restrict__ force,
                           float* __restrict__ virial,
                           float* __restrict__ partial) {
+  __shared__ double fold[kWarpsPerBlock][kTriplets * 12];
   const int lane = lane_id();
-  const int sub = lane & (kLanesPerAtom - 1);
-  const int64_t stride =
-      static_cast<int64_t>(gridDim.x) * kWarpsPerBlock * kAtomsPerWarp;
-  for (int64_t base = global_warp() * kAtomsPerWarp; base < n_nodes;
-       base += stride) {
-    const int64_t atom = base + (lane / kLanesPerAtom);
-    const bool valid = atom < n_nodes;
-    double acc[12];
-#pragma unroll
-    for (int c = 0; c < 12; ++c) acc[c] = 0.0;
-    if (valid) {
-      int64_t d0 = 0, d1 = 0;
-      if constexpr (MODE == kAssemble) {
-        d0 = __ldg(dst_offsets + atom) + sub;
-        d1 = __ldg(dst_offsets + atom + 1);
-      }
-      const int64_t s1 = __ldg(src_offsets + atom + 1);
-      for (int64_t s = __ldg(src_offsets + atom) + sub; s < s1;
-           s += static_cast<int64_t>(kSlots) * kLanesPerAtom) {
-        // Burst 1: this lane's next kSlots source slots.
-        int64_t edge[kSlots];
-        int count = 0;
-#pragma unroll
-        for (int t = 0; t < kSlots; ++t) {
-          const int64_t slot = s + static_cast<int64_t>(t) * kLanesPerAtom;
-          if (slot < s1) {
-            edge[t] = __ldg(src_order + slot);
-            count = t + 1;
-          }
-        }
-        // Destination rows of this round (contiguous), issued before the
-        // gathers are consumed.
-        float dg[kBatch][3];
-        int dcount = 0;
-        if constexpr (MODE == kAssemble) {
-#pragma unroll
-          for (int b = 0; b < kBatch; ++b) {
-            const int64_t e = d0 + static_cast<int64_t>(b) * kLanesPerAtom;
-            if (e < d1) {
-              load_row3<PAIR>(grad_edge, e, dg[b]);
-              dcount = b + 1;
-            }
-          }
-          d0 += static_cast<int64_t>(kBatch) * kLanesPerAtom;
-        }
-        // Bursts 2 and 3: the gathered rows, kBatch slots at a time.
-#pragma unroll
-        for (int h = 0; h < kSlots / kBatch; ++h) {
-          int64_t part[kBatch];
-#pragma unroll
-          for (int b = 0; b < kBatch; ++b) part[b] = edge[h * kBatch + b];
-          const int c = count - h * kBatch;
-          if (c > 0) add_src_rows<PAIR>(grad_edge, edge_vec, part, c < kBatch ? c : kBatch, acc);
-        }
-        if constexpr (MODE == kAssemble) {
-#pragma unroll
-          for (int b = 0; b < kBatch; ++b)
-            if (b < dcount) {
-              acc[0] += dg[b][0];
-              acc[1] += dg[b][1];
-              acc[2] += dg[b][2];
-            }
-        }
-      }
-      // Destination rows left over when an atom has more targets than sources.
-      if constexpr (MODE == kAssemble) {
-        for (; d0 < d1; d0 += kLanesPerAtom) {
-          float row[3];
-          load_row3<PAIR>(grad_edge, d0, row);
-          acc[0] += row[0];
-          acc[1] += row[1];
-          acc[2] += row[2];
-        }
+  const int T = lane / 3;
+  const int r = lane - 3 * T;
+  const bool active = T < kTriplets;
+  const int src_lane = 3 * (active ? T : 0);
+  double* mine = fold[threadIdx.x >> 5];
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
+  int64_t atom = global_warp();
+  AtomSpan<I> cur = atom_span<MODE, I>(dst_offsets, src_offsets, atom, n_nodes);
+  for (; atom < n_nodes; atom += warps) {
+    const AtomSpan<I> next = atom_span<MODE, I>(dst_offsets, src_offsets, atom + warps, n_nodes);
+    double af = 0.0, aw0 = 0.0, aw1 = 0.0, aw2 = 0.0;
+    const I ns = cur.s1 - cur.s0;
+    const I nd = cur.d1 - cur.d0;
+    const I span = ns > nd ? ns : nd;
+    for (I base = 0; base < span;) {  // warp-uniform
+      const I left = span - base;
+      if (left > kChunk / 2) {
+        force_chunk<MODE, I, kSlotsPerLane>(grad_edge, edge_vec, src_order, cur, base, active, T,
+                                            r, src_lane, af, aw0, aw1, aw2);
+        base += kChunk;
+      } else if (left > kTriplets) {
+        force_chunk<MODE, I, kSlotsPerLane / 2>(grad_edge, edge_vec, src_order, cur, base, active,
+                                                T, r, src_lane, af, aw0, aw1, aw2);
+        base += kChunk / 2;
+      } else {
+        force_chunk<MODE, I, 1>(grad_edge, edge_vec, src_order, cur, base, active, T, r,
+                                src_lane, af, aw0, aw1, aw2);
+        base += kTriplets;
       }
     }
-#pragma unroll
-    for (int c = 0; c < 12; ++c) acc[c] = group_sum(acc[c], kLanesPerAtom);
-    if (!valid) continue;
-    // Lane `sub` stores component sub, and sub + 8 when that exists.
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int c = sub + half * kLanesPerAtom;
-      if (c >= 12) break;
+    // Fold the ten triplets: column j of the 12-vector is summed by lane j
+    // in triplet order.
+    if (active) {
+      mine[T * 12 + r] = af;
+      mine[T * 12 + 3 + 3 * r] = aw0;
+      mine[T * 12 + 4 + 3 * r] = aw1;
+      mine[T * 12 + 5 + 3 * r] = aw2;
+    }
+    __syncwarp();
+    if (lane < 12) {
       double v = 0.0;
 #pragma unroll
-      for (int t = 0; t < 12; ++t) v = (t == c) ? acc[t] : v;
+      for (int t = 0; t < kTriplets; ++t) v += mine[t * 12 + lane];
       if constexpr (MODE == kAssemble) {
-        if (c < 3) force[atom * 3 + c] = static_cast<float>(v);
-        else if (virial) virial[atom * 9 + (c - 3)] = static_cast<float>(v);
+        if (lane < 3) force[atom * 3 + lane] = static_cast<float>(v);
+        else if (virial) virial[atom * 9 + (lane - 3)] = static_cast<float>(v);
       } else {
-        partial[atom * 12 + c] = static_cast<float>(v);
+        partial[atom * 12 + lane] = static_cast<float>(v);
       }
     }
+    __syncwarp();
+    cur = next;
   }
 }
+
+// 32-bit edge arithmetic is exact when 3 * n_edges + 3 < 2^31.
+bool force_index32(int64_t n_edges) { return n_edges < (int64_t{1} << 31) / 3 - 1; }
 
 // force[k] = sum_{dst(e)=k} g_e + summed[k, 0:3];  virial[k] = summed[k, 3:12]
 __global__ void __launch_bounds__(kBlock)
@@ -231,6 +238,16 @@ unsigned atom_blocks(int64_t n_nodes) {
   return static_cast<unsigned>(blocks);
 }
 
+// One warp per atom, at most one wave of resident warps (grid-stride beyond).
+unsigned warp_per_atom_blocks(int64_t n_nodes) {
+  int64_t blocks = (n_nodes + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const int64_t cap =
+      static_cast<int64_t>(current_device_info().sm_count) * kForceMinBlocks;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<unsigned>(blocks);
+}
+
 }  // namespace
 }  // namespace bysj
 
@@ -252,14 +269,14 @@ int bysj_force_assembly(const float* grad_edge, const float* edge_vec,
                        src_order == nullptr)))
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "force assembly: NULL pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (aligned8(grad_edge) && aligned8(edge_vec))
-    force_assembly_kernel<kAssemble, true><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
-        grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force,
-        virial, nullptr);
+  if (force_index32(n_edges))
+    force_assembly_kernel<kAssemble, int32_t><<<warp_per_atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force, virial,
+        nullptr);
   else
-    force_assembly_kernel<kAssemble, false><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
-        grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force,
-        virial, nullptr);
+    force_assembly_kernel<kAssemble, int64_t><<<warp_per_atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, dst_offsets, src_offsets, src_order, n_nodes, force, virial,
+        nullptr);
   return launch_check("force_assembly_kernel");
 }
 
@@ -278,14 +295,14 @@ int bysj_force_assembly_src_partial(const float* grad_edge,
                        src_order == nullptr)))
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "force partial: NULL pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (aligned8(grad_edge) && aligned8(edge_vec))
-    force_assembly_kernel<kSrcPartial, true><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
-        grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr,
-        nullptr, partial);
+  if (force_index32(n_edges))
+    force_assembly_kernel<kSrcPartial, int32_t><<<warp_per_atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr, nullptr,
+        partial);
   else
-    force_assembly_kernel<kSrcPartial, false><<<atom_blocks(n_nodes), kBlock, 0, s>>>(
-        grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr,
-        nullptr, partial);
+    force_assembly_kernel<kSrcPartial, int64_t><<<warp_per_atom_blocks(n_nodes), kBlock, 0, s>>>(
+        grad_edge, edge_vec, nullptr, src_offsets, src_order, n_nodes, nullptr, nullptr,
+        partial);
   return launch_check("force_assembly_kernel<src partial>");
 }
 

@@ -215,8 +215,7 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_fwd_split_kernel(SmxAr
 template <int LP>
 struct QuadSmx {
   static constexpr int G = kWarp / LP;
-  static constexpr int T =
-      LP >= 16 ? 8 : ((128 / G) < 8 ? 8 : ((128 / G) > 16 ? 16 : (128 / G)));
+  static constexpr int T = 8;
   static constexpr int CHUNK = G * T;
 };
 
@@ -228,55 +227,102 @@ __device__ __forceinline__ void quad_set(float4& v, int i, float x) {
   if (i == 0) v.x = x; else if (i == 1) v.y = x; else if (i == 2) v.z = x; else v.w = x;
 }
 
-// Loads the gated logits of slots base + g + t*G (t < T) into x (-inf past
-// `hi` and for masked edges).
+// Rows of slots base + g + t*G (t < T) that lie below `hi`.
 template <int LP>
+__device__ __forceinline__ int quad_rows(int64_t base, int64_t hi, int g) {
+  using Q = QuadSmx<LP>;
+  const int64_t left = hi - base - g;
+  if (left <= 0) return 0;
+  const int64_t r = (left + Q::G - 1) / Q::G;
+  return r < Q::T ? static_cast<int>(r) : Q::T;
+}
+
+// Loads the gated logits of slots base + g + t*G (t < T) into x (-inf past
+// `hi` and for masked edges).  The envelope shift 2 ln env of a row is
+// computed once, by lane (t mod LP) of the row's group, and shuffled to the
+// other LP - 1 lanes of that row.
+template <int LP, bool kEnv>
 __device__ __forceinline__ void quad_load(const SmxArgs& a, int64_t base, int64_t hi, int g,
                                           int q, bool qok, float4 (&x)[QuadSmx<LP>::T]) {
   using Q = QuadSmx<LP>;
-  const int64_t C = a.channels;
+  constexpr int kOwn = (Q::T + LP - 1) / LP;  // rows whose envelope this lane takes
+  const int64_t cq = a.channels / 4;
+  const int64_t first = base + g;
+  const int rows = quad_rows<LP>(base, hi, g);
+  float sh[kOwn];
+  if constexpr (kEnv) {
+#pragma unroll
+    for (int j = 0; j < kOwn; ++j) {
+      const int t = q + j * LP;
+      float v = -INFINITY;
+      if (t < rows) {
+        const int64_t s = first + static_cast<int64_t>(t) * Q::G;
+        const float env = __ldg(a.env + (a.order ? __ldg(a.order + s) : s));
+        if (env > 0.0f) v = 2.0f * __logf(env);
+      }
+      sh[j] = v;
+    }
+  }
+  const int mine = qok ? rows : 0;
+  const float4* row = reinterpret_cast<const float4*>(a.x) + q;
 #pragma unroll
   for (int t = 0; t < Q::T; ++t) {
-    const int64_t s = base + g + static_cast<int64_t>(t) * Q::G;
-    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    if (qok && s < hi) {
-      const int64_t e = a.order ? __ldg(a.order + s) : s;
-      v = __ldg(reinterpret_cast<const float4*>(a.x + e * C) + q);
-      if (a.env) {
-        const float env = __ldg(a.env + e);
-        if (env > 0.0f) {
-          const float shift = 2.0f * logf(env);
-          v.x += shift; v.y += shift; v.z += shift; v.w += shift;
-        } else {
-          v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        }
+    float shift = 0.0f;
+    if constexpr (kEnv) {
+      if constexpr (LP == 1) {
+        shift = sh[t];
+      } else {
+        shift = __shfl_sync(kFull, sh[t / LP], g * LP + (t % LP));
       }
+    }
+    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (t < mine) {
+      const int64_t slot = first + static_cast<int64_t>(t) * Q::G;
+      const float4 raw = __ldg(row + (a.order ? __ldg(a.order + slot) : slot) * cq);
+      if (!kEnv || shift != -INFINITY)
+        v = make_float4(raw.x + shift, raw.y + shift, raw.z + shift, raw.w + shift);
     }
     x[t] = v;
   }
 }
 
+// Stores x[t] as the out row of slot base + g + t*G for the rows below `hi`.
 template <int LP>
-__device__ __forceinline__ void quad_write(const SmxArgs& a, int64_t base, int64_t hi, int g,
-                                           int q, bool qok, const float4 (&x)[QuadSmx<LP>::T],
-                                           const float (&m)[4], const float (&inv)[4]) {
+__device__ __forceinline__ void quad_store(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                           int q, bool qok, const float4 (&x)[QuadSmx<LP>::T]) {
   using Q = QuadSmx<LP>;
-  if (!qok) return;
-  const int64_t C = a.channels;
+  const int mine = qok ? quad_rows<LP>(base, hi, g) : 0;
+  const int64_t cq = a.channels / 4;
+  const int64_t first = base + g;
+  float4* row = reinterpret_cast<float4*>(a.out) + q;
 #pragma unroll
   for (int t = 0; t < Q::T; ++t) {
-    const int64_t s = base + g + static_cast<int64_t>(t) * Q::G;
-    if (s >= hi) break;
-    const int64_t e = a.order ? __ldg(a.order + s) : s;
-    float4 o;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) quad_set(o, i, shifted_exp(quad_get(x[t], i), m[i]) * inv[i]);
-    reinterpret_cast<float4*>(a.out + e * C)[q] = o;
+    if (t >= mine) break;
+    const int64_t slot = first + static_cast<int64_t>(t) * Q::G;
+    row[(a.order ? __ldg(a.order + slot) : slot) * cq] = x[t];
   }
 }
 
-template <int LP, bool kSplitPass>
-__global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a) {
+// x[t] <- exp(x[t] - m) * inv, per channel of the quad.
+template <int LP>
+__device__ __forceinline__ void quad_weights(float4 (&x)[QuadSmx<LP>::T], const float (&m)[4],
+                                             const float (&inv)[4]) {
+#pragma unroll
+  for (int t = 0; t < QuadSmx<LP>::T; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) quad_set(x[t], i, shifted_exp_fast(quad_get(x[t], i), m[i]) * inv[i]);
+}
+
+template <int LP>
+__device__ __forceinline__ void quad_write(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                           int q, bool qok, float4 (&x)[QuadSmx<LP>::T],
+                                           const float (&m)[4], const float (&inv)[4]) {
+  quad_weights<LP>(x, m, inv);
+  quad_store<LP>(a, base, hi, g, q, qok, x);
+}
+
+template <int LP, bool kSplitPass, bool kEnv>
+__global__ void __launch_bounds__(kBlock, 3) segment_softmax_quad_kernel(SmxArgs a) {
   using Q = QuadSmx<LP>;
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
@@ -303,8 +349,9 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
         m[i] = qok ? __ldcg(fin + 4 * q + i) : 0.0f;
         inv[i] = qok ? __ldcg(fin + a.cpad + 4 * q + i) : 0.0f;
       }
+      #pragma unroll 1
       for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
-        quad_load<LP>(a, base, cur.hi, g, q, qok, x);
+        quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
         quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
       }
       continue;
@@ -319,7 +366,7 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
       if (one_chunk) {
         // Exact two-step form: maximum first, then each exponential once;
         // x keeps exp(l - m) for the write.
-        quad_load<LP>(a, cur.lo, cur.hi, g, q, qok, x);
+        quad_load<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, x);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           float cm = -INFINITY;
@@ -327,10 +374,13 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
           for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
           for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
           m[i] = fmaxf(cm, nl[i]);
+          // With m = -inf every row is -inf too; shifting by 0 keeps
+          // exp(-inf) = 0 and avoids -inf - -inf.
+          const float ms = m[i] == -INFINITY ? 0.0f : m[i];
           float acc = 0.0f;
 #pragma unroll
           for (int t = 0; t < Q::T; ++t) {
-            const float w = shifted_exp(quad_get(x[t], i), m[i]);
+            const float w = __expf(quad_get(x[t], i) - ms);
             quad_set(x[t], i, w);
             acc += w;
           }
@@ -340,8 +390,9 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
       } else {
 #pragma unroll
         for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
+        #pragma unroll 1
         for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
-          quad_load<LP>(a, base, cur.hi, g, q, qok, x);
+          quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             float cm = -INFINITY;
@@ -350,7 +401,7 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
             const float mn = fmaxf(m[i], cm);
             float acc = d[i] * shifted_exp(m[i], mn);
 #pragma unroll
-            for (int t = 0; t < Q::T; ++t) acc += shifted_exp(quad_get(x[t], i), mn);
+            for (int t = 0; t < Q::T; ++t) acc += shifted_exp_fast(quad_get(x[t], i), mn);
             d[i] = acc;
             m[i] = mn;
           }
@@ -384,19 +435,14 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
               make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
         }
         if (one_chunk) {
-          if (qok) {
 #pragma unroll
-            for (int t = 0; t < Q::T; ++t) {
-              const int64_t sl = cur.lo + g + static_cast<int64_t>(t) * Q::G;
-              if (sl >= cur.hi) break;
-              const int64_t e = a.order ? __ldg(a.order + sl) : sl;
-              reinterpret_cast<float4*>(a.out + e * C)[q] =
-                  make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
-            }
-          }
+          for (int t = 0; t < Q::T; ++t)
+            x[t] = make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+          quad_store<LP>(a, cur.lo, cur.hi, g, q, qok, x);
         } else {
+          #pragma unroll 1
           for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
-            quad_load<LP>(a, base, cur.hi, g, q, qok, x);
+            quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
             quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
           }
         }
@@ -446,8 +492,9 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_quad_kernel(SmxArgs a)
       const int64_t seg_lo = __ldg(a.mp.offsets + n);
       const int64_t seg_hi = __ldg(a.mp.offsets + n + 1);
       if (seg_hi - seg_lo <= kSelfWrite) {
+        #pragma unroll 1
         for (int64_t base = seg_lo; base < seg_hi; base += Q::CHUNK) {
-          quad_load<LP>(a, base, seg_hi, g, q, qok, x);
+          quad_load<LP, kEnv>(a, base, seg_hi, g, q, qok, x);
           quad_write<LP>(a, base, seg_hi, g, q, qok, x, m, inv);
         }
       } else if (lane == 0) {
@@ -639,26 +686,31 @@ SmxConfig smx_make(bool backward) {
   return c;
 }
 
-template <int LP>
-SmxConfig quad_make() {
+template <int LP, bool kEnv>
+SmxConfig quad_make_env() {
   SmxConfig c;
-  c.main = segment_softmax_quad_kernel<LP, false>;
-  c.split = segment_softmax_quad_kernel<LP, true>;
+  c.main = segment_softmax_quad_kernel<LP, false, kEnv>;
+  c.split = segment_softmax_quad_kernel<LP, true, kEnv>;
   c.tc = 4 * LP;
   c.tiles = 1;
   return c;
 }
 
-SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok) {
+template <int LP>
+SmxConfig quad_make(bool env) {
+  return env ? quad_make_env<LP, true>() : quad_make_env<LP, false>();
+}
+
+SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = true) {
   SmxConfig c;
   if (!backward && quad_ok && channels % 4 == 0 && channels <= 128) {
     switch (next_pow2(channels / 4)) {
-      case 1: return quad_make<1>();
-      case 2: return quad_make<2>();
-      case 4: return quad_make<4>();
-      case 8: return quad_make<8>();
-      case 16: return quad_make<16>();
-      default: return quad_make<32>();
+      case 1: return quad_make<1>(env);
+      case 2: return quad_make<2>(env);
+      case 4: return quad_make<4>(env);
+      case 8: return quad_make<8>(env);
+      case 16: return quad_make<16>(env);
+      default: return quad_make<32>(env);
     }
   }
   if (channels > 128) c = smx_make<8, 1>(backward);
@@ -688,9 +740,9 @@ struct SmxLayout {
 };
 
 SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
-                     bool backward, void* ws, bool quad_ok = true) {
+                     bool backward, void* ws, bool quad_ok = true, bool env = true) {
   SmxLayout L;
-  L.cfg = smx_config(channels, backward, quad_ok);
+  L.cfg = smx_config(channels, backward, quad_ok, env);
   const DeviceInfo& dev = current_device_info();
   const int64_t resident =
       static_cast<int64_t>(dev.sm_count) *
@@ -748,10 +800,14 @@ extern "C" {
 size_t bysj_segment_softmax_workspace_size(int64_t n_edges, int64_t n_nodes,
                                            int64_t channels) {
   if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
-  // Pointer alignment picks the quad-vector or the scalar kernel; size for both.
-  const size_t a = smx_layout(n_edges, n_nodes, channels, false, nullptr, true).bytes;
-  const size_t b = smx_layout(n_edges, n_nodes, channels, false, nullptr, false).bytes;
-  return a > b ? a : b;
+  // Pointer alignment and `env` pick the kernel (and with it the partition
+  // count); size for every choice.
+  size_t need = smx_layout(n_edges, n_nodes, channels, false, nullptr, false).bytes;
+  for (int env = 0; env < 2; ++env) {
+    const size_t b = smx_layout(n_edges, n_nodes, channels, false, nullptr, true, env).bytes;
+    if (b > need) need = b;
+  }
+  return need;
 }
 
 int bysj_segment_softmax_forward(const float* logit, const float* env,
@@ -773,7 +829,8 @@ int bysj_segment_softmax_forward(const float* logit, const float* env,
   const bool quad_ok = aligned16(logit) && aligned16(alpha) &&
                        (null_logit == nullptr || aligned16(null_logit)) &&
                        (null_alpha == nullptr || aligned16(null_alpha));
-  SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace, quad_ok);
+  SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace, quad_ok,
+                           env != nullptr);
   if (workspace == nullptr || workspace_bytes < L.bytes)
     return fail(BYSJ_ERR_WORKSPACE,
                 "segment softmax: workspace of %zu bytes needed, %zu given",

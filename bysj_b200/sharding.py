@@ -147,6 +147,8 @@ def reduce_scatter_sum(padded: torch.Tensor, part: DstPartition, group=None,
     """
     import torch.distributed as dist
 
+    if part.world == 1:  # one partition: nothing to exchange
+        return padded[:part.chunk], None
     block = padded.new_empty((part.chunk, padded.shape[1]))
     if dist.get_backend(group) == "nccl":
         work = dist.reduce_scatter_tensor(block, padded, op=dist.ReduceOp.SUM, group=group,

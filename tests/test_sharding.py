@@ -170,3 +170,18 @@ def test_partitioned_force_with_gloo_ranks(tmp_path, world):
                                   g.dst.numpy(), g.n_atoms)
     np.testing.assert_allclose(force.numpy(), tf, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(virial.numpy(), tv, rtol=1e-5, atol=1e-5)
+
+
+def test_single_partition_needs_no_process_group():
+    g = W.c1_box()
+    off = offsets_of(g.dst, g.n_atoms)
+    p = S.make_partition(off, g.src, 0, 1, group_by_source=cpu_group_by_source)
+    gen = torch.Generator().manual_seed(5)
+    grad = torch.randn(g.n_edges, 3, generator=gen)
+    assert not dist.is_initialized()
+    f, v = S.force_assembly_partitioned(grad, g.edge_vec, p, src_partial=cpu_src_partial,
+                                        dst_add=cpu_dst_add)
+    tf, tv = truth.force_assembly(grad.numpy(), g.edge_vec.numpy(), g.src.numpy(),
+                                  g.dst.numpy(), g.n_atoms)
+    np.testing.assert_allclose(f.numpy(), tf, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(v.numpy(), tv, rtol=1e-5, atol=1e-5)
