@@ -319,6 +319,18 @@ def _op_offsets(ctx):
                    {"note": "2 launches (check + boundary), L2 flushed"})
 
 
+def _op_group(ctx):
+    from bysj_b200 import _C
+
+    g, n, e = ctx["g"], ctx["g"].n_atoms, ctx["g"].n_edges
+    t = time_launches(lambda: _C.group_by_key(g.src, n), ctx["iters"], ctx["flush"])
+    t_sort = time_launches(lambda: torch.argsort(g.src, stable=True), ctx["iters"], ctx["flush"])
+    return op_line("group_by_source", 8 * e + 8 * e + 8 * (n + 1), t, ctx["peak"], e,
+                   {"note": "histogram, scan, scatter, per-group sort; includes the flag "
+                            "read back; L2 flushed",
+                    "torch_argsort_stable_us": t_sort * 1e6})
+
+
 def _op_attention_bf16(ctx):
     from bysj_b200 import _C
 
@@ -415,6 +427,7 @@ def _op_rmsnorm(ctx, dtype):
 
 OPS = {
     "offsets": _op_offsets,
+    "group": _op_group,
     "attention_bf16": _op_attention_bf16,
     "softmax": _op_softmax,
     "segment_sum": _op_segment_sum,

@@ -46,6 +46,7 @@ NVCC_FLAGS = [
 CU_SOURCES = [
     "runtime.cu",
     "offsets.cu",
+    "group.cu",
     "segment_sum.cu",
     "segment_softmax.cu",
     "segment_attention.cu",

@@ -115,6 +115,26 @@ Tensor segment_offsets_device(Tensor dst, int64_t n_nodes, Tensor flags) {
   return offsets;
 }
 
+// Stable grouping of edges by key on the device: (order, offsets, flags word).
+// The flags word is read back (one synchronisation), as the reference's
+// range check does.
+std::tuple<Tensor, Tensor, int64_t> group_by_key(Tensor keys, int64_t n_keys) {
+  i64(keys, "keys");
+  TORCH_CHECK(n_keys >= 0, "n_keys must be non-negative");
+  c10::cuda::CUDAGuard guard(keys.device());
+  const int64_t edges = keys.numel();
+  Tensor order = torch::empty({edges}, keys.options());
+  Tensor offsets = torch::empty({n_keys + 1}, keys.options());
+  Tensor flags = torch::zeros({1}, keys.options().dtype(torch::kInt32));
+  Tensor ws = workspace(keys, bysj_group_by_key_workspace_size(edges, n_keys));
+  check(bysj_group_by_key(keys.data_ptr<int64_t>(), edges, n_keys, order.data_ptr<int64_t>(),
+                          offsets.data_ptr<int64_t>(),
+                          reinterpret_cast<uint32_t*>(flags.data_ptr<int32_t>()), ws.data_ptr(),
+                          static_cast<size_t>(ws.numel()), stream_of(keys)),
+        "group_by_key");
+  return {order, offsets, static_cast<int64_t>(flags.item<int32_t>())};
+}
+
 // CSR view (offsets, order) of an arbitrary-order dst, for operators whose
 // reference API takes only dst (GIE).  order is undefined for sorted input.
 std::tuple<Tensor, OptTensor> csr_view(const Tensor& dst, int64_t n_nodes) {
@@ -122,7 +142,10 @@ std::tuple<Tensor, OptTensor> csr_view(const Tensor& dst, int64_t n_nodes) {
   TORCH_CHECK(!(word & BYSJ_FLAG_OUT_OF_RANGE),
               "destination values must be within the node range");
   OptTensor order;
-  if (word & BYSJ_FLAG_UNSORTED) order = torch::argsort(dst, /*stable=*/true);
+  if (word & BYSJ_FLAG_UNSORTED) {
+    auto [grouped, grouped_offsets, gword] = group_by_key(dst, n_nodes);
+    order = grouped;
+  }
   return {offsets, order};
 }
 
@@ -587,5 +610,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("edge_vec"), py::arg("src_offsets"), py::arg("src_order"));
   m.def("force_assembly_dst_add", &force_assembly_dst_add, py::arg("grad_edge"),
         py::arg("dst_offsets"), py::arg("summed_partial"));
+  m.def("group_by_key", &group_by_key, py::arg("keys"), py::arg("n_keys"));
   m.def("library_version", []() { return bysj_version(); });
 }

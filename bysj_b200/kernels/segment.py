@@ -74,11 +74,10 @@ def group_by_source(src: torch.Tensor, n_nodes: int) -> tuple[torch.Tensor, torc
     if int(n_nodes) <= 0:
         raise ValueError("group_by_source requires a positive node count")
     require_dcu(src)
-    extension = _extension("segment_offsets")
-    offsets, flags = extension.segment_offsets(src.contiguous(), int(n_nodes))
+    extension = _extension("group_by_key")
+    order, offsets, flags = extension.group_by_key(src.contiguous(), int(n_nodes))
     if flags & _FLAG_OUT_OF_RANGE:
         raise ValueError("source values must be within the node range")
-    order = torch.argsort(src, stable=True)
     return order, offsets
 
 

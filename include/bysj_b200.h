@@ -91,6 +91,22 @@ BYSJ_API int bysj_segment_offsets_histogram(const int64_t* dst, int64_t n_edges,
                                    size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * group_by_key (group_by_source / CSR view of an unsorted dst)
+ * Replaces python/kernels/segment.py:60-71 (stable argsort of the keys plus
+ * bincount + cumsum) and the argsort in python/model/fused_deepmd.py:111-124.
+ *   offsets[k] = number of edges with key < k          (int64 [n_keys + 1])
+ *   order[offsets[k] .. offsets[k+1]) = the edges with key k, ascending
+ * keys: int64 [n_edges]; out-of-range keys are skipped and flagged with
+ * BYSJ_FLAG_OUT_OF_RANGE in *flags (device uint32 the caller zeroes); the
+ * outputs are then incomplete.  Bit-exact and run-to-run identical.
+ * n_keys must be below 2^31 - 1.
+ * ------------------------------------------------------------------------ */
+BYSJ_API size_t bysj_group_by_key_workspace_size(int64_t n_edges, int64_t n_keys);
+BYSJ_API int bysj_group_by_key(const int64_t* keys, int64_t n_edges, int64_t n_keys,
+                               int64_t* order, int64_t* offsets, uint32_t* flags,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * segment_sum
  * Replaces csrc/segment_sum.cpp:214-317 (segment_sum_forward_hip /
  * segment_sum_backward_hip).

@@ -86,6 +86,41 @@ def test_offsets_golden(cuda):
     np.testing.assert_array_equal(off.cpu().numpy(), g["src_offsets"])
 
 
+@pytest.mark.parametrize("case", ["small", "block", "scan", "mixed"])
+def test_group_by_source_every_sort_regime(cuda, case):
+    # groups of <= 256 edges (warp sort), 257..4096 (CTA sort), > 4096 (scan)
+    gen = torch.Generator().manual_seed(len(case))
+    n = {"small": 3000, "block": 40, "scan": 6, "mixed": 500}[case]
+    e = {"small": 200000, "block": 60000, "scan": 60000, "mixed": 120000}[case]
+    src = torch.randint(0, n, (e,), generator=gen)
+    if case == "mixed":  # one giant, a few medium, many small and some empty keys
+        src[: e // 3] = 7
+        src[e // 3: e // 2] = torch.randint(100, 110, (e // 2 - e // 3,), generator=gen)
+        src[src == 42] = 43
+        src = src[torch.randperm(e, generator=gen)]
+    order, off = K.group_by_source(src.cuda(), n)
+    want_order, want_off = truth.group_by_source(src.numpy(), n)
+    np.testing.assert_array_equal(off.cpu().numpy(), want_off)
+    np.testing.assert_array_equal(order.cpu().numpy(), want_order)
+    again, _ = K.group_by_source(src.cuda(), n)
+    assert torch.equal(order, again)
+
+
+def test_group_by_source_edge_cases(cuda):
+    empty = torch.empty(0, dtype=torch.int64, device="cuda")
+    order, off = K.group_by_source(empty, 3)
+    assert order.numel() == 0 and off.tolist() == [0, 0, 0, 0]
+    order, off = K.group_by_source(torch.tensor([2, 0, 2, 1, 0], device="cuda"), 3)
+    assert order.tolist() == [1, 4, 3, 0, 2] and off.tolist() == [0, 2, 3, 5]
+    with pytest.raises(ValueError):
+        K.group_by_source(torch.tensor([0, 3], device="cuda"), 3)
+    with pytest.raises(ValueError):
+        K.group_by_source(torch.tensor([-1, 0], device="cuda"), 3)
+    one = torch.zeros(5000, dtype=torch.int64, device="cuda")
+    order, off = K.group_by_source(one, 1)
+    assert torch.equal(order.cpu(), torch.arange(5000)) and off.tolist() == [0, 5000]
+
+
 # ---- segment_sum -----------------------------------------------------------------
 
 @pytest.mark.parametrize("channels", [1, 3, 8, 17, 64, 640, 1024, 1500])
