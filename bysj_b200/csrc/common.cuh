@@ -324,12 +324,12 @@ enum SegKind : int { kWhole = 0, kHead = 1, kTail = 2 };
 //   SegCursor cur(mp, range);
 //   while (cur.next()) { ... cur.node, cur.lo, cur.hi, cur.kind ... }
 struct SegCursor {
-  const MergePath& mp;
+  const MergePath* mp;  // a pointer, so that a cursor can be copied and reassigned
   PartRange r;
   int64_t node, lo, hi, e;
   int kind;
   __device__ SegCursor(const MergePath& m, const PartRange& range)
-      : mp(m), r(range), node(range.a0 - 1), lo(0), hi(0), e(range.b0),
+      : mp(&m), r(range), node(range.a0 - 1), lo(0), hi(0), e(range.b0),
         kind(kWhole) {}
   __device__ __forceinline__ bool next() {
     ++node;
@@ -344,8 +344,8 @@ struct SegCursor {
       return true;
     }
     lo = e;
-    hi = __ldg(mp.offsets + node + 1);
-    kind = (__ldg(mp.offsets + node) >= r.b0) ? kWhole : kHead;
+    hi = __ldg(mp->offsets + node + 1);
+    kind = (__ldg(mp->offsets + node) >= r.b0) ? kWhole : kHead;
     e = hi;
     return true;
   }

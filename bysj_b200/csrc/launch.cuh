@@ -10,6 +10,9 @@ constexpr int kWarpsPerBlock = kBlock / kWarp;
 
 // Resident CTAs per SM for `kernel` at kBlock threads (cached per device).
 int resident_blocks(const void* kernel, size_t dynamic_smem = 0);
+// Raises the kernel's dynamic shared memory limit to `bytes` (needed above
+// 48 KB) once per kernel and device; BYSJ_OK or an error status.
+int allow_dynamic_smem(const void* kernel, size_t bytes);
 
 // Merge-path partitioning for a kernel whose warps each own one partition:
 // one wave of resident warps, but never fewer than `min_items` items each.

@@ -3,6 +3,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <unordered_map>
 
 #include "launch.cuh"
@@ -75,6 +77,21 @@ const DeviceInfo& current_device_info() {
     g_device_ready[device] = true;
   }
   return g_devices[device];
+}
+
+int allow_dynamic_smem(const void* kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return BYSJ_OK;
+  static std::mutex m;
+  static std::set<std::tuple<const void*, int, size_t>> done;
+  const DeviceInfo& info = current_device_info();
+  std::lock_guard<std::mutex> lock(m);
+  const auto key = std::make_tuple(kernel, info.device, bytes);
+  if (done.count(key)) return BYSJ_OK;
+  const int st = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(bytes)),
+                            "opt in to dynamic shared memory");
+  if (st == BYSJ_OK) done.insert(key);
+  return st;
 }
 
 int resident_blocks(const void* kernel, size_t dynamic_smem) {

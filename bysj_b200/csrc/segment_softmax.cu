@@ -321,186 +321,348 @@ __device__ __forceinline__ void quad_write(const SmxArgs& a, int64_t base, int64
   quad_store<LP>(a, base, hi, g, q, qok, x);
 }
 
-template <int LP, bool kSplitPass, bool kEnv>
-__global__ void __launch_bounds__(kBlock, 3) segment_softmax_quad_kernel(SmxArgs a) {
+// Asynchronous global -> shared copies (LDGSTS): 16 bytes of a logit row
+// quad, or one 4-byte envelope value.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Shared-memory staging of one chunk of a warp: lane (g, q) copies the quad
+// q of rows base + g + t*G into buf[32 t + lane] (the place it reads it from
+// later), and lane q == 0 of each group the row's envelope into
+// env[t G + g].  4 KB of rows + G*T floats of envelope per buffer.
+template <int LP>
+struct QuadStage {
+  static constexpr int kRowsF4 = QuadSmx<LP>::T * kWarp;
+  static constexpr int kEnvF = QuadSmx<LP>::CHUNK;
+  static constexpr size_t kBytes = sizeof(float4) * kRowsF4 + sizeof(float) * kEnvF;
+  static constexpr size_t kWarpBytes = 2 * kBytes;  // double buffer
+};
+
+template <int LP, bool kEnv>
+__device__ __forceinline__ void quad_stage(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                           int q, bool qok, float4* buf, float* env) {
   using Q = QuadSmx<LP>;
-  const int64_t p = global_warp();
-  if (p >= a.mp.parts) return;
-  const int lane = lane_id();
-  const int g = lane / LP;
-  const int q = lane % LP;
+  const int rows = quad_rows<LP>(base, hi, g);
   const int64_t C = a.channels;
-  const bool qok = 4 * q < C;
-  if constexpr (kSplitPass) {
-    if (*reinterpret_cast<volatile int*>(a.big_split) == 0) return;
+  const int lane = g * LP + q;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    if (t >= rows) break;
+    const int64_t slot = base + g + static_cast<int64_t>(t) * Q::G;
+    const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+    if (qok) cp_async16(buf + t * kWarp + lane, a.x + e * C + 4 * q);
+    if (kEnv && q == 0) cp_async4(env + t * Q::G + g, a.env + e);
   }
-  SegCursor cur(a.mp, part_range(a.mp, p));
-  while (cur.next()) {
-    const int64_t n = cur.node;
-    const bool whole = cur.kind == kWhole;
-    float4 x[Q::T];
-    float m[4], inv[4];
-    if constexpr (kSplitPass) {
-      if (whole) continue;
-      if (__ldg(a.mp.offsets + n + 1) - __ldg(a.mp.offsets + n) <= kSelfWrite) continue;
-      const float* fin = a.final_stats + a.mp.part_of_end(n) * 2 * a.cpad;
+}
+
+// quad_load from a staged chunk.
+template <int LP, bool kEnv>
+__device__ __forceinline__ void quad_load_smem(const float4* buf, const float* envs,
+                                               int64_t base, int64_t hi, int g, int q, bool qok,
+                                               float4 (&x)[QuadSmx<LP>::T]) {
+  using Q = QuadSmx<LP>;
+  constexpr int kOwn = (Q::T + LP - 1) / LP;
+  const int rows = quad_rows<LP>(base, hi, g);
+  const int lane = g * LP + q;
+  float sh[kOwn];
+  if constexpr (kEnv) {
+#pragma unroll
+    for (int j = 0; j < kOwn; ++j) {
+      const int t = q + j * LP;
+      float v = -INFINITY;
+      if (t < rows) {
+        const float env = envs[t * Q::G + g];
+        if (env > 0.0f) v = 2.0f * __logf(env);
+      }
+      sh[j] = v;
+    }
+  }
+  const int mine = qok ? rows : 0;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    float shift = 0.0f;
+    if constexpr (kEnv) {
+      if constexpr (LP == 1) {
+        shift = sh[t];
+      } else {
+        shift = __shfl_sync(kFull, sh[t / LP], g * LP + (t % LP));
+      }
+    }
+    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (t < mine) {
+      const float4 raw = buf[t * kWarp + lane];
+      if (!kEnv || shift != -INFINITY)
+        v = make_float4(raw.x + shift, raw.y + shift, raw.z + shift, raw.w + shift);
+    }
+    x[t] = v;
+  }
+}
+
+// The segment piece a cursor stands on.
+struct Piece {
+  int64_t node, lo, hi;
+  int kind;
+};
+__device__ __forceinline__ Piece piece_of(const SegCursor& c) {
+  return Piece{c.node, c.lo, c.hi, c.kind};
+}
+
+// One segment piece of the quad kernel (`staged`: its rows in shared memory,
+// or nullptr to read them from global memory).
+template <int LP, bool kSplitPass, bool kEnv>
+__device__ __forceinline__ void quad_segment(const SmxArgs& a, int64_t p, const Piece& cur,
+                                             int lane, int g, int q, bool qok,
+                                             const float4* staged, const float* staged_env) {
+  using Q = QuadSmx<LP>;
+  const int64_t C = a.channels;
+  const int64_t n = cur.node;
+  const bool whole = cur.kind == kWhole;
+  float4 x[Q::T];
+  float m[4], inv[4];
+  if constexpr (kSplitPass) {
+    if (whole) return;
+    if (__ldg(a.mp.offsets + n + 1) - __ldg(a.mp.offsets + n) <= kSelfWrite) return;
+    const float* fin = a.final_stats + a.mp.part_of_end(n) * 2 * a.cpad;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      m[i] = qok ? __ldcg(fin + 4 * q + i) : 0.0f;
+      inv[i] = qok ? __ldcg(fin + a.cpad + 4 * q + i) : 0.0f;
+    }
+    #pragma unroll 1
+    for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+      quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
+      quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
+    }
+    return;
+  } else {
+    float d[4];
+    const bool one_chunk = cur.hi - cur.lo <= Q::CHUNK;
+    float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (whole && a.xn && qok) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+      nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
+    }
+    if (one_chunk) {
+      // Exact two-step form: maximum first, then each exponential once;
+      // x keeps exp(l - m) for the write.
+      if (staged != nullptr)
+        quad_load_smem<LP, kEnv>(staged, staged_env, cur.lo, cur.hi, g, q, qok, x);
+      else
+        quad_load<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, x);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        m[i] = qok ? __ldcg(fin + 4 * q + i) : 0.0f;
-        inv[i] = qok ? __ldcg(fin + a.cpad + 4 * q + i) : 0.0f;
+        float cm = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
+        for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
+        m[i] = fmaxf(cm, nl[i]);
+        // With m = -inf every row is -inf too; shifting by 0 keeps
+        // exp(-inf) = 0 and avoids -inf - -inf.
+        const float ms = m[i] == -INFINITY ? 0.0f : m[i];
+        float acc = 0.0f;
+#pragma unroll
+        for (int t = 0; t < Q::T; ++t) {
+          const float w = __expf(quad_get(x[t], i) - ms);
+          quad_set(x[t], i, w);
+          acc += w;
+        }
+        for (int st = LP; st < kWarp; st <<= 1) acc += __shfl_xor_sync(kFull, acc, st);
+        d[i] = acc;
       }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
       #pragma unroll 1
       for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
         quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
-        quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
-      }
-      continue;
-    } else {
-      float d[4];
-      const bool one_chunk = cur.hi - cur.lo <= Q::CHUNK;
-      float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (whole && a.xn && qok) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
-        nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
-      }
-      if (one_chunk) {
-        // Exact two-step form: maximum first, then each exponential once;
-        // x keeps exp(l - m) for the write.
-        quad_load<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, x);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           float cm = -INFINITY;
 #pragma unroll
           for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
-          for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
-          m[i] = fmaxf(cm, nl[i]);
-          // With m = -inf every row is -inf too; shifting by 0 keeps
-          // exp(-inf) = 0 and avoids -inf - -inf.
-          const float ms = m[i] == -INFINITY ? 0.0f : m[i];
-          float acc = 0.0f;
+          const float mn = fmaxf(m[i], cm);
+          float acc = d[i] * shifted_exp(m[i], mn);
 #pragma unroll
-          for (int t = 0; t < Q::T; ++t) {
-            const float w = __expf(quad_get(x[t], i) - ms);
-            quad_set(x[t], i, w);
-            acc += w;
-          }
-          for (int st = LP; st < kWarp; st <<= 1) acc += __shfl_xor_sync(kFull, acc, st);
+          for (int t = 0; t < Q::T; ++t) acc += shifted_exp_fast(quad_get(x[t], i), mn);
           d[i] = acc;
+          m[i] = mn;
         }
-      } else {
+      }
+      // Merge the G edge groups (fixed butterfly; every lane ends equal).
+      for (int st = LP; st < kWarp; st <<= 1) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
+        for (int i = 0; i < 4; ++i) {
+          const float mo = __shfl_xor_sync(kFull, m[i], st);
+          const float dd = __shfl_xor_sync(kFull, d[i], st);
+          const float mn = fmaxf(m[i], mo);
+          d[i] = d[i] * shifted_exp(m[i], mn) + dd * shifted_exp(mo, mn);
+          m[i] = mn;
+        }
+      }
+    }
+    if (whole) {
+      float w0[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        // one_chunk: m already includes the null logit and x holds
+        // exp(l - m); otherwise rescale the running sum to the final max.
+        const float mm = fmaxf(m[i], nl[i]);
+        w0[i] = shifted_exp(nl[i], mm);
+        const float total = (one_chunk ? d[i] : d[i] * shifted_exp(m[i], mm)) + w0[i];
+        inv[i] = total > 0.0f ? 1.0f / total : 0.0f;
+        m[i] = mm;
+      }
+      if (g == 0 && qok && a.out_null) {
+        reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+            make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
+      }
+      if (one_chunk) {
+#pragma unroll
+        for (int t = 0; t < Q::T; ++t)
+          x[t] = make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+        quad_store<LP>(a, cur.lo, cur.hi, g, q, qok, x);
+      } else {
         #pragma unroll 1
         for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
           quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float cm = -INFINITY;
-#pragma unroll
-            for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
-            const float mn = fmaxf(m[i], cm);
-            float acc = d[i] * shifted_exp(m[i], mn);
-#pragma unroll
-            for (int t = 0; t < Q::T; ++t) acc += shifted_exp_fast(quad_get(x[t], i), mn);
-            d[i] = acc;
-            m[i] = mn;
-          }
-        }
-        // Merge the G edge groups (fixed butterfly; every lane ends equal).
-        for (int st = LP; st < kWarp; st <<= 1) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float mo = __shfl_xor_sync(kFull, m[i], st);
-            const float dd = __shfl_xor_sync(kFull, d[i], st);
-            const float mn = fmaxf(m[i], mo);
-            d[i] = d[i] * shifted_exp(m[i], mn) + dd * shifted_exp(mo, mn);
-            m[i] = mn;
-          }
+          quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
         }
       }
-      if (whole) {
-        float w0[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          // one_chunk: m already includes the null logit and x holds
-          // exp(l - m); otherwise rescale the running sum to the final max.
-          const float mm = fmaxf(m[i], nl[i]);
-          w0[i] = shifted_exp(nl[i], mm);
-          const float total = (one_chunk ? d[i] : d[i] * shifted_exp(m[i], mm)) + w0[i];
-          inv[i] = total > 0.0f ? 1.0f / total : 0.0f;
-          m[i] = mm;
-        }
-        if (g == 0 && qok && a.out_null) {
-          reinterpret_cast<float4*>(a.out_null + n * C)[q] =
-              make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
-        }
-        if (one_chunk) {
-#pragma unroll
-          for (int t = 0; t < Q::T; ++t)
-            x[t] = make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
-          quad_store<LP>(a, cur.lo, cur.hi, g, q, qok, x);
-        } else {
-          #pragma unroll 1
-          for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
-            quad_load<LP, kEnv>(a, base, cur.hi, g, q, qok, x);
-            quad_write<LP>(a, base, cur.hi, g, q, qok, x, m, inv);
-          }
-        }
-        continue;
-      }
-      // Split segment: publish per-channel (m, d); the last piece combines.
-      float* mine = a.ss.slot(p, cur.kind);
-      if (g == 0 && qok) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          __stcg(mine + 4 * q + i, m[i]);
-          __stcg(mine + a.cpad + 4 * q + i, d[i]);
-        }
-      }
-      const int64_t first = a.mp.part_of_first_edge(n);
-      const int64_t last = a.mp.part_of_end(n);
-      if (!arrive_last(a.ss, first, last, 0)) continue;
-      // Every lane combines its own channel quad (the G copies agree).
-      if (a.xn && qok) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
-        nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
-      }
-      float* fin = a.final_stats + last * 2 * a.cpad;
+      return;
+    }
+    // Split segment: publish per-channel (m, d); the last piece combines.
+    float* mine = a.ss.slot(p, cur.kind);
+    if (g == 0 && qok) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int64_t c = 4 * q + i;
-        float mm = nl[i];
-        float total = 0.0f;
-        if (qok) {
-          for (int64_t qq = first; qq <= last; ++qq)
-            mm = fmaxf(mm, __ldcg(a.ss.slot(qq, qq == last ? kHead : kTail) + c));
-          total = shifted_exp(nl[i], mm);
-          for (int64_t qq = first; qq <= last; ++qq) {
-            const float* sq = a.ss.slot(qq, qq == last ? kHead : kTail);
-            total += shifted_exp(__ldcg(sq + c), mm) * __ldcg(sq + a.cpad + c);
-          }
-        }
-        const float iv = total > 0.0f ? 1.0f / total : 0.0f;
-        m[i] = mm;
-        inv[i] = iv;
-        if (g == 0 && qok) {
-          if (a.out_null) a.out_null[n * C + c] = shifted_exp(nl[i], mm) * iv;
-          __stcg(fin + c, mm);
-          __stcg(fin + a.cpad + c, iv);
-        }
-      }
-      const int64_t seg_lo = __ldg(a.mp.offsets + n);
-      const int64_t seg_hi = __ldg(a.mp.offsets + n + 1);
-      if (seg_hi - seg_lo <= kSelfWrite) {
-        #pragma unroll 1
-        for (int64_t base = seg_lo; base < seg_hi; base += Q::CHUNK) {
-          quad_load<LP, kEnv>(a, base, seg_hi, g, q, qok, x);
-          quad_write<LP>(a, base, seg_hi, g, q, qok, x, m, inv);
-        }
-      } else if (lane == 0) {
-        atomicExch(a.big_split, 1);
+        __stcg(mine + 4 * q + i, m[i]);
+        __stcg(mine + a.cpad + 4 * q + i, d[i]);
       }
     }
+    const int64_t first = a.mp.part_of_first_edge(n);
+    const int64_t last = a.mp.part_of_end(n);
+    if (!arrive_last(a.ss, first, last, 0)) return;
+    // Every lane combines its own channel quad (the G copies agree).
+    if (a.xn && qok) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+      nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
+    }
+    float* fin = a.final_stats + last * 2 * a.cpad;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t c = 4 * q + i;
+      float mm = nl[i];
+      float total = 0.0f;
+      if (qok) {
+        for (int64_t qq = first; qq <= last; ++qq)
+          mm = fmaxf(mm, __ldcg(a.ss.slot(qq, qq == last ? kHead : kTail) + c));
+        total = shifted_exp(nl[i], mm);
+        for (int64_t qq = first; qq <= last; ++qq) {
+          const float* sq = a.ss.slot(qq, qq == last ? kHead : kTail);
+          total += shifted_exp(__ldcg(sq + c), mm) * __ldcg(sq + a.cpad + c);
+        }
+      }
+      const float iv = total > 0.0f ? 1.0f / total : 0.0f;
+      m[i] = mm;
+      inv[i] = iv;
+      if (g == 0 && qok) {
+        if (a.out_null) a.out_null[n * C + c] = shifted_exp(nl[i], mm) * iv;
+        __stcg(fin + c, mm);
+        __stcg(fin + a.cpad + c, iv);
+      }
+    }
+    const int64_t seg_lo = __ldg(a.mp.offsets + n);
+    const int64_t seg_hi = __ldg(a.mp.offsets + n + 1);
+    if (seg_hi - seg_lo <= kSelfWrite) {
+      #pragma unroll 1
+      for (int64_t base = seg_lo; base < seg_hi; base += Q::CHUNK) {
+        quad_load<LP, kEnv>(a, base, seg_hi, g, q, qok, x);
+        quad_write<LP>(a, base, seg_hi, g, q, qok, x, m, inv);
+      }
+    } else if (lane == 0) {
+      atomicExch(a.big_split, 1);
+    }
+  }
+}
+
+// Channel counts up to 8 (LP <= 2) hold a typical segment (<= 128 rows) in
+// one chunk, so the main pass stages the next piece in shared memory while
+// computing the current one (2 CTAs per SM: 72 KB of buffers each).  Wider
+// rows do not fit a chunk; their main pass reads global memory directly.
+template <int LP>
+constexpr bool quad_pipelined() {
+  return LP <= 2;
+}
+
+template <int LP, bool kSplitPass, bool kEnv>
+__global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
+    segment_softmax_quad_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  using S = QuadStage<LP>;
+  extern __shared__ float4 quad_smem[];
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const bool qok = 4 * q < a.channels;
+  if constexpr (kSplitPass || !quad_pipelined<LP>()) {
+    if constexpr (kSplitPass) {
+      if (*reinterpret_cast<volatile int*>(a.big_split) == 0) return;
+    }
+    SegCursor cur(a.mp, part_range(a.mp, p));
+    while (cur.next())
+      quad_segment<LP, kSplitPass, kEnv>(a, p, piece_of(cur), lane, g, q, qok, nullptr, nullptr);
+  } else {
+    // Double-buffered pipeline: the next piece's rows (when it fits one
+    // chunk) are copied into shared memory while this one is computed.
+    char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
+    float4* bufs[2] = {reinterpret_cast<float4*>(mine),
+                       reinterpret_cast<float4*>(mine + S::kBytes)};
+    SegCursor ahead(a.mp, part_range(a.mp, p));  // one piece ahead of `cur`
+    bool have = ahead.next();
+    Piece cur = piece_of(ahead);
+    int b = 0;
+    if (have && cur.hi - cur.lo <= Q::CHUNK)
+      quad_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, bufs[0],
+                           reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+    cp_async_commit();
+    while (have) {
+      const bool have_next = ahead.next();
+      const Piece nxt = piece_of(ahead);
+      if (have_next && nxt.hi - nxt.lo <= Q::CHUNK)
+        quad_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, qok, bufs[b ^ 1],
+                             reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
+      cp_async_commit();
+      cp_async_wait<1>();  // this piece's copies have landed
+      __syncwarp();
+      const bool staged = cur.hi - cur.lo <= Q::CHUNK;
+      quad_segment<LP, false, kEnv>(a, p, cur, lane, g, q, qok, staged ? bufs[b] : nullptr,
+                                    staged ? reinterpret_cast<float*>(bufs[b] + S::kRowsF4)
+                                           : nullptr);
+      __syncwarp();  // every lane is done with bufs[b] before it is refilled
+      cur = nxt;
+      have = have_next;
+      b ^= 1;
+    }
+    cp_async_wait<0>();
   }
 }
 
@@ -674,6 +836,7 @@ using SmxKernel = void (*)(SmxArgs);
 struct SmxConfig {
   SmxKernel main = nullptr, split = nullptr;
   int64_t tc = 0, tiles = 1;
+  size_t main_smem = 0;  // dynamic shared memory of the main launch
 };
 
 template <int NC, int G>
@@ -693,6 +856,7 @@ SmxConfig quad_make_env() {
   c.split = segment_softmax_quad_kernel<LP, true, kEnv>;
   c.tc = 4 * LP;
   c.tiles = 1;
+  c.main_smem = quad_pipelined<LP>() ? kWarpsPerBlock * QuadStage<LP>::kWarpBytes : 0;
   return c;
 }
 
@@ -737,6 +901,7 @@ struct SmxLayout {
   size_t bytes = 0;
   SplitSlots ss{};
   float* final_stats = nullptr;
+  int smem_status = BYSJ_OK;
 };
 
 SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
@@ -744,9 +909,10 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
   SmxLayout L;
   L.cfg = smx_config(channels, backward, quad_ok, env);
   const DeviceInfo& dev = current_device_info();
+  L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem);
   const int64_t resident =
       static_cast<int64_t>(dev.sm_count) *
-      resident_blocks(reinterpret_cast<const void*>(L.cfg.main)) *
+      resident_blocks(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem) *
       kWarpsPerBlock;
   int64_t warps = resident / L.cfg.tiles;
   if (warps < 1) warps = 1;
@@ -773,8 +939,9 @@ int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
   a.final_stats = L.final_stats;
   a.big_split = L.ss.tickets + L.plan.parts * L.cfg.tiles;
   a.cpad = L.cpad;
+  if (L.smem_status != BYSJ_OK) return L.smem_status;
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
-  L.cfg.main<<<grid, kBlock, 0, s>>>(a);
+  L.cfg.main<<<grid, kBlock, L.cfg.main_smem, s>>>(a);
   st = launch_check(name);
   if (st) return st;
   L.cfg.split<<<grid, kBlock, 0, s>>>(a);
