@@ -5,10 +5,11 @@
 // The reference (python/kernels/segment.py:60-71) runs a stable argsort of
 // the int64 keys plus bincount/cumsum.  Here, all on the device:
 //
-//  1. offsets: warp-aggregated histogram + three-phase scan (offsets.cu);
-//  2. scatter: each edge takes a slot in its key's group with a warp-
-//     aggregated integer atomic (lanes of one warp instruction keep their
-//     order, warps do not);
+//  1. count: warp-aggregated integer atomics count the edges per key, and
+//     each edge keeps the count its increment found (its slot in the group:
+//     lanes of one warp instruction keep their order, warps do not);
+//     a three-phase scan turns the counts into offsets;
+//  2. place: order[offsets[key] + slot] = edge, with no atomics;
 //  3. sort each group by edge index, which restores the stable order
 //     exactly (edge indices are distinct, so the sorted group is unique and
 //     the result does not depend on the scatter's interleaving):
@@ -24,48 +25,149 @@ namespace {
 
 constexpr int kWarpBucket = 256;   // largest group sorted by one warp
 constexpr int kBlockBucket = 4096; // largest group sorted by one CTA in shared memory
-constexpr int64_t kNoEdge = INT64_MAX;
 
 __device__ __forceinline__ unsigned lanemask_lt() {
   return (1u << lane_id()) - 1u;
 }
 
-// order[offsets[k] + cursor[k]++] = e for every edge, lanes holding the same
-// key merged by __match_any_sync.
+// Pass 1: counts[k] = number of edges with key k, and rank[e] = the count
+// edge e's increment found (its arrival slot in its group; lanes of one warp
+// instruction that share a key are merged by __match_any_sync and keep lane
+// order).  Out-of-range keys are skipped and flagged.
 __global__ void __launch_bounds__(kBlock)
-    group_scatter_kernel(const int64_t* __restrict__ keys, int64_t n_edges, int64_t n_keys,
-                         const int64_t* __restrict__ offsets, unsigned* __restrict__ cursor,
-                         int64_t* __restrict__ order) {
+    group_count_kernel(const int64_t* __restrict__ keys, int64_t n_edges, int64_t n_keys,
+                       unsigned* __restrict__ counts, unsigned* __restrict__ rank,
+                       uint32_t* flags) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t warp_begin =
       static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x - lane_id();
+  uint32_t bad = 0;
   for (int64_t base = warp_begin; base < n_edges; base += stride) {  // warp-uniform
     const int64_t e = base + lane_id();
     int64_t k = -1;
     if (e < n_edges) {
       k = __ldg(keys + e);
-      if (k < 0 || k >= n_keys) k = -1;
+      if (k < 0 || k >= n_keys) {
+        bad = BYSJ_FLAG_OUT_OF_RANGE;
+        k = -1;
+      }
     }
     const unsigned peers = __match_any_sync(kFull, static_cast<unsigned long long>(k));
     const int leader = __ffs(peers) - 1;
     unsigned slot = 0;
-    if (k >= 0 && lane_id() == leader) slot = atomicAdd(cursor + k, __popc(peers));
+    if (k >= 0 && lane_id() == leader) slot = atomicAdd(counts + k, __popc(peers));
     slot = __shfl_sync(kFull, slot, leader);
-    if (k >= 0) order[__ldg(offsets + k) + slot + __popc(peers & lanemask_lt())] = e;
+    if (e < n_edges) rank[e] = slot + __popc(peers & lanemask_lt());
   }
+  bad = __reduce_or_sync(kFull, bad);
+  if (bad && lane_id() == 0) atomicOr(flags, bad);
+}
+
+// Pass 2 (no atomics): order[offsets[k] + rank[e]] = e.
+template <typename V>
+__global__ void __launch_bounds__(kBlock)
+    group_place_kernel(const int64_t* __restrict__ keys, int64_t n_edges, int64_t n_keys,
+                       const int64_t* __restrict__ offsets, const unsigned* __restrict__ rank,
+                       V* __restrict__ order) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n_edges;
+       e += stride) {
+    const int64_t k = __ldg(keys + e);
+    if (k < 0 || k >= n_keys) continue;
+    order[__ldg(offsets + k) + __ldg(rank + e)] = static_cast<V>(e);
+  }
+}
+
+// Inclusive CTA-wide scan of one int64 per thread; *total gets the CTA sum.
+__device__ int64_t block_scan_i64(int64_t v, int64_t* total) {
+  __shared__ int64_t warp_sums[kWarpsPerBlock];
+  const int lane = lane_id();
+  const int warp = threadIdx.x >> 5;
+  for (int s = 1; s < kWarp; s <<= 1) {
+    const int64_t t = __shfl_up_sync(kFull, v, s);
+    if (lane >= s) v += t;
+  }
+  if (lane == kWarp - 1) warp_sums[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t w = lane < kWarpsPerBlock ? warp_sums[lane] : 0;
+    for (int s = 1; s < kWarpsPerBlock; s <<= 1) {
+      const int64_t t = __shfl_up_sync(kFull, w, s);
+      if (lane >= s) w += t;
+    }
+    if (lane < kWarpsPerBlock) warp_sums[lane] = w;
+  }
+  __syncthreads();
+  if (warp > 0) v += warp_sums[warp - 1];
+  *total = warp_sums[kWarpsPerBlock - 1];
+  __syncthreads();
+  return v;
+}
+
+constexpr int kScanTile = 2048;  // counts per CTA in the offsets scan
+
+// Exclusive scan of counts[0, n) into offsets[0, n] in three phases.
+__global__ void __launch_bounds__(kBlock)
+    group_tile_sums_kernel(const unsigned* __restrict__ counts, int64_t n,
+                           int64_t* __restrict__ tile_sums) {
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
+  int64_t v = 0;
+  for (int i = threadIdx.x; i < kScanTile; i += kBlock)
+    if (base + i < n) v += counts[base + i];
+  int64_t total = 0;
+  block_scan_i64(v, &total);
+  if (threadIdx.x == 0) tile_sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kBlock)
+    group_tile_prefix_kernel(int64_t* __restrict__ tile_sums, int64_t tiles) {
+  int64_t carry = 0;
+  for (int64_t base = 0; base < tiles; base += kBlock) {
+    const int64_t i = base + threadIdx.x;
+    const int64_t v = i < tiles ? tile_sums[i] : 0;
+    int64_t total = 0;
+    const int64_t inc = block_scan_i64(v, &total);
+    if (i < tiles) tile_sums[i] = carry + inc - v;
+    carry += total;
+  }
+}
+
+__global__ void __launch_bounds__(kBlock)
+    group_tile_apply_kernel(const unsigned* __restrict__ counts, int64_t n,
+                            const int64_t* __restrict__ tile_prefix,
+                            int64_t* __restrict__ offsets) {
+  constexpr int kPer = kScanTile / kBlock;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile +
+                       static_cast<int64_t>(threadIdx.x) * kPer;
+  int64_t local[kPer];
+  int64_t run = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    run += base + i < n ? counts[base + i] : 0;
+    local[i] = run;
+  }
+  int64_t total = 0;
+  const int64_t inc = block_scan_i64(run, &total);
+  const int64_t before = tile_prefix[blockIdx.x] + inc - run;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    if (base + i < n) offsets[base + i + 1] = before + local[i];
+  if (blockIdx.x == 0 && threadIdx.x == 0) offsets[0] = 0;
 }
 
 // Sorts seg[0, n) ascending, n <= 32 K, with one warp: element i = 32 k + lane
 // lives in register a[k] of that lane; strides below 32 exchange across lanes,
-// larger strides inside a lane.
-template <int K>
+// larger strides inside a lane.  V: the register type of an edge index
+// (uint32_t when every index fits, else int64_t).
+template <int K, typename V>
 __device__ __forceinline__ void warp_bitonic(int64_t* __restrict__ seg, int n) {
+  constexpr V kPad = ~V(0) > V(0) ? ~V(0) : V(INT64_MAX);
   const int lane = lane_id();
-  int64_t a[K];
+  V a[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     const int i = 32 * k + lane;
-    a[k] = i < n ? seg[i] : kNoEdge;
+    a[k] = i < n ? static_cast<V>(seg[i]) : kPad;
   }
 #pragma unroll
   for (int size = 2; size <= 32 * K; size <<= 1) {
@@ -78,19 +180,19 @@ __device__ __forceinline__ void warp_bitonic(int64_t* __restrict__ seg, int n) {
           if ((k & ks) != 0) continue;
           const int k2 = k | ks;
           const bool up = ((32 * k + lane) & size) == 0;
-          const int64_t lo = a[k] < a[k2] ? a[k] : a[k2];
-          const int64_t hi = a[k] < a[k2] ? a[k2] : a[k];
+          const V lo = a[k] < a[k2] ? a[k] : a[k2];
+          const V hi = a[k] < a[k2] ? a[k2] : a[k];
           a[k] = up ? lo : hi;
           a[k2] = up ? hi : lo;
         }
       } else {
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-          const int64_t other = __shfl_xor_sync(kFull, a[k], stride);
+          const V other = __shfl_xor_sync(kFull, a[k], stride);
           const bool up = ((32 * k + lane) & size) == 0;
           const bool lower = (lane & stride) == 0;
-          const int64_t lo = a[k] < other ? a[k] : other;
-          const int64_t hi = a[k] < other ? other : a[k];
+          const V lo = a[k] < other ? a[k] : other;
+          const V hi = a[k] < other ? other : a[k];
           a[k] = (lower == up) ? lo : hi;
         }
       }
@@ -99,7 +201,7 @@ __device__ __forceinline__ void warp_bitonic(int64_t* __restrict__ seg, int n) {
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     const int i = 32 * k + lane;
-    if (i < n) seg[i] = a[k];
+    if (i < n) seg[i] = static_cast<int64_t>(a[k]);
   }
 }
 
@@ -110,6 +212,7 @@ struct GroupLists {
 };
 
 // One warp per key: sorts groups of up to 256 edges, lists the others.
+template <typename V>
 __global__ void __launch_bounds__(kBlock)
     group_sort_warp_kernel(const int64_t* __restrict__ offsets, int64_t n_keys,
                            int64_t* __restrict__ order, GroupLists lists) {
@@ -121,13 +224,13 @@ __global__ void __launch_bounds__(kBlock)
     int64_t* seg = order + lo;
     const int m = static_cast<int>(n < kWarpBucket ? n : kWarpBucket);
     if (n <= 32) {
-      warp_bitonic<1>(seg, m);
+      warp_bitonic<1, V>(seg, m);
     } else if (n <= 64) {
-      warp_bitonic<2>(seg, m);
+      warp_bitonic<2, V>(seg, m);
     } else if (n <= 128) {
-      warp_bitonic<4>(seg, m);
+      warp_bitonic<4, V>(seg, m);
     } else if (n <= kWarpBucket) {
-      warp_bitonic<8>(seg, m);
+      warp_bitonic<8, V>(seg, m);
     } else if (lane_id() == 0) {
       if (n <= kBlockBucket)
         lists.block_groups[atomicAdd(lists.counts, 1)] = static_cast<int>(key);
@@ -137,93 +240,66 @@ __global__ void __launch_bounds__(kBlock)
   }
 }
 
-// One CTA per listed group of 257..4096 edges: bitonic sort in shared memory.
+// The groups the warp pass listed, one CTA each: groups of 257..4096 edges
+// are sorted by a bitonic network in shared memory; larger groups are
+// rebuilt by scanning all keys in edge order with a CTA-wide prefix count.
+template <typename V>
 __global__ void __launch_bounds__(kBlock)
-    group_sort_block_kernel(const int64_t* __restrict__ offsets, int64_t* __restrict__ order,
+    group_sort_large_kernel(const int64_t* __restrict__ keys, int64_t n_edges,
+                            const int64_t* __restrict__ offsets, int64_t* __restrict__ order,
                             GroupLists lists) {
-  __shared__ int64_t s[kBlockBucket];
-  const int used = *reinterpret_cast<volatile int*>(lists.counts);
-  for (int g = blockIdx.x; g < used; g += gridDim.x) {
-    const int key = lists.block_groups[g];
-    const int64_t lo = offsets[key];
-    const int n = static_cast<int>(offsets[key + 1] - lo);
-    int p = 1;
-    while (p < n) p <<= 1;
-    for (int i = threadIdx.x; i < p; i += blockDim.x) s[i] = i < n ? order[lo + i] : kNoEdge;
-    __syncthreads();
-    for (int size = 2; size <= p; size <<= 1) {
-      for (int stride = size / 2; stride > 0; stride >>= 1) {
-        for (int t = threadIdx.x; t < p / 2; t += blockDim.x) {
-          const int i = 2 * stride * (t / stride) + (t % stride);
-          const int j = i + stride;
-          const bool up = (i & size) == 0;
-          const int64_t x = s[i], y = s[j];
-          if ((x > y) == up) {
-            s[i] = y;
-            s[j] = x;
+  constexpr V kPad = ~V(0) > V(0) ? ~V(0) : V(INT64_MAX);
+  constexpr int kPer = 4;  // consecutive edges per thread per scan step
+  __shared__ V s[kBlockBucket];
+  const int sorted = *reinterpret_cast<volatile int*>(lists.counts);
+  const int scanned = *reinterpret_cast<volatile int*>(lists.counts + 1);
+  for (int g = blockIdx.x; g < sorted + scanned; g += gridDim.x) {
+    if (g < sorted) {
+      const int key = lists.block_groups[g];
+      const int64_t lo = offsets[key];
+      const int n = static_cast<int>(offsets[key + 1] - lo);
+      int p = 1;
+      while (p < n) p <<= 1;
+      for (int i = threadIdx.x; i < p; i += blockDim.x)
+        s[i] = i < n ? static_cast<V>(order[lo + i]) : kPad;
+      __syncthreads();
+      for (int size = 2; size <= p; size <<= 1) {
+        for (int stride = size / 2; stride > 0; stride >>= 1) {
+          for (int t = threadIdx.x; t < p / 2; t += blockDim.x) {
+            const int i = 2 * stride * (t / stride) + (t % stride);
+            const int j = i + stride;
+            const bool up = (i & size) == 0;
+            const V x = s[i], y = s[j];
+            if ((x > y) == up) {
+              s[i] = y;
+              s[j] = x;
+            }
           }
+          __syncthreads();
         }
-        __syncthreads();
       }
-    }
-    for (int i = threadIdx.x; i < n; i += blockDim.x) order[lo + i] = s[i];
-    __syncthreads();
-  }
-}
-
-// Inclusive CTA-wide scan of one int per thread; *total gets the CTA sum.
-__device__ int block_scan_int(int v, int* total) {
-  __shared__ int warp_sums[kWarpsPerBlock];
-  const int lane = lane_id();
-  const int warp = threadIdx.x >> 5;
-  for (int s = 1; s < kWarp; s <<= 1) {
-    const int t = __shfl_up_sync(kFull, v, s);
-    if (lane >= s) v += t;
-  }
-  if (lane == kWarp - 1) warp_sums[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < kWarpsPerBlock ? warp_sums[lane] : 0;
-    for (int s = 1; s < kWarpsPerBlock; s <<= 1) {
-      const int t = __shfl_up_sync(kFull, w, s);
-      if (lane >= s) w += t;
-    }
-    if (lane < kWarpsPerBlock) warp_sums[lane] = w;
-  }
-  __syncthreads();
-  if (warp > 0) v += warp_sums[warp - 1];
-  *total = warp_sums[kWarpsPerBlock - 1];
-  __syncthreads();
-  return v;
-}
-
-// One CTA per listed group of more than 4096 edges: scans all keys in edge
-// order and writes the group's edges in that order.
-__global__ void __launch_bounds__(kBlock)
-    group_scan_kernel(const int64_t* __restrict__ keys, int64_t n_edges,
-                      const int64_t* __restrict__ offsets, int64_t* __restrict__ order,
-                      GroupLists lists) {
-  constexpr int kPer = 4;  // consecutive edges per thread per step
-  const int used = *reinterpret_cast<volatile int*>(lists.counts + 1);
-  for (int g = blockIdx.x; g < used; g += gridDim.x) {
-    const int64_t key = lists.scan_groups[g];
-    int64_t out = offsets[key];
-    for (int64_t base = 0; base < n_edges; base += static_cast<int64_t>(kBlock) * kPer) {
-      const int64_t first = base + static_cast<int64_t>(threadIdx.x) * kPer;
-      bool hit[kPer];
-      int mine = 0;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) order[lo + i] = static_cast<int64_t>(s[i]);
+      __syncthreads();
+    } else {
+      const int64_t key = lists.scan_groups[g - sorted];
+      int64_t out = offsets[key];
+      for (int64_t base = 0; base < n_edges; base += static_cast<int64_t>(kBlock) * kPer) {
+        const int64_t first = base + static_cast<int64_t>(threadIdx.x) * kPer;
+        bool hit[kPer];
+        int mine = 0;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        hit[j] = first + j < n_edges && __ldg(keys + first + j) == key;
-        mine += hit[j];
+        for (int j = 0; j < kPer; ++j) {
+          hit[j] = first + j < n_edges && __ldg(keys + first + j) == key;
+          mine += hit[j];
+        }
+        int64_t total = 0;
+        const int64_t inclusive = block_scan_i64(mine, &total);
+        int64_t at = out + inclusive - mine;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j)
+          if (hit[j]) order[at++] = first + j;
+        out += total;
       }
-      int total = 0;
-      const int inclusive = block_scan_int(mine, &total);
-      int64_t at = out + inclusive - mine;
-#pragma unroll
-      for (int j = 0; j < kPer; ++j)
-        if (hit[j]) order[at++] = first + j;
-      out += total;
     }
   }
 }
@@ -237,24 +313,38 @@ unsigned grid_for(int64_t items, int64_t per_block, int64_t cap_per_sm) {
 }
 
 struct GroupLayout {
-  size_t offsets_ws = 0;
   size_t need = 0;
-  void* offsets_workspace = nullptr;
-  unsigned* cursor = nullptr;
+  int64_t tiles = 0;
+  unsigned* counts = nullptr;   // [n_keys]
+  unsigned* rank = nullptr;     // [n_edges]
+  int64_t* tile_sums = nullptr; // [tiles + 1]
   GroupLists lists{};
 };
 
-GroupLayout group_layout(int64_t n_keys, void* ws) {
+GroupLayout group_layout(int64_t n_edges, int64_t n_keys, void* ws) {
   GroupLayout L;
-  L.offsets_ws = bysj_segment_offsets_workspace_size(n_keys);
+  L.tiles = (n_keys + kScanTile - 1) / kScanTile;
   Carver carve(ws);
-  L.offsets_workspace = carve.take<char>(L.offsets_ws);
-  L.cursor = carve.take<unsigned>(static_cast<size_t>(n_keys) + 1);
+  L.counts = carve.take<unsigned>(static_cast<size_t>(n_keys) + 1);
+  L.rank = carve.take<unsigned>(static_cast<size_t>(n_edges) + 1);
+  L.tile_sums = carve.take<int64_t>(static_cast<size_t>(L.tiles) + 1);
   L.lists.counts = carve.take<int>(2);
   L.lists.block_groups = carve.take<int>(static_cast<size_t>(n_keys) + 1);
   L.lists.scan_groups = carve.take<int>(static_cast<size_t>(n_keys) + 1);
   L.need = carve.need;
   return L;
+}
+
+template <typename V>
+int group_sorts(const int64_t* keys, int64_t n_edges, int64_t n_keys, const int64_t* offsets,
+                int64_t* order, const GroupLayout& L, cudaStream_t s) {
+  group_sort_warp_kernel<V><<<grid_for(n_keys, kWarpsPerBlock, 16), kBlock, 0, s>>>(
+      offsets, n_keys, order, L.lists);
+  int st = launch_check("group_sort_warp_kernel");
+  if (st) return st;
+  const unsigned sms = static_cast<unsigned>(current_device_info().sm_count);
+  group_sort_large_kernel<V><<<2 * sms, kBlock, 0, s>>>(keys, n_edges, offsets, order, L.lists);
+  return launch_check("group_sort_large_kernel");
 }
 
 }  // namespace
@@ -266,7 +356,7 @@ extern "C" {
 
 size_t bysj_group_by_key_workspace_size(int64_t n_edges, int64_t n_keys) {
   if (n_edges < 0 || n_keys < 0) return 0;
-  return group_layout(n_keys, nullptr).need;
+  return group_layout(n_edges, n_keys, nullptr).need;
 }
 
 int bysj_group_by_key(const int64_t* keys, int64_t n_edges, int64_t n_keys, int64_t* order,
@@ -275,40 +365,49 @@ int bysj_group_by_key(const int64_t* keys, int64_t n_edges, int64_t n_keys, int6
   clear_error();
   if (n_edges < 0 || n_keys < 0)
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "group by key: invalid sizes");
-  if (n_keys > INT32_MAX - 1)
-    return fail(BYSJ_ERR_TOO_LARGE, "group by key: more than 2^31 - 2 keys");
+  if (n_keys > INT32_MAX - 1 || n_edges > static_cast<int64_t>(UINT32_MAX))
+    return fail(BYSJ_ERR_TOO_LARGE, "group by key: more than 2^31 - 2 keys or 2^32 - 1 edges");
   if (offsets == nullptr || flags == nullptr ||
       (n_edges > 0 && (keys == nullptr || order == nullptr)))
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "group by key: NULL pointer");
-  GroupLayout L = group_layout(n_keys, workspace);
+  GroupLayout L = group_layout(n_edges, n_keys, workspace);
   if (workspace == nullptr || workspace_bytes < L.need)
     return fail(BYSJ_ERR_WORKSPACE, "group by key: workspace of %zu bytes needed, %zu given",
                 L.need, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int st = bysj_segment_offsets_histogram(keys, n_edges, n_keys, offsets, flags,
-                                          L.offsets_workspace, L.offsets_ws, stream);
-  if (st) return st;
-  if (n_edges == 0 || n_keys == 0) return BYSJ_OK;
-  st = cuda_check(cudaMemsetAsync(L.cursor, 0, sizeof(unsigned) * n_keys, s),
-                  "group by key: zero cursors");
+  if (n_keys == 0)
+    return cuda_check(cudaMemsetAsync(offsets, 0, sizeof(int64_t), s), "group by key: offsets");
+  int st = cuda_check(cudaMemsetAsync(L.counts, 0, sizeof(unsigned) * n_keys, s),
+                      "group by key: zero counts");
   if (st) return st;
   st = cuda_check(cudaMemsetAsync(L.lists.counts, 0, 2 * sizeof(int), s),
                   "group by key: zero list counts");
   if (st) return st;
-  group_scatter_kernel<<<grid_for(n_edges, kBlock, 8), kBlock, 0, s>>>(keys, n_edges, n_keys,
-                                                                      offsets, L.cursor, order);
-  st = launch_check("group_scatter_kernel");
+  if (n_edges > 0) {
+    group_count_kernel<<<grid_for(n_edges, kBlock, 8), kBlock, 0, s>>>(keys, n_edges, n_keys,
+                                                                      L.counts, L.rank, flags);
+    st = launch_check("group_count_kernel");
+    if (st) return st;
+  }
+  group_tile_sums_kernel<<<static_cast<unsigned>(L.tiles), kBlock, 0, s>>>(L.counts, n_keys,
+                                                                          L.tile_sums);
+  st = launch_check("group_tile_sums_kernel");
   if (st) return st;
-  group_sort_warp_kernel<<<grid_for(n_keys, kWarpsPerBlock, 16), kBlock, 0, s>>>(
-      offsets, n_keys, order, L.lists);
-  st = launch_check("group_sort_warp_kernel");
+  group_tile_prefix_kernel<<<1, kBlock, 0, s>>>(L.tile_sums, L.tiles);
+  st = launch_check("group_tile_prefix_kernel");
   if (st) return st;
-  const unsigned sms = static_cast<unsigned>(current_device_info().sm_count);
-  group_sort_block_kernel<<<2 * sms, kBlock, 0, s>>>(offsets, order, L.lists);
-  st = launch_check("group_sort_block_kernel");
+  group_tile_apply_kernel<<<static_cast<unsigned>(L.tiles), kBlock, 0, s>>>(
+      L.counts, n_keys, L.tile_sums, offsets);
+  st = launch_check("group_tile_apply_kernel");
+  if (st || n_edges == 0) return st;
+  group_place_kernel<int64_t><<<grid_for(n_edges, kBlock, 8), kBlock, 0, s>>>(
+      keys, n_edges, n_keys, offsets, L.rank, order);
+  st = launch_check("group_place_kernel");
   if (st) return st;
-  group_scan_kernel<<<sms, kBlock, 0, s>>>(keys, n_edges, offsets, order, L.lists);
-  return launch_check("group_scan_kernel");
+  // Sorting 32-bit edge indices halves the register and shuffle traffic.
+  if (n_edges <= static_cast<int64_t>(UINT32_MAX) - 1)
+    return group_sorts<uint32_t>(keys, n_edges, n_keys, offsets, order, L, s);
+  return group_sorts<int64_t>(keys, n_edges, n_keys, offsets, order, L, s);
 }
 
 }  // extern "C"
