@@ -158,14 +158,23 @@ __global__ void __launch_bounds__(kBlock, 2) gie_fwd_kernel(GieArgs a) {
 // with R = (L+1)^2 - 1, row r has degree l(r) = floor(sqrt(r+1)) and reads
 // radial slot l(r) + slot_base.  A lane owns one 4-channel column quad for
 // all R rows (LPE = C/4 lanes per edge, EG = 32/LPE edges side by side), so
-// per edge it loads each degree's radial quad once (L loads) plus the R zonal
-// coefficients, and the row -> slot choice is resolved at compile time.
+// per edge it streams each degree's radial quad once (L 16-byte loads), and
+// the row -> slot choice is resolved at compile time.  The R zonal
+// coefficients of an edge are the same for its LPE lanes: each warp stages
+// them for 32 edges at a time in shared memory with coalesced loads, and the
+// lanes read them back as broadcasts.  With L = 3 the 15 x 4 accumulators
+// take 60 registers, so two CTAs per SM (also for L = 2); three for L = 1.
+constexpr int kZonalChunk = 32;  // edges whose zonal rows a warp stages at once
+
 template <int LPE, int L>
-__global__ void __launch_bounds__(kBlock, 2) gie_fwd_degree_kernel(GieArgs a, int64_t slot_base) {
+__global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
+    gie_fwd_degree_kernel(GieArgs a, int64_t slot_base) {
   constexpr int R = (L + 1) * (L + 1) - 1;
   constexpr int EG = kWarp / LPE;
+  __shared__ float zstage[kWarpsPerBlock][kZonalChunk * R];
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
+  float* zb = zstage[threadIdx.x >> 5];
   const int lane = lane_id();
   const int eg = lane / LPE;
   const int c4 = lane % LPE;
@@ -180,46 +189,61 @@ __global__ void __launch_bounds__(kBlock, 2) gie_fwd_degree_kernel(GieArgs a, in
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
-    int64_t s = cur.lo + eg;
-    for (; s + EG < cur.hi; s += 2 * EG) {
-      float4 rad[2][L];
-      float z[2][R];
+    for (int64_t lo = cur.lo; lo < cur.hi; lo += kZonalChunk) {  // warp-uniform
+      const int rows = static_cast<int>(cur.hi - lo < kZonalChunk ? cur.hi - lo : kZonalChunk);
+      __syncwarp();  // the previous chunk's reads are done
+      if (a.order == nullptr) {
+        const float* src = a.zonal + lo * R;
+        for (int i = lane; i < rows * R; i += kWarp) zb[i] = __ldg(src + i);
+      } else {
+        for (int i = lane; i < rows * R; i += kWarp) {
+          const int k = i / R;
+          zb[i] = __ldg(a.zonal + __ldg(a.order + lo + k) * R + (i - k * R));
+        }
+      }
+      __syncwarp();
+      int k = eg;
+      for (; k + EG < rows; k += 2 * EG) {
+        float4 rad[2][L];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int64_t slot = s + u * EG;
+        for (int u = 0; u < 2; ++u) {
+          const int64_t slot = lo + k + u * EG;
+          const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+          const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
+#pragma unroll
+          for (int l = 1; l <= L; ++l) rad[u][l - 1] = ld_stream_f4(rr + l * C);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float* z = zb + (k + u * EG) * R;
+#pragma unroll
+          for (int l = 1; l <= L; ++l)
+#pragma unroll
+            for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
+              const float zr = z[r];
+              acc[r][0] = fmaf(zr, rad[u][l - 1].x, acc[r][0]);
+              acc[r][1] = fmaf(zr, rad[u][l - 1].y, acc[r][1]);
+              acc[r][2] = fmaf(zr, rad[u][l - 1].z, acc[r][2]);
+              acc[r][3] = fmaf(zr, rad[u][l - 1].w, acc[r][3]);
+            }
+        }
+      }
+      if (k < rows) {
+        const int64_t slot = lo + k;
         const int64_t e = a.order ? __ldg(a.order + slot) : slot;
         const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
+        const float* z = zb + k * R;
 #pragma unroll
-        for (int l = 1; l <= L; ++l)
-          rad[u][l - 1] = __ldg(reinterpret_cast<const float4*>(rr + l * C));
-#pragma unroll
-        for (int r = 0; r < R; ++r) z[u][r] = __ldg(a.zonal + e * R + r);
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int l = 1; l <= L; ++l)
+        for (int l = 1; l <= L; ++l) {
+          const float4 q = ld_stream_f4(rr + l * C);
 #pragma unroll
           for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
-            acc[r][0] = fmaf(z[u][r], rad[u][l - 1].x, acc[r][0]);
-            acc[r][1] = fmaf(z[u][r], rad[u][l - 1].y, acc[r][1]);
-            acc[r][2] = fmaf(z[u][r], rad[u][l - 1].z, acc[r][2]);
-            acc[r][3] = fmaf(z[u][r], rad[u][l - 1].w, acc[r][3]);
+            const float zr = z[r];
+            acc[r][0] = fmaf(zr, q.x, acc[r][0]);
+            acc[r][1] = fmaf(zr, q.y, acc[r][1]);
+            acc[r][2] = fmaf(zr, q.z, acc[r][2]);
+            acc[r][3] = fmaf(zr, q.w, acc[r][3]);
           }
-    }
-    if (s < cur.hi) {
-      const int64_t e = a.order ? __ldg(a.order + s) : s;
-      const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
-#pragma unroll
-      for (int l = 1; l <= L; ++l) {
-        const float4 q = __ldg(reinterpret_cast<const float4*>(rr + l * C));
-#pragma unroll
-        for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
-          const float z = __ldg(a.zonal + e * R + r);
-          acc[r][0] = fmaf(z, q.x, acc[r][0]);
-          acc[r][1] = fmaf(z, q.y, acc[r][1]);
-          acc[r][2] = fmaf(z, q.z, acc[r][2]);
-          acc[r][3] = fmaf(z, q.w, acc[r][3]);
         }
       }
     }
