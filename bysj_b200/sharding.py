@@ -28,6 +28,7 @@ on CPU (where the reduce-scatter is an all-reduce and a slice).
 """
 from __future__ import annotations
 
+from contextlib import nullcontext
 from dataclasses import dataclass
 from typing import Callable
 
@@ -165,13 +166,15 @@ class ForceExchange:
 
     ``start`` launches the source-partial kernel and the reduce-scatter
     (asynchronous on NCCL); ``finish`` waits for it and adds the local
-    destination sums.  Anything launched between the two on the current
-    stream (e.g. the local attention kernel) overlaps the exchange.
+    destination sums.  On CUDA the whole exchange runs on a side stream that
+    first waits for the caller's stream, so the kernels the caller launches
+    between ``start`` and ``finish`` (e.g. the local attention) overlap all of
+    it; ``finish`` makes the caller's stream wait for the side stream again.
     """
 
     def __init__(self, part: DstPartition, *, src_partial: Callable | None = None,
                  dst_add: Callable | None = None, combine: Callable | None = None,
-                 group=None):
+                 group=None, side_stream: bool = True):
         if src_partial is None or dst_add is None:
             from ._C import force_assembly_dst_add, force_assembly_src_partial
 
@@ -179,30 +182,53 @@ class ForceExchange:
             dst_add = dst_add or force_assembly_dst_add
         self.part, self.group = part, group
         self._src_partial, self._dst_add, self._combine = src_partial, dst_add, combine
+        self._use_side = side_stream
+        self._side = None
         self._pending = None
+
+    def _stream_for(self, tensor: torch.Tensor):
+        if not (self._use_side and tensor.is_cuda):
+            return None
+        if self._side is None or self._side.device != tensor.device:
+            self._side = torch.cuda.Stream(device=tensor.device)
+        return self._side
 
     def start(self, grad_edge: torch.Tensor, edge_vec: torch.Tensor) -> None:
         """``grad_edge`` / ``edge_vec``: this rank's edges, ``[E_local, 3]`` fp32."""
         if self._pending is not None:
             raise RuntimeError("ForceExchange.start called twice without finish")
         p = self.part
-        partial = self._src_partial(grad_edge, edge_vec, p.src_offsets, p.src_order)
-        if self._combine is not None:
-            block, work = self._combine(partial, p), None
-        else:
-            block, work = reduce_scatter_sum(partial, p, self.group, async_op=True)
-        self._pending = (grad_edge, partial, block, work)
+        side = self._stream_for(grad_edge)
+        main = torch.cuda.current_stream(grad_edge.device) if side is not None else None
+        if side is not None:
+            side.wait_stream(main)
+        with torch.cuda.stream(side) if side is not None else nullcontext():
+            partial = self._src_partial(grad_edge, edge_vec, p.src_offsets, p.src_order)
+            if self._combine is not None:
+                block, work = self._combine(partial, p), None
+            else:
+                block, work = reduce_scatter_sum(partial, p, self.group, async_op=True)
+        if side is not None:
+            for t in (grad_edge, edge_vec, p.src_offsets, p.src_order, p.dst_offsets):
+                t.record_stream(side)
+        self._pending = (grad_edge, partial, block, work, side, main)
 
     def finish(self):
         """``(force [n_local, 3], virial [n_local, 9])`` of this rank's atoms."""
         if self._pending is None:
             raise RuntimeError("ForceExchange.finish called before start")
-        grad_edge, _partial, block, work = self._pending
+        grad_edge, _partial, block, work, side, main = self._pending
         self._pending = None
-        if work is not None:
-            work.wait()
         p = self.part
-        return self._dst_add(grad_edge, p.dst_offsets, block[:p.n_local])
+        with torch.cuda.stream(side) if side is not None else nullcontext():
+            if work is not None:
+                work.wait()
+            force, virial = self._dst_add(grad_edge, p.dst_offsets, block[:p.n_local])
+        if side is not None:
+            main.wait_stream(side)
+            force.record_stream(main)
+            virial.record_stream(main)
+        return force, virial
 
 
 def force_assembly_partitioned(grad_edge: torch.Tensor, edge_vec: torch.Tensor,
