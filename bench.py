@@ -425,6 +425,71 @@ def _op_rmsnorm(ctx, dtype):
                    {"rows": n * 16, "note": "per-degree weights [4,128], L2 flushed"})
 
 
+def _op_segment_sum_bwd(ctx):
+    from bysj_b200 import _C
+
+    g, e, n = ctx["g"], ctx["g"].n_edges, ctx["g"].n_atoms
+    device = ctx["device"]
+    src = ctx["value32"]().reshape(e, -1)
+    ws = torch.rand(e, device=device) + 0.5
+    ns = torch.rand(n, device=device) + 0.5
+    grad = torch.randn(n, src.shape[1], device=device)
+    t = time_launches(lambda: _C.segment_sum_backward(grad, src, g.dst, ctx["offsets"], ws, ns,
+                                                      True), ctx["iters"])
+    c = src.shape[1] * 4
+    return op_line("segment_sum_bwd_c1024", e * (2 * c + 4) + n * (c + 8) + 8 * (n + 1), t,
+                   ctx["peak"], e, {"note": "grad_src and grad_node_scale"})
+
+
+def _op_softmax_bwd(ctx):
+    from bysj_b200 import _C
+
+    e, n = ctx["g"].n_edges, ctx["g"].n_atoms
+    env = torch.rand(e, device=ctx["device"]) * 0.9 + 0.1
+    alpha, _ = _C.segment_softmax_forward(ctx["logit"](), env, ctx["offsets"])
+    grad = torch.randn_like(alpha)
+    t = time_launches(lambda: _C.segment_softmax_backward(alpha, grad, env, ctx["offsets"]),
+                      ctx["iters"], ctx["flush"])
+    return op_line("segment_softmax_bwd_h8", e * (32 * 3 + 4 + 4) + 8 * (n + 1), t, ctx["peak"],
+                   e, {"note": "grad_logit and grad_env, L2 flushed"})
+
+
+def _op_rmsnorm_bwd(ctx):
+    from bysj_b200 import _C
+
+    n = ctx["g"].n_atoms
+    device = ctx["device"]
+    x = torch.randn(n, 16, 128, device=device)
+    w = torch.rand(128, device=device) + 0.5
+    y, inv = _C.rmsnorm_forward(x, w, 1e-6)
+    grad = torch.randn_like(x)
+    t = time_launches(lambda: _C.rmsnorm_backward(grad, x, w, inv, True), ctx["iters"],
+                      ctx["flush"])
+    rows = n * 16
+    return op_line("rmsnorm_bwd_f32", rows * (3 * 512 + 4) + 2 * 512, t, ctx["peak"], None,
+                   {"rows": rows, "note": "gx and grad_scale, L2 flushed"})
+
+
+def _op_zonal_bwd(ctx):
+    from bysj_b200 import _C
+    from bysj_b200 import workloads as W
+
+    g, e, n = ctx["g"], ctx["g"].n_edges, ctx["g"].n_atoms
+    device = ctx["device"]
+    gen = torch.Generator(device=device).manual_seed(98)
+    zonal = W.real_sph_zonal(g.unit)
+    radial = torch.randn(e, 4, 64, device=device, generator=gen)
+    slot = W.degree_slots().to(device)
+    inv = torch.rsqrt(torch.bincount(g.dst, minlength=n).float() + 1.0)
+    grad = torch.randn(n, 16, 64, device=device, generator=gen)
+    t = time_launches(lambda: _C.gie_zonal_scatter_backward(grad, zonal, radial, g.dst, slot,
+                                                            inv), ctx["iters"])
+    return op_line("zonal_scatter_bwd", e * (60 + 8 + 768 + 60 + 1024) + n * (4096 + 8), t,
+                   ctx["peak"], e,
+                   {"note": "grad_zonal, grad_radial (all 4 slots written), grad_inv; includes "
+                            "the device CSR view of dst"})
+
+
 OPS = {
     "offsets": _op_offsets,
     "group": _op_group,
@@ -436,6 +501,10 @@ OPS = {
     "zonal": _op_zonal,
     "rmsnorm": lambda ctx: _op_rmsnorm(ctx, torch.float32),
     "rmsnorm_bf16": lambda ctx: _op_rmsnorm(ctx, torch.bfloat16),
+    "segment_sum_bwd": _op_segment_sum_bwd,
+    "softmax_bwd": _op_softmax_bwd,
+    "rmsnorm_bwd": _op_rmsnorm_bwd,
+    "zonal_bwd": _op_zonal_bwd,
 }
 
 

@@ -292,6 +292,165 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
   }
 }
 
+// Backward for the degree row layout (C = 4 LPE, LPE <= 16 lanes per edge,
+// EG = 32 / LPE edges side by side).  With gi = g[n, 1:] * inv[n]:
+//   grad_radial[e, base + l, c] = sum_{r of degree l} gi[r, c] zonal[e, r]
+//   grad_radial[e, other slots, c] = 0
+//   grad_zonal[e, r] = sum_c gi[r, c] radial[e, base + l(r), c]
+//   grad_inv[n] = <g[n, 1:], pre[n]>,  pre[n, r, c] = sum_e zonal[e, r] radial[e, base + l(r), c]
+// Per warp, shared memory holds gi of the current segment (R x C floats),
+// the zonal rows of 32 edges, and a 32 x 17 tile through which each lane's
+// 4-channel share of grad_zonal is summed over the LPE lanes of its edge (in
+// lane order).  pre is summed over all the segment's edges (edge groups
+// merged, split pieces combined) before the single dot product, as the
+// forward normalises after its sum.
+constexpr int kTilePitch = 17;  // floats per lane row of the fold tile
+
+template <int LPE, int L>
+struct GieBwdSmem {
+  static constexpr int R = (L + 1) * (L + 1) - 1;
+  static constexpr size_t kG = sizeof(float4) * R * LPE;
+  static constexpr size_t kZ = sizeof(float) * kZonalChunk * R;
+  static constexpr size_t kT = sizeof(float) * kWarp * kTilePitch;
+  static constexpr size_t kWarpBytes = (kG + kZ + kT + 15) / 16 * 16;
+};
+
+template <int LPE, int L>
+__global__ void __launch_bounds__(kBlock, 2)
+    gie_bwd_degree_kernel(GieArgs a, int64_t slot_base) {
+  using M = GieBwdSmem<LPE, L>;
+  constexpr int R = M::R;
+  constexpr int EG = kWarp / LPE;
+  static_assert(LPE <= 16 && R <= 16, "degree backward needs C <= 64 and L <= 3");
+  extern __shared__ float4 gie_bwd_smem[];
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  char* mine_smem = reinterpret_cast<char*>(gie_bwd_smem) + (threadIdx.x >> 5) * M::kWarpBytes;
+  float4* gq = reinterpret_cast<float4*>(mine_smem);
+  float* zb = reinterpret_cast<float*>(mine_smem + M::kG);
+  float* tile = reinterpret_cast<float*>(mine_smem + M::kG + M::kZ);
+  const int lane = lane_id();
+  const int eg = lane / LPE;
+  const int c4 = lane % LPE;
+  const int64_t C = a.channels;
+  const int64_t block = (R + 1) * C;
+  const int64_t radial_row = a.n_radial * C;
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const float inv = __ldg(a.inv + n);
+    const float4* gn = reinterpret_cast<const float4*>(a.grad + n * block + C);  // rows 1..R
+    __syncwarp();  // the previous piece's reads of gq are done
+    for (int i = lane; i < R * LPE; i += kWarp) {
+      const float4 v = __ldg(gn + i);
+      gq[i] = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+    }
+    float acc[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+    for (int64_t lo = cur.lo; lo < cur.hi; lo += kZonalChunk) {  // warp-uniform
+      const int rows = static_cast<int>(cur.hi - lo < kZonalChunk ? cur.hi - lo : kZonalChunk);
+      __syncwarp();
+      if (a.order == nullptr) {
+        const float* src = a.zonal + lo * R;
+        for (int i = lane; i < rows * R; i += kWarp) zb[i] = __ldg(src + i);
+      } else {
+        for (int i = lane; i < rows * R; i += kWarp) {
+          const int k = i / R;
+          zb[i] = __ldg(a.zonal + __ldg(a.order + lo + k) * R + (i - k * R));
+        }
+      }
+      __syncwarp();
+      for (int k0 = 0; k0 < rows; k0 += EG) {  // warp-uniform
+        const int k = k0 + eg;
+        const bool valid = k < rows;
+        const int kk = valid ? k : 0;
+        const int64_t slot = lo + kk;
+        const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+        const float* rr = a.radial + e * radial_row + 4 * c4;
+        const float* z = zb + kk * R;
+#pragma unroll
+        for (int l = 1; l <= L; ++l) {
+          const float4 q = ld_stream_f4(rr + (slot_base + l) * C);
+          float4 gr = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+          for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
+            const float zr = valid ? z[r] : 0.0f;
+            const float4 g = gq[r * LPE + c4];
+            acc[r][0] = fmaf(zr, q.x, acc[r][0]);
+            acc[r][1] = fmaf(zr, q.y, acc[r][1]);
+            acc[r][2] = fmaf(zr, q.z, acc[r][2]);
+            acc[r][3] = fmaf(zr, q.w, acc[r][3]);
+            tile[lane * kTilePitch + r] = fmaf(g.x, q.x, fmaf(g.y, q.y, fmaf(g.z, q.z, g.w * q.w)));
+            gr.x = fmaf(g.x, zr, gr.x);
+            gr.y = fmaf(g.y, zr, gr.y);
+            gr.z = fmaf(g.z, zr, gr.z);
+            gr.w = fmaf(g.w, zr, gr.w);
+          }
+          if (valid)
+            reinterpret_cast<float4*>(a.grad_radial + e * radial_row + (slot_base + l) * C)[c4] =
+                gr;
+        }
+        if (valid) {
+          for (int64_t sl = 0; sl < a.n_radial; ++sl) {
+            if (sl >= slot_base + 1 && sl <= slot_base + L) continue;
+            reinterpret_cast<float4*>(a.grad_radial + e * radial_row + sl * C)[c4] =
+                make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          }
+        }
+        __syncwarp();
+        if (valid) {
+          for (int r = c4; r < R; r += LPE) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int t = 0; t < LPE; ++t) sum += tile[(eg * LPE + t) * kTilePitch + r];
+            a.grad_zonal[e * R + r] = sum;
+          }
+        }
+        __syncwarp();  // the tile is read before the next edge overwrites it
+      }
+    }
+    if constexpr (EG > 1) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[r][i] = xor_sum(acc[r][i], LPE);
+    }
+    if (cur.kind != kWhole) {
+      float* mine = a.ss.slot(p, cur.kind);
+      if (eg == 0) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) store_cg<4>(mine + r * C + 4 * c4, acc[r]);
+      }
+      const int64_t first = a.mp.part_of_first_edge(n);
+      const int64_t last = a.mp.part_of_end(n);
+      if (!arrive_last(a.ss, first, last, 0)) continue;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int64_t q = first; q <= last; ++q) {
+          float piece[4];
+          load_cg<4>(a.ss.slot(q, q == last ? kHead : kTail) + r * C + 4 * c4, piece);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sum[i] += piece[i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[r][i] = sum[i];
+      }
+    }
+    float dot = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float4 g = __ldg(gn + r * LPE + c4);
+      dot = fmaf(g.x, acc[r][0], fmaf(g.y, acc[r][1], fmaf(g.z, acc[r][2], fmaf(g.w, acc[r][3], dot))));
+    }
+    if constexpr (LPE > 1) dot = group_sum(dot, LPE);
+    if (lane == 0) a.out[n] = dot;
+  }
+}
+
 // Backward.  Per edge, with gi = g[n] * inv[n] (g rows are re-read from L1):
 //   grad_zonal[e, r]     = sum_c gi[r, c] * radial[e, slot r, c]
 //   grad_radial[e, s, c] = sum_{r: slot r = s} gi[r, c] * zonal[e, r]
@@ -456,7 +615,17 @@ GieLayout gie_layout(bool vec_ok, int64_t n_edges, int64_t n_nodes,
 using GieDegreeKernel = void (*)(GieArgs, int64_t);
 
 template <int L>
-GieDegreeKernel gie_degree_pick(int64_t lpe) {
+GieDegreeKernel gie_degree_pick(int64_t lpe, bool backward) {
+  if (backward) {
+    switch (lpe) {
+      case 1: return gie_bwd_degree_kernel<1, L>;
+      case 2: return gie_bwd_degree_kernel<2, L>;
+      case 4: return gie_bwd_degree_kernel<4, L>;
+      case 8: return gie_bwd_degree_kernel<8, L>;
+      case 16: return gie_bwd_degree_kernel<16, L>;
+      default: return nullptr;
+    }
+  }
   switch (lpe) {
     case 1: return gie_fwd_degree_kernel<1, L>;
     case 2: return gie_fwd_degree_kernel<2, L>;
@@ -468,13 +637,13 @@ GieDegreeKernel gie_degree_pick(int64_t lpe) {
   }
 }
 
-GieDegreeKernel gie_degree_kernel(int64_t degrees, int64_t channels) {
+GieDegreeKernel gie_degree_kernel(int64_t degrees, int64_t channels, bool backward) {
   if (channels % 4 != 0) return nullptr;
   const int64_t lpe = channels / 4;
   switch (degrees) {
-    case 1: return gie_degree_pick<1>(lpe);
-    case 2: return gie_degree_pick<2>(lpe);
-    case 3: return gie_degree_pick<3>(lpe);
+    case 1: return gie_degree_pick<1>(lpe, backward);
+    case 2: return gie_degree_pick<2>(lpe, backward);
+    case 3: return gie_degree_pick<3>(lpe, backward);
     default: return nullptr;
   }
 }
@@ -483,18 +652,42 @@ struct GieDegreeLayout {
   GieDegreeKernel kernel = nullptr;
   PartitionPlan plan;
   size_t bytes = 0;
+  size_t smem = 0;  // dynamic shared memory per CTA (backward)
+  int smem_status = BYSJ_OK;
   SplitSlots ss{};
 };
 
+template <int L>
+size_t gie_bwd_smem_bytes(int64_t lpe) {
+  switch (lpe) {
+    case 1: return kWarpsPerBlock * GieBwdSmem<1, L>::kWarpBytes;
+    case 2: return kWarpsPerBlock * GieBwdSmem<2, L>::kWarpBytes;
+    case 4: return kWarpsPerBlock * GieBwdSmem<4, L>::kWarpBytes;
+    case 8: return kWarpsPerBlock * GieBwdSmem<8, L>::kWarpBytes;
+    default: return kWarpsPerBlock * GieBwdSmem<16, L>::kWarpBytes;
+  }
+}
+
+size_t gie_bwd_smem_size(int64_t degrees, int64_t channels) {
+  const int64_t lpe = channels / 4;
+  if (degrees == 1) return gie_bwd_smem_bytes<1>(lpe);
+  if (degrees == 2) return gie_bwd_smem_bytes<2>(lpe);
+  return gie_bwd_smem_bytes<3>(lpe);
+}
+
 GieDegreeLayout gie_degree_layout(int64_t n_edges, int64_t n_nodes, int64_t degrees,
-                                  int64_t channels, void* ws) {
+                                  int64_t channels, void* ws, bool backward = false) {
   GieDegreeLayout L;
-  L.kernel = gie_degree_kernel(degrees, channels);
+  L.kernel = gie_degree_kernel(degrees, channels, backward);
   if (L.kernel == nullptr) return L;
   const int64_t rows = (degrees + 1) * (degrees + 1) - 1;
+  if (backward) {
+    L.smem = gie_bwd_smem_size(degrees, channels);
+    L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.kernel), L.smem);
+  }
   const DeviceInfo& dev = current_device_info();
   const int64_t resident = static_cast<int64_t>(dev.sm_count) *
-                           resident_blocks(reinterpret_cast<const void*>(L.kernel)) *
+                           resident_blocks(reinterpret_cast<const void*>(L.kernel), L.smem) *
                            kWarpsPerBlock;
   L.plan = plan_partitions(n_edges, n_nodes, resident, 16);
   const int64_t stride = (rows * channels + 7) / 8 * 8;
@@ -714,6 +907,66 @@ int bysj_gie_zonal_scatter_backward(
   const size_t smem = sizeof(float) * kBlock * L.cfg.nv;
   L.cfg.kernel<<<L.plan.blocks, kBlock, smem, s>>>(a);
   return launch_check("gie_bwd_kernel");
+}
+
+size_t bysj_gie_zonal_scatter_backward_degree_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                                             int64_t degrees, int64_t channels) {
+  if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
+  return gie_degree_layout(n_edges, n_nodes, degrees, channels, nullptr, true).bytes;
+}
+
+int bysj_gie_zonal_scatter_backward_degree(
+    const float* grad_out, const float* zonal, const float* radial, const int64_t* offsets,
+    const int64_t* order, int64_t slot_base, const float* inv_sqrt_deg, int64_t n_edges,
+    int64_t n_nodes, int64_t degrees, int64_t n_radial, int64_t channels, float* grad_zonal,
+    float* grad_radial, float* grad_inv, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  const int64_t rows = (degrees + 1) * (degrees + 1) - 1;
+  int st = gie_check(n_edges, n_nodes, rows, n_radial, channels);
+  if (st) return st;
+  if (degrees < 1 || degrees > 3 || channels % 4 != 0 || channels > 64 ||
+      (channels / 4 & (channels / 4 - 1)) != 0)
+    return fail(BYSJ_ERR_UNSUPPORTED,
+                "zonal scatter backward (degree rows): needs 1..3 degrees and channels = "
+                "4 * 2^k <= 64");
+  if (slot_base < -1 || slot_base + degrees > n_radial - 1)
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "zonal scatter backward (degree rows): slots out of range");
+  if (n_nodes == 0) return BYSJ_OK;
+  if (grad_inv == nullptr || inv_sqrt_deg == nullptr || offsets == nullptr || grad_out == nullptr ||
+      (n_edges > 0 && (zonal == nullptr || radial == nullptr || grad_zonal == nullptr ||
+                       grad_radial == nullptr)))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter backward (degree rows): NULL pointer");
+  if (!aligned16(radial) || !aligned16(grad_out) || !aligned16(grad_radial))
+    return fail(BYSJ_ERR_INVALID_ARGUMENT,
+                "zonal scatter backward (degree rows): radial, grad_out and grad_radial must be "
+                "16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  GieDegreeLayout L = gie_degree_layout(n_edges, n_nodes, degrees, channels, workspace, true);
+  if (workspace == nullptr || workspace_bytes < L.bytes)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "zonal scatter backward (degree rows): workspace of %zu bytes needed, %zu given",
+                L.bytes, workspace_bytes);
+  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts, s),
+                  "zonal scatter backward (degree rows): ticket reset");
+  if (st) return st;
+  GieArgs a{};
+  a.zonal = zonal;
+  a.radial = radial;
+  a.order = order;
+  a.inv = inv_sqrt_deg;
+  a.grad = grad_out;
+  a.out = grad_inv;
+  a.grad_zonal = grad_zonal;
+  a.grad_radial = grad_radial;
+  a.rows = rows;
+  a.n_radial = n_radial;
+  a.channels = channels;
+  a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
+  a.ss = L.ss;
+  if (L.smem_status != BYSJ_OK) return L.smem_status;
+  L.kernel<<<L.plan.blocks, kBlock, L.smem, s>>>(a, slot_base);
+  return launch_check("gie_bwd_degree_kernel");
 }
 
 }  // extern "C"

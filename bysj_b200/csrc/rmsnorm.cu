@@ -230,6 +230,113 @@ __global__ void __launch_bounds__(kBlock)
   }
 }
 
+// Vectorised backward for rows of 4 K floats (K = 32 NV lanes x 4), at most
+// kBwdMaxDegrees weight rows: one pass over g and x.  A warp takes R rows at a
+// time (16-byte loads for all of them issued first), writes gx, and keeps
+// its share of grad_scale per weight row in registers; the warps' partials
+// land in partial[warp][l][c] and are summed in warp order afterwards.
+constexpr int kBwdMaxDegrees = 4;
+
+template <int NV, int R>
+__global__ void __launch_bounds__(kBlock)
+    rmsnorm_bwd_vec_kernel(const float* __restrict__ grad, const float* __restrict__ x,
+                           const float* __restrict__ scale, int64_t scale_rows, int64_t comps,
+                           const float* __restrict__ inv_rms, int64_t rows, int64_t width,
+                           float* __restrict__ grad_x, float* __restrict__ partial) {
+  const int lane = lane_id();
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
+  const int64_t w = global_warp();
+  const float inv_width = 1.0f / static_cast<float>(width);
+  float acc[kBwdMaxDegrees][NV][4];
+#pragma unroll
+  for (int l = 0; l < kBwdMaxDegrees; ++l)
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[l][k][i] = 0.0f;
+  for (int64_t r0 = w * R; r0 < rows; r0 += warps * R) {
+    float4 gv[R][NV], xv[R][NV];
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+      const int64_t r = r0 + rr < rows ? r0 + rr : rows - 1;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int64_t c = 4 * (lane + kWarp * k);
+        gv[rr][k] = ld_stream_f4(grad + r * width + c);
+        xv[rr][k] = ld_stream_f4(x + r * width + c);
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+      const int64_t r = r0 + rr;
+      if (r >= rows) break;  // warp-uniform
+      const int l = scale_rows > 1 ? static_cast<int>(degree_of_row(r, comps)) : 0;
+      float4 wv[NV];
+#pragma unroll
+      for (int k = 0; k < NV; ++k)
+        wv[k] = scale ? __ldg(reinterpret_cast<const float4*>(scale + l * width) + lane + kWarp * k)
+                      : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      float dot = 0.0f;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        dot = fmaf(xv[rr][k].x, gv[rr][k].x * wv[k].x, dot);
+        dot = fmaf(xv[rr][k].y, gv[rr][k].y * wv[k].y, dot);
+        dot = fmaf(xv[rr][k].z, gv[rr][k].z * wv[k].z, dot);
+        dot = fmaf(xv[rr][k].w, gv[rr][k].w * wv[k].w, dot);
+      }
+      dot = xor_sum(dot, 1);
+      const float inv = __ldg(inv_rms + r);
+      const float coef = inv * inv * inv * (dot * inv_width);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int64_t c = 4 * (lane + kWarp * k);
+        const float4 g4 = gv[rr][k], x4 = xv[rr][k], w4 = wv[k];
+        *reinterpret_cast<float4*>(grad_x + r * width + c) =
+            make_float4(inv * (g4.x * w4.x) - x4.x * coef, inv * (g4.y * w4.y) - x4.y * coef,
+                        inv * (g4.z * w4.z) - x4.z * coef, inv * (g4.w * w4.w) - x4.w * coef);
+        if (partial) {
+#pragma unroll
+          for (int ll = 0; ll < kBwdMaxDegrees; ++ll) {
+            if (ll != l) continue;
+            acc[ll][k][0] = fmaf(g4.x * x4.x, inv, acc[ll][k][0]);
+            acc[ll][k][1] = fmaf(g4.y * x4.y, inv, acc[ll][k][1]);
+            acc[ll][k][2] = fmaf(g4.z * x4.z, inv, acc[ll][k][2]);
+            acc[ll][k][3] = fmaf(g4.w * x4.w, inv, acc[ll][k][3]);
+          }
+        }
+      }
+    }
+  }
+  if (partial) {
+    // Fold the CTA's warps in warp order through shared memory; one partial
+    // per CTA: partial[block][l][c].
+    __shared__ float4 fold[kWarpsPerBlock][kBwdMaxDegrees][2 * kWarp];
+    const int64_t srows = scale_rows > 0 ? scale_rows : 1;
+    const int warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int l = 0; l < kBwdMaxDegrees; ++l)
+#pragma unroll
+      for (int k = 0; k < NV; ++k)
+        fold[warp][l][lane + kWarp * k] =
+            make_float4(acc[l][k][0], acc[l][k][1], acc[l][k][2], acc[l][k][3]);
+    __syncthreads();
+    const int cols4 = static_cast<int>(width / 4);
+    for (int i = threadIdx.x; i < srows * cols4; i += blockDim.x) {
+      const int l = i / cols4;
+      const int c4 = i - l * cols4;
+      float4 sum = fold[0][l][c4];
+      for (int ww = 1; ww < kWarpsPerBlock; ++ww) {
+        const float4 v = fold[ww][l][c4];
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      *reinterpret_cast<float4*>(partial + (blockIdx.x * srows + l) * width + 4 * c4) = sum;
+    }
+  }
+}
+
 // Stage 1 of grad_scale: partial[chunk, l, c] = sum over the chunk's rows of
 // weight row l of g*x*inv.  Threads own columns; rows are visited in order.
 __global__ void __launch_bounds__(kBlock)
@@ -257,16 +364,39 @@ __global__ void __launch_bounds__(kBlock)
   }
 }
 
-// Stage 2: grad_scale[l, c] = sum_chunk partial[chunk, l, c] in chunk order.
+// Stage 2: grad_scale[cell] = sum over k of partial[k, cell], in a fixed
+// order: a CTA takes 32 cells; thread group g (8 groups) sums k = g, g+8, ...
+// into four interleaved accumulators (k / 8 mod 4), which are added in
+// order, and the 8 group sums are added in group order.
 __global__ void __launch_bounds__(kBlock)
     rmsnorm_scale_reduce_kernel(const float* __restrict__ partial,
                                 int64_t chunks, int64_t cells,
                                 float* __restrict__ grad_scale) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= cells) return;
-  float acc = 0.0f;
-  for (int64_t k = 0; k < chunks; ++k) acc += __ldcg(partial + k * cells + i);
-  grad_scale[i] = acc;
+  __shared__ float groups[kWarpsPerBlock][kWarp];
+  const int g = threadIdx.x >> 5;
+  const int64_t cell = static_cast<int64_t>(blockIdx.x) * kWarp + lane_id();
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (cell < cells) {
+    int64_t k = g;
+    for (; k + 3 * kWarpsPerBlock < chunks; k += 4 * kWarpsPerBlock) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] += __ldcg(partial + (k + j * kWarpsPerBlock) * cells + cell);
+    }
+    for (int j = 0; k < chunks; k += kWarpsPerBlock, ++j)
+      acc[j & 3] += __ldcg(partial + k * cells + cell);
+  }
+  groups[g][lane_id()] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  __syncthreads();
+  if (g == 0 && cell < cells) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kWarpsPerBlock; ++j) sum += groups[j][lane_id()];
+    grad_scale[cell] = sum;
+  }
+}
+
+unsigned reduce_blocks(int64_t cells) {
+  return static_cast<unsigned>((cells + kWarp - 1) / kWarp);
 }
 
 using NormKernel = void (*)(NormArgs);
@@ -384,6 +514,20 @@ int bysj_rmsnorm_forward(const void* x, int dtype, int64_t rows, int64_t width,
   return launch_check("rmsnorm_fwd_kernel");
 }
 
+// Warps of the vectorised backward: one wave of resident warps.
+int64_t bwd_vec_warps(int64_t rows) {
+  const int64_t per_block = static_cast<int64_t>(kWarpsPerBlock) * 4;
+  int64_t blocks = (rows + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(current_device_info().sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return blocks * kWarpsPerBlock;
+}
+
+bool bwd_vec_shape(int64_t width, int64_t scale_rows) {
+  return width % 128 == 0 && width <= 256 && scale_rows <= kBwdMaxDegrees;
+}
+
 size_t bysj_rmsnorm_backward_workspace_size(int64_t rows, int64_t width,
                                             int64_t scale_rows) {
   if (rows <= 0 || width <= 0 || scale_rows < 1) return 0;
@@ -391,7 +535,14 @@ size_t bysj_rmsnorm_backward_workspace_size(int64_t rows, int64_t width,
   const int64_t chunks = (rows + chunk_rows - 1) / chunk_rows;
   Carver carve(nullptr);
   carve.take<float>(static_cast<size_t>(chunks) * scale_rows * width);
-  return carve.need;
+  size_t need = carve.need;
+  if (bwd_vec_shape(width, scale_rows)) {
+    Carver vec(nullptr);
+    vec.take<float>(static_cast<size_t>(bwd_vec_warps(rows) / kWarpsPerBlock) * scale_rows *
+                    width);
+    if (vec.need > need) need = vec.need;
+  }
+  return need;
 }
 
 int bysj_rmsnorm_backward(const float* grad_out, const float* x,
@@ -422,6 +573,34 @@ int bysj_rmsnorm_backward(const float* grad_out, const float* x,
   }
   if (grad_out == nullptr || x == nullptr || inv_rms == nullptr || grad_x == nullptr)
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "rmsnorm backward: NULL pointer");
+  const bool vec = bwd_vec_shape(width, scale_rows) && aligned16(grad_out) && aligned16(x) &&
+                   aligned16(grad_x) && (scale == nullptr || aligned16(scale));
+  if (vec) {
+    const int64_t warps = bwd_vec_warps(rows);
+    const int64_t vec_blocks = warps / kWarpsPerBlock;
+    float* partial = nullptr;
+    if (grad_scale != nullptr) {
+      Carver carve(workspace);
+      partial = carve.take<float>(static_cast<size_t>(vec_blocks) * scale_rows * width);
+      if (workspace == nullptr || workspace_bytes < carve.need)
+        return fail(BYSJ_ERR_WORKSPACE,
+                    "rmsnorm backward: workspace of %zu bytes needed, %zu given", carve.need,
+                    workspace_bytes);
+    }
+    const unsigned blocks = static_cast<unsigned>(warps / kWarpsPerBlock);
+    if (width == 128)
+      rmsnorm_bwd_vec_kernel<1, 4><<<blocks, kBlock, 0, s>>>(
+          grad_out, x, scale, scale_rows, comps, inv_rms, rows, width, grad_x, partial);
+    else
+      rmsnorm_bwd_vec_kernel<2, 2><<<blocks, kBlock, 0, s>>>(
+          grad_out, x, scale, scale_rows, comps, inv_rms, rows, width, grad_x, partial);
+    int st = launch_check("rmsnorm_bwd_vec_kernel");
+    if (st || grad_scale == nullptr) return st;
+    const int64_t cells = scale_rows * width;
+    rmsnorm_scale_reduce_kernel<<<reduce_blocks(cells), kBlock, 0, s>>>(partial, vec_blocks,
+                                                                       cells, grad_scale);
+    return launch_check("rmsnorm_scale_reduce_kernel");
+  }
   const DeviceInfo& dev = current_device_info();
   int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
   const int64_t cap = static_cast<int64_t>(dev.sm_count) * 8;
@@ -448,8 +627,8 @@ int bysj_rmsnorm_backward(const float* grad_out, const float* x,
   st = launch_check("rmsnorm_scale_partial_kernel");
   if (st) return st;
   const int64_t cells = scale_rows * width;
-  rmsnorm_scale_reduce_kernel<<<static_cast<unsigned>((cells + kBlock - 1) / kBlock),
-                                kBlock, 0, s>>>(partial, chunks, cells, grad_scale);
+  rmsnorm_scale_reduce_kernel<<<reduce_blocks(cells), kBlock, 0, s>>>(partial, chunks, cells,
+                                                                     grad_scale);
   return launch_check("rmsnorm_scale_reduce_kernel");
 }
 

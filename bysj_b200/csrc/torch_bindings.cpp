@@ -562,6 +562,24 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
   Tensor gi = torch::empty_like(inv_sqrt_deg);
   if (nodes == 0) return {gz, gr, gi};
   auto [offsets, order] = csr_view(dst, nodes);
+  const int64_t degrees = degree_layout(radial_slot, rows, n_radial);
+  if (degrees > 0 && channels % 4 == 0 && channels <= 64 &&
+      ((channels / 4) & (channels / 4 - 1)) == 0 &&
+      reinterpret_cast<uintptr_t>(radial.data_ptr()) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(grad_output.data_ptr()) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(gr.data_ptr()) % 16 == 0) {
+    const int64_t base = radial_slot.index({0}).item<int64_t>() - 1;
+    Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_degree_workspace_size(
+                                     edges, nodes, degrees, channels));
+    check(bysj_gie_zonal_scatter_backward_degree(
+              grad_output.data_ptr<float>(), zonal.data_ptr<float>(), radial.data_ptr<float>(),
+              offsets.data_ptr<int64_t>(), opt_ptr<int64_t>(order), base,
+              inv_sqrt_deg.data_ptr<float>(), edges, nodes, degrees, n_radial, channels,
+              gz.data_ptr<float>(), gr.data_ptr<float>(), gi.data_ptr<float>(), ws.data_ptr(),
+              static_cast<size_t>(ws.numel()), stream_of(zonal)),
+          "gie_zonal_scatter_backward");
+    return {gz, gr, gi};
+  }
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_workspace_size(edges, nodes, rows,
                                                                               channels));
   check(bysj_gie_zonal_scatter_backward(

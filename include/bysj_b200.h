@@ -324,6 +324,21 @@ BYSJ_API int bysj_gie_zonal_scatter_forward_degree(
     int64_t channels, float* out, void* workspace, size_t workspace_bytes,
     void* stream);
 
+/* Backward of bysj_gie_zonal_scatter_forward_degree (same row layout; see
+ * bysj_gie_zonal_scatter_backward for the gradients).  channels = 4 * 2^k
+ * <= 64; radial, grad_out and grad_radial 16-byte aligned; grad_radial's
+ * slots that no row reads are written as zeros.  No reference counterpart:
+ * the degree-specialised form of csrc/gie.cpp:170-228. */
+BYSJ_API size_t bysj_gie_zonal_scatter_backward_degree_workspace_size(int64_t n_edges,
+                                                                      int64_t n_nodes,
+                                                                      int64_t degrees,
+                                                                      int64_t channels);
+BYSJ_API int bysj_gie_zonal_scatter_backward_degree(
+    const float* grad_out, const float* zonal, const float* radial, const int64_t* offsets,
+    const int64_t* order, int64_t slot_base, const float* inv_sqrt_deg, int64_t n_edges,
+    int64_t n_nodes, int64_t degrees, int64_t n_radial, int64_t channels, float* grad_zonal,
+    float* grad_radial, float* grad_inv, void* workspace, size_t workspace_bytes, void* stream);
+
 /* grad_zonal[e, r]     = inv[dst e] * sum_c g[dst e, r+1, c] radial[e, slot r, c]
  * grad_radial[e, s, c] = inv[dst e] * sum_{r: slot r = s} g[dst e, r+1, c] zonal[e, r]
  * grad_inv[n]          = sum_{r,c} g[n, r+1, c] * sum_{e in n} zonal[e,r] radial[e, slot r, c]

@@ -196,3 +196,51 @@ def test_rmsnorm_misaligned_scale_view(cuda):
     got = K.rmsnorm(x, scale)
     torch.testing.assert_close(got.cpu(), reference_rmsnorm(x.cpu(), scale.cpu()), rtol=2e-5,
                                atol=2e-5)
+
+
+@pytest.mark.parametrize("zero_based,channels,shuffled",
+                         [(True, 64, False), (False, 16, True), (False, 64, True), (True, 4, False)])
+def test_gie_degree_layout_backward(cuda, zero_based, channels, shuffled):
+    # The degree-specialised backward: skewed segments (split across
+    # partitions), optionally unsorted destinations (CSR view with an order).
+    gen = torch.Generator().manual_seed(3 * channels + shuffled)
+    sizes = torch.randint(0, 12, (200,), generator=gen)
+    sizes[30], sizes[-1] = 2500, 900
+    dst = torch.repeat_interleave(torch.arange(200), sizes)
+    if shuffled:
+        dst = dst[torch.randperm(dst.numel(), generator=gen)]
+    e = dst.numel()
+    z = torch.randn(e, 15, generator=gen)
+    r = torch.randn(e, 4, channels, generator=gen)
+    inv = torch.rand(200, generator=gen) + 0.2
+    slot = W.degree_slots(zero_based=zero_based)
+    up = torch.randn(200, 16, channels, generator=gen)
+    zc, rc, ic = (t.cuda().requires_grad_(True) for t in (z, r, inv))
+    out = K.zonal_scatter(zc, rc, dst.cuda(), slot.cuda(), ic)
+    got = torch.autograd.grad(out, (zc, rc, ic), up.cuda())
+    zr, rr, ir = (t.clone().requires_grad_(True) for t in (z, r, inv))
+    want = zonal_scatter_reference(zr, rr, dst, slot, ir)
+    wg = torch.autograd.grad(want, (zr, rr, ir), up)
+    for a, b in zip(got, wg):
+        torch.testing.assert_close(a.cpu(), b, rtol=4e-4, atol=2e-5 * float(b.abs().max()) + 2e-5)
+    unused = 0 if not zero_based else 3  # the radial slot no row reads
+    assert got[1][:, unused, :].count_nonzero() == 0
+    again = torch.autograd.grad(K.zonal_scatter(zc, rc, dst.cuda(), slot.cuda(), ic),
+                                (zc, rc, ic), up.cuda())
+    assert all(torch.equal(a, b) for a, b in zip(got, again))
+
+
+def test_gie_degree_backward_inverse_gradient_sums_first(cuda):
+    # Degree layout with L = 1 (rows 0..2 read radial slot 1): the three
+    # edges' unnormalised sums cancel exactly before the dot with g.
+    zonal = torch.zeros(3, 3, device="cuda")
+    zonal[:, 0] = torch.tensor([1e8, -1e8 + 8, 1.0], device="cuda")
+    radial = torch.ones(3, 2, 4, device="cuda")
+    dst = torch.zeros(3, dtype=torch.int64, device="cuda")
+    slot = torch.tensor([1, 1, 1], device="cuda")
+    inverse = torch.ones(1, device="cuda", requires_grad=True)
+    out = K.zonal_scatter(zonal, radial, dst, slot, inverse)
+    up = torch.zeros(1, 4, 4, device="cuda")
+    up[0, 1, :] = 0.3
+    (grad,) = torch.autograd.grad(out, (inverse,), up)
+    assert abs(grad.item() - 4 * 0.3 * 9.0) < 1e-4
