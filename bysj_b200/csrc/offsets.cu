@@ -19,9 +19,98 @@ namespace {
 
 constexpr int kScanTile = 2048;  // elements per CTA in the scan
 
+// The sorted path reads dst as 16-byte pairs (elements 2i, 2i+1), two pairs
+// per thread per step so that four loads are in flight; the element before a
+// pair comes from its own 8-byte load (an L1 hit: the neighbouring lane read
+// it).  `dst` must be 16-byte aligned for the pair loads (the host checks).
+constexpr int kPairsPerStep = 2;
+
+__device__ __forceinline__ longlong2 ld_pair(const int64_t* dst, int64_t i) {
+  return __ldg(reinterpret_cast<const longlong2*>(dst) + i);
+}
+
 __global__ void __launch_bounds__(kBlock)
     offsets_check_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
                          int64_t n_nodes, uint32_t* flags) {
+  uint32_t local = 0;
+  const int64_t pairs = n_edges / 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < pairs;
+       i0 += stride * kPairsPerStep) {
+    longlong2 v[kPairsPerStep];
+    int64_t before[kPairsPerStep];
+#pragma unroll
+    for (int k = 0; k < kPairsPerStep; ++k) {
+      const int64_t i = i0 + k * stride;
+      v[k] = i < pairs ? ld_pair(dst, i) : make_longlong2(0, 0);
+      before[k] = (i < pairs && i > 0) ? __ldg(dst + 2 * i - 1) : INT64_MIN;
+    }
+#pragma unroll
+    for (int k = 0; k < kPairsPerStep; ++k) {
+      if (i0 + k * stride >= pairs) continue;
+      const int64_t x = v[k].x, y = v[k].y;
+      if (x < 0 || x >= n_nodes || y < 0 || y >= n_nodes) local |= BYSJ_FLAG_OUT_OF_RANGE;
+      if (before[k] > x || x > y) local |= BYSJ_FLAG_UNSORTED;
+    }
+  }
+  // An odd element count leaves the last element to one thread.
+  if ((n_edges & 1) && blockIdx.x == 0 && threadIdx.x == 0) {
+    const int64_t e = n_edges - 1;
+    const int64_t d = __ldg(dst + e);
+    if (d < 0 || d >= n_nodes) local |= BYSJ_FLAG_OUT_OF_RANGE;
+    if (e > 0 && __ldg(dst + e - 1) > d) local |= BYSJ_FLAG_UNSORTED;
+  }
+  local = __reduce_or_sync(kFull, local);
+  if (local && lane_id() == 0) atomicOr(flags, local);
+}
+
+// offsets[n] for the nodes in (dst[e-1], dst[e]] is e.
+__device__ __forceinline__ void write_boundary(int64_t prev, int64_t cur, int64_t e,
+                                               int64_t* __restrict__ offsets) {
+  for (int64_t n = prev + 1; n <= cur; ++n) offsets[n] = e;
+}
+
+__global__ void __launch_bounds__(kBlock)
+    offsets_boundary_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
+                            int64_t n_nodes, int64_t* __restrict__ offsets,
+                            const uint32_t* flags) {
+  if (*flags != 0) return;
+  const int64_t pairs = n_edges / 2;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < pairs;
+       i0 += stride * kPairsPerStep) {
+    longlong2 v[kPairsPerStep];
+    int64_t before[kPairsPerStep];
+#pragma unroll
+    for (int k = 0; k < kPairsPerStep; ++k) {
+      const int64_t i = i0 + k * stride;
+      v[k] = i < pairs ? ld_pair(dst, i) : make_longlong2(0, 0);
+      before[k] = (i < pairs && i > 0) ? __ldg(dst + 2 * i - 1) : -1;
+    }
+#pragma unroll
+    for (int k = 0; k < kPairsPerStep; ++k) {
+      const int64_t i = i0 + k * stride;
+      if (i >= pairs) continue;
+      write_boundary(before[k], v[k].x, 2 * i, offsets);
+      write_boundary(v[k].x, v[k].y, 2 * i + 1, offsets);
+    }
+  }
+  // The odd last element and the end marker: nodes in (dst[E-1], N] start at E.
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    int64_t prev = n_edges >= 2 ? __ldg(dst + 2 * pairs - 1) : -1;
+    if (n_edges & 1) {
+      const int64_t last = __ldg(dst + n_edges - 1);
+      write_boundary(prev, last, n_edges - 1, offsets);
+      prev = last;
+    }
+    write_boundary(prev, n_nodes, n_edges, offsets);
+  }
+}
+
+// Scalar forms for a dst that is not 16-byte aligned.
+__global__ void __launch_bounds__(kBlock)
+    offsets_check_scalar_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
+                                int64_t n_nodes, uint32_t* flags) {
   uint32_t local = 0;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -35,17 +124,16 @@ __global__ void __launch_bounds__(kBlock)
 }
 
 __global__ void __launch_bounds__(kBlock)
-    offsets_boundary_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
-                            int64_t n_nodes, int64_t* __restrict__ offsets,
-                            const uint32_t* flags) {
+    offsets_boundary_scalar_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
+                                   int64_t n_nodes, int64_t* __restrict__ offsets,
+                                   const uint32_t* flags) {
   if (*flags != 0) return;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        e <= n_edges; e += stride) {
-    // Nodes in (prev, cur] start at slot e.
     const int64_t prev = e > 0 ? __ldg(dst + e - 1) : -1;
     const int64_t cur = e < n_edges ? __ldg(dst + e) : n_nodes;
-    for (int64_t n = prev + 1; n <= cur; ++n) offsets[n] = e;
+    write_boundary(prev, cur, e, offsets);
   }
 }
 
@@ -186,13 +274,21 @@ int bysj_segment_offsets_sorted(const int64_t* dst, int64_t n_edges,
   if (n_edges == 0)
     return cuda_check(cudaMemsetAsync(offsets, 0, sizeof(int64_t) * (n_nodes + 1), s),
                       "segment offsets: zero fill");
-  offsets_check_kernel<<<stream_blocks(n_edges), kBlock, 0, s>>>(dst, n_edges,
-                                                                 n_nodes, flags);
-  int st = launch_check("offsets_check_kernel");
+  if (aligned16(dst)) {
+    const unsigned blocks = stream_blocks((n_edges / 2 + kPairsPerStep - 1) / kPairsPerStep);
+    offsets_check_kernel<<<blocks, kBlock, 0, s>>>(dst, n_edges, n_nodes, flags);
+    int st = launch_check("offsets_check_kernel");
+    if (st) return st;
+    offsets_boundary_kernel<<<blocks, kBlock, 0, s>>>(dst, n_edges, n_nodes, offsets, flags);
+    return launch_check("offsets_boundary_kernel");
+  }
+  offsets_check_scalar_kernel<<<stream_blocks(n_edges), kBlock, 0, s>>>(dst, n_edges, n_nodes,
+                                                                        flags);
+  int st = launch_check("offsets_check_scalar_kernel");
   if (st) return st;
-  offsets_boundary_kernel<<<stream_blocks(n_edges + 1), kBlock, 0, s>>>(
+  offsets_boundary_scalar_kernel<<<stream_blocks(n_edges + 1), kBlock, 0, s>>>(
       dst, n_edges, n_nodes, offsets, flags);
-  return launch_check("offsets_boundary_kernel");
+  return launch_check("offsets_boundary_scalar_kernel");
 }
 
 size_t bysj_segment_offsets_workspace_size(int64_t n_nodes) {
