@@ -811,6 +811,187 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_bwd_split_kernel(SmxAr
   }
 }
 
+// ---- backward, quad-vector form (C % 4 == 0, C <= 128) -----------------------
+// Same lane layout as the forward quad kernel (LP lanes per row, G rows side
+// by side, T rows per lane per chunk).  Per segment: S[c] = sum_e alpha g
+// (+ null_alpha g0) from 16-byte loads of alpha and grad_alpha, a butterfly
+// over the G groups, then grad_logit = alpha (g - S) and, per row,
+// grad_env = 2 / env * sum_c grad_logit (a butterfly over the row's LP lanes).
+// A piece that fits one chunk keeps its rows in registers between the sum
+// and the write.  Split segments publish partial S; the last piece combines
+// them and writes segments of up to kSelfWrite edges itself, longer ones in
+// the equally partitioned second pass.
+template <int LP>
+__device__ __forceinline__ void quad_bwd_load(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                              int q, bool qok, float4 (&al)[QuadSmx<LP>::T],
+                                              float4 (&gr)[QuadSmx<LP>::T]) {
+  using Q = QuadSmx<LP>;
+  const int mine = qok ? quad_rows<LP>(base, hi, g) : 0;
+  const int64_t cq = a.channels / 4;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    al[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    gr[t] = al[t];
+    if (t < mine) {
+      const int64_t slot = base + g + static_cast<int64_t>(t) * Q::G;
+      const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+      al[t] = __ldg(reinterpret_cast<const float4*>(a.x) + e * cq + q);
+      gr[t] = __ldg(reinterpret_cast<const float4*>(a.y) + e * cq + q);
+    }
+  }
+}
+
+// Writes grad_logit (and grad_env) of slots base + g + t G from rows in registers.
+template <int LP>
+__device__ __forceinline__ void quad_bwd_store(const SmxArgs& a, int64_t base, int64_t hi, int g,
+                                               int q, bool qok, const float4 (&al)[QuadSmx<LP>::T],
+                                               const float4 (&gr)[QuadSmx<LP>::T],
+                                               const float (&S)[4]) {
+  using Q = QuadSmx<LP>;
+  const int rows = quad_rows<LP>(base, hi, g);
+  const int64_t cq = a.channels / 4;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    const int64_t slot = base + g + static_cast<int64_t>(t) * Q::G;
+    const bool live = t < rows;
+    const int64_t e = live ? (a.order ? __ldg(a.order + slot) : slot) : 0;
+    float4 gl = make_float4(al[t].x * (gr[t].x - S[0]), al[t].y * (gr[t].y - S[1]),
+                            al[t].z * (gr[t].z - S[2]), al[t].w * (gr[t].w - S[3]));
+    if (!qok) gl = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (live && qok) reinterpret_cast<float4*>(a.out)[e * cq + q] = gl;
+    if (a.out_env) {
+      float rowsum = (gl.x + gl.y) + (gl.z + gl.w);
+      if constexpr (LP > 1) rowsum = group_sum(rowsum, LP);
+      if (live && q == 0) {
+        const float env = a.env ? __ldg(a.env + e) : 1.0f;
+        a.out_env[e] = env > 0.0f ? rowsum * 2.0f / env : 0.0f;
+      }
+    }
+  }
+}
+
+template <int LP, bool kSplitPass>
+__global__ void __launch_bounds__(kBlock, 2) segment_softmax_quad_bwd_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t C = a.channels;
+  const bool qok = 4 * q < C;
+  if constexpr (kSplitPass) {
+    if (*reinterpret_cast<volatile int*>(a.big_split) == 0) return;
+  }
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const bool whole = cur.kind == kWhole;
+    float4 al[Q::T], gr[Q::T];
+    float S[4];
+    if constexpr (kSplitPass) {
+      if (whole) continue;
+      if (__ldg(a.mp.offsets + n + 1) - __ldg(a.mp.offsets + n) <= kSelfWrite) continue;
+      const float* fin = a.final_stats + a.mp.part_of_end(n) * 2 * a.cpad;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) S[i] = qok ? __ldcg(fin + 4 * q + i) : 0.0f;
+#pragma unroll 1
+      for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+        quad_bwd_load<LP>(a, base, cur.hi, g, q, qok, al, gr);
+        quad_bwd_store<LP>(a, base, cur.hi, g, q, qok, al, gr, S);
+      }
+      continue;
+    } else {
+      const bool one_chunk = cur.hi - cur.lo <= Q::CHUNK;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) S[i] = 0.0f;
+#pragma unroll 1
+      for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+        quad_bwd_load<LP>(a, base, cur.hi, g, q, qok, al, gr);
+#pragma unroll
+        for (int t = 0; t < Q::T; ++t) {
+          S[0] = fmaf(al[t].x, gr[t].x, S[0]);
+          S[1] = fmaf(al[t].y, gr[t].y, S[1]);
+          S[2] = fmaf(al[t].z, gr[t].z, S[2]);
+          S[3] = fmaf(al[t].w, gr[t].w, S[3]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        for (int st = LP; st < kWarp; st <<= 1) S[i] += __shfl_xor_sync(kFull, S[i], st);
+      if (whole) {
+        if (a.xn && qok) {
+          const float4 a0 = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+          const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.yn + n * C) + q);
+          S[0] = fmaf(a0.x, g0.x, S[0]);
+          S[1] = fmaf(a0.y, g0.y, S[1]);
+          S[2] = fmaf(a0.z, g0.z, S[2]);
+          S[3] = fmaf(a0.w, g0.w, S[3]);
+          if (g == 0)
+            reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+                make_float4(a0.x * (g0.x - S[0]), a0.y * (g0.y - S[1]), a0.z * (g0.z - S[2]),
+                            a0.w * (g0.w - S[3]));
+        }
+        if (one_chunk) {
+          quad_bwd_store<LP>(a, cur.lo, cur.hi, g, q, qok, al, gr, S);
+        } else {
+#pragma unroll 1
+          for (int64_t base = cur.lo; base < cur.hi; base += Q::CHUNK) {
+            quad_bwd_load<LP>(a, base, cur.hi, g, q, qok, al, gr);
+            quad_bwd_store<LP>(a, base, cur.hi, g, q, qok, al, gr, S);
+          }
+        }
+        continue;
+      }
+      // Split segment: publish the partial S; the last piece combines.
+      float* mine = a.ss.slot(p, cur.kind);
+      if (g == 0 && qok) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) __stcg(mine + 4 * q + i, S[i]);
+      }
+      const int64_t first = a.mp.part_of_first_edge(n);
+      const int64_t last = a.mp.part_of_end(n);
+      if (!arrive_last(a.ss, first, last, 0)) continue;
+      float* fin = a.final_stats + last * 2 * a.cpad;
+      float total[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (qok) {
+        for (int64_t qq = first; qq <= last; ++qq) {
+          const float* sq = a.ss.slot(qq, qq == last ? kHead : kTail);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) total[i] += __ldcg(sq + 4 * q + i);
+        }
+        if (a.xn) {
+          const float4 a0 = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+          const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.yn + n * C) + q);
+          total[0] = fmaf(a0.x, g0.x, total[0]);
+          total[1] = fmaf(a0.y, g0.y, total[1]);
+          total[2] = fmaf(a0.z, g0.z, total[2]);
+          total[3] = fmaf(a0.w, g0.w, total[3]);
+          if (g == 0)
+            reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+                make_float4(a0.x * (g0.x - total[0]), a0.y * (g0.y - total[1]),
+                            a0.z * (g0.z - total[2]), a0.w * (g0.w - total[3]));
+        }
+        if (g == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) __stcg(fin + 4 * q + i, total[i]);
+        }
+      }
+      const int64_t seg_lo = __ldg(a.mp.offsets + n);
+      const int64_t seg_hi = __ldg(a.mp.offsets + n + 1);
+      if (seg_hi - seg_lo <= kSelfWrite) {
+#pragma unroll 1
+        for (int64_t base = seg_lo; base < seg_hi; base += Q::CHUNK) {
+          quad_bwd_load<LP>(a, base, seg_hi, g, q, qok, al, gr);
+          quad_bwd_store<LP>(a, base, seg_hi, g, q, qok, al, gr, total);
+        }
+      } else if (lane == 0) {
+        atomicExch(a.big_split, 1);
+      }
+    }
+  }
+}
+
 // grad_env for channel counts wider than one warp tile.
 __global__ void __launch_bounds__(kBlock)
     segment_softmax_env_kernel(const float* __restrict__ grad_logit,
@@ -865,8 +1046,28 @@ SmxConfig quad_make(bool env) {
   return env ? quad_make_env<LP, true>() : quad_make_env<LP, false>();
 }
 
+template <int LP>
+SmxConfig quad_bwd_make() {
+  SmxConfig c;
+  c.main = segment_softmax_quad_bwd_kernel<LP, false>;
+  c.split = segment_softmax_quad_bwd_kernel<LP, true>;
+  c.tc = 4 * LP;
+  c.tiles = 1;
+  return c;
+}
+
 SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = true) {
   SmxConfig c;
+  if (backward && quad_ok && channels % 4 == 0 && channels <= 128) {
+    switch (next_pow2(channels / 4)) {
+      case 1: return quad_bwd_make<1>();
+      case 2: return quad_bwd_make<2>();
+      case 4: return quad_bwd_make<4>();
+      case 8: return quad_bwd_make<8>();
+      case 16: return quad_bwd_make<16>();
+      default: return quad_bwd_make<32>();
+    }
+  }
   if (!backward && quad_ok && channels % 4 == 0 && channels <= 128) {
     switch (next_pow2(channels / 4)) {
       case 1: return quad_make<1>(env);
@@ -1018,7 +1219,10 @@ size_t bysj_segment_softmax_backward_workspace_size(int64_t n_edges,
                                                     int64_t n_nodes,
                                                     int64_t channels) {
   if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
-  return smx_layout(n_edges, n_nodes, channels, true, nullptr).bytes;
+  // Pointer alignment picks the quad-vector or the scalar kernel; size for both.
+  const size_t a = smx_layout(n_edges, n_nodes, channels, true, nullptr, true).bytes;
+  const size_t b = smx_layout(n_edges, n_nodes, channels, true, nullptr, false).bytes;
+  return a > b ? a : b;
 }
 
 int bysj_segment_softmax_backward(const float* alpha, const float* grad_alpha,
@@ -1045,7 +1249,11 @@ int bysj_segment_softmax_backward(const float* alpha, const float* grad_alpha,
     return fail(BYSJ_ERR_INVALID_ARGUMENT,
                 "segment softmax backward: NULL alpha/grad_alpha/grad_logit");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  SmxLayout L = smx_layout(n_edges, n_nodes, channels, true, workspace);
+  const bool quad_ok = aligned16(alpha) && aligned16(grad_alpha) && aligned16(grad_logit) &&
+                       (null_alpha == nullptr || aligned16(null_alpha)) &&
+                       (grad_null_alpha == nullptr || aligned16(grad_null_alpha)) &&
+                       (grad_null_logit == nullptr || aligned16(grad_null_logit));
+  SmxLayout L = smx_layout(n_edges, n_nodes, channels, true, workspace, quad_ok);
   if (workspace == nullptr || workspace_bytes < L.bytes)
     return fail(BYSJ_ERR_WORKSPACE,
                 "segment softmax backward: workspace of %zu bytes needed, %zu "

@@ -271,6 +271,19 @@ def test_segment_softmax_skewed_split_segments(cuda):
         0, dst.cpu(), (a * ga).double().cpu()) + (n0 * gn).double().cpu()
     want_gl = a.double().cpu() * (ga.double().cpu() - S[dst.cpu()])
     np.testing.assert_allclose(gl.cpu().numpy(), want_gl.numpy(), rtol=1e-4, atol=1e-6)
+    want_env = want_gl.sum(1) * 2.0 / env.double()
+    np.testing.assert_allclose(genv.cpu().numpy(), want_env.numpy(), rtol=1e-4, atol=1e-5)
+    want_gnl = n0.double().cpu() * (gn.double().cpu() - S)
+    np.testing.assert_allclose(gnl.cpu().numpy(), want_gnl.numpy(), rtol=1e-4, atol=1e-6)
+    # the same rows stored in a permuted order and addressed through `order`
+    perm = torch.randperm(e, generator=gen)
+    ap, gp, ep = (torch.empty_like(t) for t in (a, ga, env.cuda()))
+    ap[perm.cuda()], gp[perm.cuda()], ep[perm.cuda()] = a, ga, env.cuda()
+    glp, _, genvp = ext.segment_softmax_backward(ap, gp, ep, off, n0, gn, order=perm.cuda())
+    np.testing.assert_allclose(glp[perm.cuda()].cpu().numpy(), want_gl.numpy(), rtol=1e-4,
+                               atol=1e-6)
+    np.testing.assert_allclose(genvp[perm.cuda()].cpu().numpy(), want_env.numpy(), rtol=1e-4,
+                               atol=1e-5)
 
 
 def test_segment_softmax_all_masked_segment_is_zero(cuda):
