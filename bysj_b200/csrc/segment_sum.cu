@@ -222,6 +222,54 @@ struct NodeScaleGradArgs {
   SplitSlots ss;
 };
 
+// grad_src for 16-byte rows over merge-path partitions: a warp loads the
+// node's grad_out row (its NV vectors per lane) once per piece and streams
+// row * (edge_scale[e] * node_scale[n]) to the piece's edges (the reference's
+// scale order, csrc/segment_sum.cpp:136-149).  Pieces of a split segment are
+// independent, so nothing is combined.
+template <int NV>
+__global__ void __launch_bounds__(kBlock)
+    segment_sum_grad_src_rows_kernel(const float* __restrict__ grad_out,
+                                     const float* __restrict__ edge_scale,
+                                     const float* __restrict__ node_scale,
+                                     const int64_t* __restrict__ order, MergePath mp,
+                                     int64_t channels, float* __restrict__ grad_src) {
+  constexpr int TV = kWarp * NV;
+  const int64_t p = global_warp();
+  if (p >= mp.parts) return;
+  const int lane = lane_id();
+  const int64_t lv = channels / 4;
+  const int64_t j0 = static_cast<int64_t>(blockIdx.y) * TV + lane;
+  SegCursor cur(mp, part_range(mp, p));
+  while (cur.next()) {
+    if (cur.lo >= cur.hi) continue;
+    const int64_t n = cur.node;
+    const float sn = node_scale ? __ldg(node_scale + n) : 1.0f;
+    float4 row[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int64_t j = j0 + k * kWarp;
+      row[k] = j < lv ? __ldg(reinterpret_cast<const float4*>(grad_out + n * channels) + j)
+                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    for (int64_t slot = cur.lo; slot < cur.hi; ++slot) {
+      const int64_t e = order ? __ldg(order + slot) : slot;
+      const float scale = (edge_scale ? __ldg(edge_scale + e) : 1.0f) * sn;
+      float4* out = reinterpret_cast<float4*>(grad_src + e * channels);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int64_t j = j0 + k * kWarp;
+        if (j < lv)
+          __stcs(out + j, make_float4(row[k].x * scale, row[k].y * scale, row[k].z * scale,
+                                      row[k].w * scale));
+      }
+    }
+  }
+}
+
+// grad_node_scale[n] = sum_{e in n} edge_scale[e] * <grad_out[n], src[e]>:
+// lanes over the row's vectors, edges in slot order, merge-path pieces
+// combined in partition order.
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kBlock)
     segment_sum_grad_scale_kernel(NodeScaleGradArgs a) {
@@ -464,25 +512,45 @@ int bysj_segment_sum_backward(const float* grad_out, const void* src,
     return fail(BYSJ_ERR_INVALID_ARGUMENT,
                 "segment sum backward: a node_scale gradient needs node_scale");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n_edges > 0) {
-    const bool vec = channels % 4 == 0 && aligned16(grad_out) &&
-                     aligned16(grad_src);
-    const int64_t lv = vec ? channels / 4 : channels;
-    const int64_t total = n_edges * lv;
+  if (n_edges > 0 && channels % 4 == 0 && aligned16(grad_out) && aligned16(grad_src)) {
+    const int64_t lv = channels / 4;
+    const int nv = lv > 128 ? 8 : lv > 64 ? 4 : lv > 32 ? 2 : 1;
+    const int64_t tiles = (lv + kWarp * nv - 1) / (kWarp * nv);
+    const DeviceInfo& dev = current_device_info();
+    const int64_t resident = static_cast<int64_t>(dev.sm_count) * 8 * kWarpsPerBlock;
+    int64_t warps = resident / tiles;
+    if (warps < 1) warps = 1;
+    const PartitionPlan plan = plan_partitions(n_edges, n_nodes, warps, 16);
+    const MergePath mp{offsets, n_nodes, n_edges, plan.ipc, plan.parts};
+    const dim3 grid(plan.blocks, static_cast<unsigned>(tiles));
+    switch (nv) {
+      case 8:
+        segment_sum_grad_src_rows_kernel<8><<<grid, kBlock, 0, s>>>(
+            grad_out, edge_scale, node_scale, order, mp, channels, grad_src);
+        break;
+      case 4:
+        segment_sum_grad_src_rows_kernel<4><<<grid, kBlock, 0, s>>>(
+            grad_out, edge_scale, node_scale, order, mp, channels, grad_src);
+        break;
+      case 2:
+        segment_sum_grad_src_rows_kernel<2><<<grid, kBlock, 0, s>>>(
+            grad_out, edge_scale, node_scale, order, mp, channels, grad_src);
+        break;
+      default:
+        segment_sum_grad_src_rows_kernel<1><<<grid, kBlock, 0, s>>>(
+            grad_out, edge_scale, node_scale, order, mp, channels, grad_src);
+    }
+    st = launch_check("segment_sum_grad_src_rows_kernel");
+    if (st) return st;
+  } else if (n_edges > 0) {
+    // Unaligned or narrow rows: one element per thread, node from dst.
+    const int64_t total = n_edges * channels;
     const DeviceInfo& dev = current_device_info();
     int64_t blocks = (total + kBlock - 1) / kBlock;
     const int64_t cap = static_cast<int64_t>(dev.sm_count) * 16;
     if (blocks > cap) blocks = cap;
-    if (vec)
-      segment_sum_grad_src_kernel<4><<<static_cast<unsigned>(blocks), kBlock,
-                                       0, s>>>(grad_out, edge_scale,
-                                               node_scale, dst, grad_src,
-                                               n_edges, channels);
-    else
-      segment_sum_grad_src_kernel<1><<<static_cast<unsigned>(blocks), kBlock,
-                                       0, s>>>(grad_out, edge_scale,
-                                               node_scale, dst, grad_src,
-                                               n_edges, channels);
+    segment_sum_grad_src_kernel<1><<<static_cast<unsigned>(blocks), kBlock, 0, s>>>(
+        grad_out, edge_scale, node_scale, dst, grad_src, n_edges, channels);
     st = launch_check("segment_sum_grad_src_kernel");
     if (st) return st;
   }
@@ -516,11 +584,9 @@ int bysj_segment_sum_backward(const float* grad_out, const void* src,
                         : (channels % 4 == 0 && aligned16(src));
   if (bf16) {
     if (vec)
-      segment_sum_grad_scale_kernel<__nv_bfloat16, 8>
-          <<<plan.blocks, kBlock, 0, s>>>(a);
+      segment_sum_grad_scale_kernel<__nv_bfloat16, 8><<<plan.blocks, kBlock, 0, s>>>(a);
     else
-      segment_sum_grad_scale_kernel<__nv_bfloat16, 1>
-          <<<plan.blocks, kBlock, 0, s>>>(a);
+      segment_sum_grad_scale_kernel<__nv_bfloat16, 1><<<plan.blocks, kBlock, 0, s>>>(a);
   } else {
     if (vec)
       segment_sum_grad_scale_kernel<float, 4><<<plan.blocks, kBlock, 0, s>>>(a);
