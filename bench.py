@@ -490,8 +490,56 @@ def _op_zonal_bwd(ctx):
                             "the device CSR view of dst"})
 
 
+def _op_small_step_graph(ctx):
+    """A launch-bound step on the 192-atom C1 box, eager and as a CUDA-graph replay."""
+    from bysj_b200 import _C
+    from bysj_b200 import kernels as K
+    from bysj_b200 import workloads as W
+
+    device = ctx["device"]
+    g = W.c1_box(device=device)
+    e, n = g.n_edges, g.n_atoms
+    gen = torch.Generator(device=device).manual_seed(23)
+    logit = torch.randn(e, 8, device=device, generator=gen)
+    value = torch.randn(e, 16, 64, device=device, generator=gen)
+    env = torch.rand(e, device=device, generator=gen) + 0.05
+    grad = torch.randn(e, 3, device=device, generator=gen) * 0.1
+    x = torch.randn(n, 16, 128, device=device, generator=gen)
+    w = torch.rand(4, 128, device=device, generator=gen) + 0.5
+    order, soff = K.group_by_source(g.src, n)
+    flags = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def step():
+        off = _C.segment_offsets_device(g.dst, n, flags)
+        _C.segment_attention_forward(logit, value, off)
+        _C.segment_softmax_forward(logit, env, off)
+        _C.force_assembly(grad, g.unit, off, soff, order)
+        _C.rmsnorm_forward(x, w, 1e-6)
+
+    reps = 20
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    t_eager = time_launches(lambda: [step() for _ in range(reps)], ctx["iters"]) / reps
+    t_graph = time_launches(lambda: [graph.replay() for _ in range(reps)], ctx["iters"]) / reps
+    del graph
+    alg = (e * (32 + 4096) + n * 4096 + e * (32 + 4 + 32) + e * 32 + n * 64
+           + 2 * n * 16 * 128 * 4 + 8 * e + 8 * (n + 1))
+    return op_line("c1_step_graph", alg, t_graph, ctx["peak"], e,
+                   {"eager_us": t_eager * 1e6,
+                    "note": "offsets + attention + softmax + force + RMSNorm on the 192-atom "
+                            "C1 box (17.7k edges, launch-bound); us = one CUDA-graph replay, "
+                            "eager_us = the same launches issued one by one"})
+
+
 OPS = {
     "offsets": _op_offsets,
+    "c1_step_graph": _op_small_step_graph,
     "group": _op_group,
     "attention_bf16": _op_attention_bf16,
     "softmax": _op_softmax,
