@@ -5,6 +5,8 @@ Subpackages mirror the reference project's Python API:
 * :mod:`bysj_b200.kernels` -- the ``kernels.*`` operator wrappers
   (segment_offsets, segment_sum, segment_softmax, segment_attention,
   force_assembly, rmsnorm, zonal_scatter).
+* :mod:`bysj_b200.reference` -- the ``reference.*`` PyTorch implementations
+  for explicit testing and comparison (never called by the kernels).
 * :mod:`bysj_b200.model` -- ``DPA4Model(fused=...)`` and the DeepMD seam.
 * :mod:`bysj_b200.sharding` -- multi-GPU frame sharding and the
   destination-range partition of one large frame.
