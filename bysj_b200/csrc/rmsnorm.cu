@@ -410,7 +410,7 @@ NormKernel norm_pick_w(int64_t lv, int* g_out) {
   if (lv > 32) return rmsnorm_fwd_kernel<T, VEC, 2, 1, 4, WM>;
   switch (next_pow2(lv)) {
     case 32: return rmsnorm_fwd_kernel<T, VEC, 1, 1, 4, WM>;
-    case 16: *g_out = 2; return rmsnorm_fwd_kernel<T, VEC, 1, 2, 4, WM>;
+    case 16: *g_out = 4; return rmsnorm_fwd_kernel<T, VEC, 2, 4, 2, WM>;
     case 8: *g_out = 4; return rmsnorm_fwd_kernel<T, VEC, 1, 4, 4, WM>;
     case 4: *g_out = 8; return rmsnorm_fwd_kernel<T, VEC, 1, 8, 4, WM>;
     case 2: *g_out = 16; return rmsnorm_fwd_kernel<T, VEC, 1, 16, 4, WM>;
