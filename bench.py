@@ -19,11 +19,17 @@ segment sum) producing [N, 8, 16, 8].  The metric is edges/s.
   average launch time (events on its stream), against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the reference's PyTorch oracle (restated under
   ``oracle/``) on the host cores, on a bounded sample of the same frame.
-* ``ops``: per-operator roofline lines for the other configs (bf16 values,
-  standalone softmax, segment_sum, force_assembly, zonal_scatter, RMSNorm,
-  segment_offsets) at N = 1.
+* ``ops``: per-operator roofline lines for the other configs at N = 1:
+  segment_offsets, group_by_source, bf16-value attention, standalone
+  softmax, segment_sum, force_assembly (Morton and random atom order),
+  zonal_scatter, RMSNorm fp32/bf16, the backward operators, and a small
+  launch-bound step replayed from a CUDA graph.  ``--only OP`` times one.
+* ``--mode partition``: one 500k-atom box split by destination ranges over
+  the ranks (strong scaling; force partials reduce-scattered over NCCL).
 
-``--impl reference`` times the CPU oracle instead (rank 0 only).
+``--impl reference`` times the CPU oracle instead (rank 0 only) and reports
+the same metric and config, its bounded sample described in
+``cpu_baseline.sample``.
 """
 from __future__ import annotations
 
@@ -222,6 +228,15 @@ def make_frame(device, seed, values_dtype, small=False):
     if values_dtype == "bf16":
         value = value.to(torch.bfloat16)
     return g, logit.contiguous(), value.contiguous()
+
+
+def c3_config(n_atoms, n_edges, values, world):
+    """The headline workload's `config` object (both arms report the same one)."""
+    return {"workload": "C3 fused attention: segment_offsets -> segment_attention",
+            "n_atoms": n_atoms, "n_edges_per_frame": n_edges, "heads": 8, "components": 16,
+            "channels": 64, "values": values, "frames_per_gpu_per_step": 1,
+            "parallelism": f"frame-sharded x{world} (no collective)",
+            "l2": "inputs (~9.1 GB fp32 values) larger than L2; no flush"}
 
 
 def attention_bytes(e, n, value_elem_bytes):
@@ -631,8 +646,7 @@ def run_reference(args, dist):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "C3 fused attention (bounded CPU sample)", "n_atoms": g.n_atoms,
-                   "sample_edges": e_s, "heads": 8, "components": 16, "channels": 64},
+        "config": c3_config(g.n_atoms, g.n_edges, "f32", args.gpus),
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -755,11 +769,7 @@ def run_ours(args, dist):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_max * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32" if args.values == "f32" else "bf16-in/f32-acc", "data": "synthetic",
-            "config": {"workload": "C3 fused attention: segment_offsets -> segment_attention",
-                       "n_atoms": n, "n_edges_per_frame": e, "heads": 8, "components": 16,
-                       "channels": 64, "values": args.values, "frames_per_gpu_per_step": 1,
-                       "parallelism": f"frame-sharded x{dist.world} (no collective)",
-                       "l2": "inputs (~9.1 GB fp32 values) larger than L2; no flush"},
+            "config": c3_config(n, e, args.values, dist.world),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
