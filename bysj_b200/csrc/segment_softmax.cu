@@ -343,6 +343,25 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Reads of a staged chunk through explicit shared-memory addresses (the
+// buffers are picked at run time, which would otherwise leave generic loads).
+// volatile: kept in order with the cp.async waits above them.
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 // Shared-memory staging of one chunk of a warp: lane (g, q) copies the quad
 // q of rows base + g + t*G into buf[32 t + lane] (the place it reads it from
 // later), and lane q == 0 of each group the row's envelope into
@@ -381,6 +400,8 @@ __device__ __forceinline__ void quad_load_smem(const float4* buf, const float* e
   constexpr int kOwn = (Q::T + LP - 1) / LP;
   const int rows = quad_rows<LP>(base, hi, g);
   const int lane = g * LP + q;
+  const uint32_t rows_s = smem_addr(buf) + 16u * lane;
+  const uint32_t env_s = smem_addr(envs) + 4u * g;
   float sh[kOwn];
   if constexpr (kEnv) {
 #pragma unroll
@@ -388,7 +409,7 @@ __device__ __forceinline__ void quad_load_smem(const float4* buf, const float* e
       const int t = q + j * LP;
       float v = -INFINITY;
       if (t < rows) {
-        const float env = envs[t * Q::G + g];
+        const float env = lds_f32(env_s + 4u * t * Q::G);
         if (env > 0.0f) v = 2.0f * __logf(env);
       }
       sh[j] = v;
@@ -407,7 +428,7 @@ __device__ __forceinline__ void quad_load_smem(const float4* buf, const float* e
     }
     float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
     if (t < mine) {
-      const float4 raw = buf[t * kWarp + lane];
+      const float4 raw = lds_f4(rows_s + 16u * t * kWarp);
       if (!kEnv || shift != -INFINITY)
         v = make_float4(raw.x + shift, raw.y + shift, raw.z + shift, raw.w + shift);
     }
@@ -602,6 +623,99 @@ __device__ __forceinline__ void quad_segment(const SmxArgs& a, int64_t p, const 
   }
 }
 
+// ---- forward, lean form: C == 4 LP exactly, rows in storage order --------
+// The common case of the pipelined kernel (H = 4 or 8 heads, no storage
+// order): a row is exactly LP quads, so every row address is one base plus a
+// compile-time stride, and the envelope shift of a row is taken by both of
+// its lanes (no shuffle).  Same staging layout as quad_stage, same
+// arithmetic as quad_segment's one-chunk path, hence the same bits.
+
+template <int LP, bool kEnv>
+__device__ __forceinline__ void lean_stage(const SmxArgs& a, int64_t lo, int64_t hi, int g,
+                                           int q, float4* buf, float* env) {
+  using Q = QuadSmx<LP>;
+  const int rows = quad_rows<LP>(lo, hi, g);
+  const int lane = g * LP + q;
+  const float4* src = reinterpret_cast<const float4*>(a.x) + (lo + g) * LP + q;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t)
+    if (t < rows) cp_async16(buf + t * kWarp + lane, src + t * Q::G * LP);
+  if constexpr (kEnv) {
+    const float* es = a.env + lo + g;
+#pragma unroll
+    for (int j = 0; j < Q::T / LP; ++j) {
+      const int t = q + j * LP;
+      if (t < rows) cp_async4(env + t * Q::G + g, es + t * Q::G);
+    }
+  }
+}
+
+template <int LP, bool kEnv>
+__device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
+                                           int g, int q, const float4* buf, const float* envs) {
+  using Q = QuadSmx<LP>;
+  constexpr int C = 4 * LP;
+  const int rows = quad_rows<LP>(lo, hi, g);
+  const int lane = g * LP + q;
+  const uint32_t rows_s = smem_addr(buf) + 16u * lane;
+  const uint32_t env_s = smem_addr(envs) + 4u * g;
+  float4 x[Q::T];
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t) {
+    float shift = 0.0f;
+    bool keep = t < rows;
+    if constexpr (kEnv) {
+      const float e = keep ? lds_f32(env_s + 4u * t * Q::G) : 0.0f;
+      keep = keep && e > 0.0f;
+      shift = keep ? 2.0f * __logf(e) : 0.0f;
+    }
+    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (keep) {
+      const float4 raw = lds_f4(rows_s + 16u * t * kWarp);
+      v = make_float4(raw.x + shift, raw.y + shift, raw.z + shift, raw.w + shift);
+    }
+    x[t] = v;
+  }
+  float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  if (a.xn) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+    nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
+  }
+  float w0[4], inv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float cm = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
+#pragma unroll
+    for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
+    const float m = fmaxf(cm, nl[i]);
+    const float ms = m == -INFINITY ? 0.0f : m;
+    float acc = 0.0f;
+#pragma unroll
+    for (int t = 0; t < Q::T; ++t) {
+      const float w = __expf(quad_get(x[t], i) - ms);
+      quad_set(x[t], i, w);
+      acc += w;
+    }
+#pragma unroll
+    for (int st = LP; st < kWarp; st <<= 1) acc += __shfl_xor_sync(kFull, acc, st);
+    w0[i] = shifted_exp(nl[i], m);
+    const float total = acc + w0[i];
+    inv[i] = total > 0.0f ? __frcp_rn(total) : 0.0f;
+  }
+  if (g == 0 && a.out_null) {
+    reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+        make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
+  }
+  float4* dst = reinterpret_cast<float4*>(a.out) + (lo + g) * LP + q;
+#pragma unroll
+  for (int t = 0; t < Q::T; ++t)
+    if (t < rows)
+      dst[t * Q::G * LP] =
+          make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+}
+
 // Channel counts up to 8 (LP <= 2) hold a typical segment (<= 128 rows) in
 // one chunk, so the main pass stages the next piece in shared memory while
 // computing the current one (2 CTAs per SM: 72 KB of buffers each).  Wider
@@ -611,7 +725,7 @@ constexpr bool quad_pipelined() {
   return LP <= 2;
 }
 
-template <int LP, bool kSplitPass, bool kEnv>
+template <int LP, bool kSplitPass, bool kEnv, bool kLean = false>
 __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
     segment_softmax_quad_kernel(SmxArgs a) {
   using Q = QuadSmx<LP>;
@@ -640,23 +754,37 @@ __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
     bool have = ahead.next();
     Piece cur = piece_of(ahead);
     int b = 0;
-    if (have && cur.hi - cur.lo <= Q::CHUNK)
-      quad_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, bufs[0],
-                           reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+    if (have && cur.hi - cur.lo <= Q::CHUNK) {
+      if constexpr (kLean)
+        lean_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, bufs[0],
+                             reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+      else
+        quad_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, bufs[0],
+                             reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+    }
     cp_async_commit();
     while (have) {
       const bool have_next = ahead.next();
       const Piece nxt = piece_of(ahead);
-      if (have_next && nxt.hi - nxt.lo <= Q::CHUNK)
-        quad_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, qok, bufs[b ^ 1],
-                             reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
+      if (have_next && nxt.hi - nxt.lo <= Q::CHUNK) {
+        if constexpr (kLean)
+          lean_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, bufs[b ^ 1],
+                               reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
+        else
+          quad_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, qok, bufs[b ^ 1],
+                               reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
+      }
       cp_async_commit();
       cp_async_wait<1>();  // this piece's copies have landed
       __syncwarp();
       const bool staged = cur.hi - cur.lo <= Q::CHUNK;
-      quad_segment<LP, false, kEnv>(a, p, cur, lane, g, q, qok, staged ? bufs[b] : nullptr,
-                                    staged ? reinterpret_cast<float*>(bufs[b] + S::kRowsF4)
-                                           : nullptr);
+      if (kLean && staged && cur.kind == kWhole)
+        lean_whole<LP, kEnv>(a, cur.node, cur.lo, cur.hi, g, q, bufs[b],
+                             reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
+      else
+        quad_segment<LP, false, kEnv>(a, p, cur, lane, g, q, qok, staged ? bufs[b] : nullptr,
+                                      staged ? reinterpret_cast<float*>(bufs[b] + S::kRowsF4)
+                                             : nullptr);
       __syncwarp();  // every lane is done with bufs[b] before it is refilled
       cur = nxt;
       have = have_next;
@@ -1030,10 +1158,10 @@ SmxConfig smx_make(bool backward) {
   return c;
 }
 
-template <int LP, bool kEnv>
+template <int LP, bool kEnv, bool kLean = false>
 SmxConfig quad_make_env() {
   SmxConfig c;
-  c.main = segment_softmax_quad_kernel<LP, false, kEnv>;
+  c.main = segment_softmax_quad_kernel<LP, false, kEnv, kLean>;
   c.split = segment_softmax_quad_kernel<LP, true, kEnv>;
   c.tc = 4 * LP;
   c.tiles = 1;
@@ -1046,6 +1174,12 @@ SmxConfig quad_make(bool env) {
   return env ? quad_make_env<LP, true>() : quad_make_env<LP, false>();
 }
 
+// C == 4 LP with rows in storage order (LP <= 2, the pipelined widths).
+template <int LP>
+SmxConfig quad_make_lean(bool env) {
+  return env ? quad_make_env<LP, true, true>() : quad_make_env<LP, false, true>();
+}
+
 template <int LP>
 SmxConfig quad_bwd_make() {
   SmxConfig c;
@@ -1056,8 +1190,13 @@ SmxConfig quad_bwd_make() {
   return c;
 }
 
-SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = true) {
+SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = true,
+                     bool lean = false) {
   SmxConfig c;
+  if (!backward && quad_ok && lean) {
+    if (channels == 4) return quad_make_lean<1>(env);
+    if (channels == 8) return quad_make_lean<2>(env);
+  }
   if (backward && quad_ok && channels % 4 == 0 && channels <= 128) {
     switch (next_pow2(channels / 4)) {
       case 1: return quad_bwd_make<1>();
@@ -1106,9 +1245,10 @@ struct SmxLayout {
 };
 
 SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
-                     bool backward, void* ws, bool quad_ok = true, bool env = true) {
+                     bool backward, void* ws, bool quad_ok = true, bool env = true,
+                     bool lean = false) {
   SmxLayout L;
-  L.cfg = smx_config(channels, backward, quad_ok, env);
+  L.cfg = smx_config(channels, backward, quad_ok, env, lean);
   const DeviceInfo& dev = current_device_info();
   L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem);
   const int64_t resident =
@@ -1168,13 +1308,15 @@ extern "C" {
 size_t bysj_segment_softmax_workspace_size(int64_t n_edges, int64_t n_nodes,
                                            int64_t channels) {
   if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
-  // Pointer alignment and `env` pick the kernel (and with it the partition
-  // count); size for every choice.
+  // Pointer alignment, `env` and `order` pick the kernel (and with it the
+  // partition count); size for every choice.
   size_t need = smx_layout(n_edges, n_nodes, channels, false, nullptr, false).bytes;
-  for (int env = 0; env < 2; ++env) {
-    const size_t b = smx_layout(n_edges, n_nodes, channels, false, nullptr, true, env).bytes;
-    if (b > need) need = b;
-  }
+  for (int env = 0; env < 2; ++env)
+    for (int lean = 0; lean < 2; ++lean) {
+      const size_t b =
+          smx_layout(n_edges, n_nodes, channels, false, nullptr, true, env, lean).bytes;
+      if (b > need) need = b;
+    }
   return need;
 }
 
@@ -1198,7 +1340,7 @@ int bysj_segment_softmax_forward(const float* logit, const float* env,
                        (null_logit == nullptr || aligned16(null_logit)) &&
                        (null_alpha == nullptr || aligned16(null_alpha));
   SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace, quad_ok,
-                           env != nullptr);
+                           env != nullptr, order == nullptr);
   if (workspace == nullptr || workspace_bytes < L.bytes)
     return fail(BYSJ_ERR_WORKSPACE,
                 "segment softmax: workspace of %zu bytes needed, %zu given",
