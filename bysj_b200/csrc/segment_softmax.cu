@@ -15,7 +15,10 @@
 // L1.  For a segment cut by partition boundaries, the pieces publish their
 // partial statistics, the last piece to finish combines them in partition
 // order into a final-statistics slot, and a second, equally partitioned
-// kernel writes the per-edge outputs of those segments.
+// kernel writes the per-edge outputs of those segments.  The forward pass
+// for C = 4 or 8 with rows in storage order (the attention widths) instead
+// gives each warp whole segments (segment_softmax_whole_kernel): no split,
+// no second pass.
 #include "launch.cuh"
 
 namespace bysj {
@@ -624,11 +627,11 @@ __device__ __forceinline__ void quad_segment(const SmxArgs& a, int64_t p, const 
 }
 
 // ---- forward, lean form: C == 4 LP exactly, rows in storage order --------
-// The common case of the pipelined kernel (H = 4 or 8 heads, no storage
+// The common case of the pipelined widths (H = 4 or 8 heads, no storage
 // order): a row is exactly LP quads, so every row address is one base plus a
 // compile-time stride, and the envelope shift of a row is taken by both of
-// its lanes (no shuffle).  Same staging layout as quad_stage, same
-// arithmetic as quad_segment's one-chunk path, hence the same bits.
+// its lanes (no shuffle).  Same staging layout as quad_stage and the same
+// arithmetic as quad_segment's one-chunk path for a whole segment.
 
 template <int LP, bool kEnv>
 __device__ __forceinline__ void lean_stage(const SmxArgs& a, int64_t lo, int64_t hi, int g,
@@ -725,7 +728,7 @@ constexpr bool quad_pipelined() {
   return LP <= 2;
 }
 
-template <int LP, bool kSplitPass, bool kEnv, bool kLean = false>
+template <int LP, bool kSplitPass, bool kEnv>
 __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
     segment_softmax_quad_kernel(SmxArgs a) {
   using Q = QuadSmx<LP>;
@@ -754,37 +757,23 @@ __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
     bool have = ahead.next();
     Piece cur = piece_of(ahead);
     int b = 0;
-    if (have && cur.hi - cur.lo <= Q::CHUNK) {
-      if constexpr (kLean)
-        lean_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, bufs[0],
-                             reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
-      else
-        quad_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, bufs[0],
-                             reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
-    }
+    if (have && cur.hi - cur.lo <= Q::CHUNK)
+      quad_stage<LP, kEnv>(a, cur.lo, cur.hi, g, q, qok, bufs[0],
+                           reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
     cp_async_commit();
     while (have) {
       const bool have_next = ahead.next();
       const Piece nxt = piece_of(ahead);
-      if (have_next && nxt.hi - nxt.lo <= Q::CHUNK) {
-        if constexpr (kLean)
-          lean_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, bufs[b ^ 1],
-                               reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
-        else
-          quad_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, qok, bufs[b ^ 1],
-                               reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
-      }
+      if (have_next && nxt.hi - nxt.lo <= Q::CHUNK)
+        quad_stage<LP, kEnv>(a, nxt.lo, nxt.hi, g, q, qok, bufs[b ^ 1],
+                             reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
       cp_async_commit();
       cp_async_wait<1>();  // this piece's copies have landed
       __syncwarp();
       const bool staged = cur.hi - cur.lo <= Q::CHUNK;
-      if (kLean && staged && cur.kind == kWhole)
-        lean_whole<LP, kEnv>(a, cur.node, cur.lo, cur.hi, g, q, bufs[b],
-                             reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
-      else
-        quad_segment<LP, false, kEnv>(a, p, cur, lane, g, q, qok, staged ? bufs[b] : nullptr,
-                                      staged ? reinterpret_cast<float*>(bufs[b] + S::kRowsF4)
-                                             : nullptr);
+      quad_segment<LP, false, kEnv>(a, p, cur, lane, g, q, qok, staged ? bufs[b] : nullptr,
+                                    staged ? reinterpret_cast<float*>(bufs[b] + S::kRowsF4)
+                                           : nullptr);
       __syncwarp();  // every lane is done with bufs[b] before it is refilled
       cur = nxt;
       have = have_next;
@@ -792,6 +781,145 @@ __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
     }
     cp_async_wait<0>();
   }
+}
+
+// ---- forward, whole-segment partitions (lean widths) -----------------------
+// For the lean widths the merge-path partitions are used only to balance the
+// work: warp p takes every segment whose first merge-path item (diagonal
+// offsets[n] + n) lies in its partition, whole.  No segment is split, so
+// there are no partial statistics, tickets or second pass; the imbalance is
+// at most one segment (<= CHUNK rows in the pipelined case).
+
+// Number of segments n < N whose start diagonal offsets[n] + n lies below d
+// (warp-wide; every lane returns the same value).  32-ary search.
+__device__ __forceinline__ int64_t starts_before(const MergePath& mp, int64_t d) {
+  const int lane = lane_id();
+  if (d > mp.n_edges + mp.n_nodes) d = mp.n_edges + mp.n_nodes;  // the last partition's end
+  int64_t lo = d > mp.n_edges ? d - mp.n_edges : 0;
+  int64_t hi = d < mp.n_nodes ? d : mp.n_nodes;
+  while (hi - lo > kWarp) {
+    const int64_t step = (hi - lo + kWarp - 1) / kWarp;
+    const int64_t probe = lo + lane * step;
+    const bool before = probe < hi && (__ldg(mp.offsets + probe) + probe < d);
+    const int cnt = __popc(__ballot_sync(kFull, before));
+    if (cnt == 0) return lo;
+    const int64_t new_lo = lo + (cnt - 1) * step + 1;
+    const int64_t new_hi = lo + cnt * step;
+    lo = new_lo;
+    hi = new_hi < hi ? new_hi : hi;
+  }
+  const int64_t probe = lo + lane;
+  const bool before = probe < hi && (__ldg(mp.offsets + probe) + probe < d);
+  return lo + __popc(__ballot_sync(kFull, before));
+}
+
+// A whole segment longer than one chunk: running (max, sum) per channel over
+// chunks read from global memory, merged over the edge groups, then a second
+// read for the weights (as quad_segment's multi-chunk whole path).
+template <int LP, bool kEnv>
+__device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
+                                         int g, int q) {
+  using Q = QuadSmx<LP>;
+  constexpr int C = 4 * LP;
+  float4 x[Q::T];
+  float m[4], d[4], inv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
+  #pragma unroll 1
+  for (int64_t base = lo; base < hi; base += Q::CHUNK) {
+    quad_load<LP, kEnv>(a, base, hi, g, q, true, x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float cm = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
+      const float mn = fmaxf(m[i], cm);
+      float acc = d[i] * shifted_exp(m[i], mn);
+#pragma unroll
+      for (int t = 0; t < Q::T; ++t) acc += shifted_exp_fast(quad_get(x[t], i), mn);
+      d[i] = acc;
+      m[i] = mn;
+    }
+  }
+  for (int st = LP; st < kWarp; st <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float mo = __shfl_xor_sync(kFull, m[i], st);
+      const float dd = __shfl_xor_sync(kFull, d[i], st);
+      const float mn = fmaxf(m[i], mo);
+      d[i] = d[i] * shifted_exp(m[i], mn) + dd * shifted_exp(mo, mn);
+      m[i] = mn;
+    }
+  }
+  float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  if (a.xn) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+    nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
+  }
+  float w0[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float mm = fmaxf(m[i], nl[i]);
+    w0[i] = shifted_exp(nl[i], mm);
+    const float total = d[i] * shifted_exp(m[i], mm) + w0[i];
+    inv[i] = total > 0.0f ? 1.0f / total : 0.0f;
+    m[i] = mm;
+  }
+  if (g == 0 && a.out_null)
+    reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+        make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
+  #pragma unroll 1
+  for (int64_t base = lo; base < hi; base += Q::CHUNK) {
+    quad_load<LP, kEnv>(a, base, hi, g, q, true, x);
+    quad_write<LP>(a, base, hi, g, q, true, x, m, inv);
+  }
+}
+
+// Three CTAs per SM: 80 registers, 3 x 72 KB of staging buffers.
+template <int LP, bool kEnv>
+__global__ void __launch_bounds__(kBlock, 3) segment_softmax_whole_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  using S = QuadStage<LP>;
+  extern __shared__ float4 quad_smem[];
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t n0 = starts_before(a.mp, p * a.mp.ipc);
+  const int64_t n1 = starts_before(a.mp, (p + 1) * a.mp.ipc);
+  if (n0 >= n1) return;
+  char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
+  float4* bufs[2] = {reinterpret_cast<float4*>(mine), reinterpret_cast<float4*>(mine + S::kBytes)};
+  const int64_t* off = a.mp.offsets;
+  // Segment n is [lo, hi); the next one ends at nhi.  Its rows are copied
+  // into the other buffer while this one is computed.
+  int64_t lo = __ldg(off + n0), hi = __ldg(off + n0 + 1);
+  int64_t nhi = n0 + 1 < n1 ? __ldg(off + n0 + 2) : hi;
+  if (hi - lo <= Q::CHUNK)
+    lean_stage<LP, kEnv>(a, lo, hi, g, q, bufs[0], reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+  cp_async_commit();
+  int b = 0;
+  for (int64_t n = n0; n < n1; ++n) {
+    const int64_t nnhi = n + 2 < n1 ? __ldg(off + n + 3) : nhi;
+    if (n + 1 < n1 && nhi - hi <= Q::CHUNK)
+      lean_stage<LP, kEnv>(a, hi, nhi, g, q, bufs[b ^ 1],
+                           reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
+    cp_async_commit();
+    cp_async_wait<1>();  // this segment's copies have landed
+    __syncwarp();
+    if (hi - lo <= Q::CHUNK)
+      lean_whole<LP, kEnv>(a, n, lo, hi, g, q, bufs[b],
+                           reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
+    else
+      lean_big<LP, kEnv>(a, n, lo, hi, g, q);
+    __syncwarp();  // every lane is done with bufs[b] before it is refilled
+    lo = hi;
+    hi = nhi;
+    nhi = nnhi;
+    b ^= 1;
+  }
+  cp_async_wait<0>();
 }
 
 // ---- backward -------------------------------------------------------------
@@ -1161,8 +1289,13 @@ SmxConfig smx_make(bool backward) {
 template <int LP, bool kEnv, bool kLean = false>
 SmxConfig quad_make_env() {
   SmxConfig c;
-  c.main = segment_softmax_quad_kernel<LP, false, kEnv, kLean>;
-  c.split = segment_softmax_quad_kernel<LP, true, kEnv>;
+  if constexpr (kLean) {
+    c.main = segment_softmax_whole_kernel<LP, kEnv>;
+    c.split = nullptr;  // no segment is split
+  } else {
+    c.main = segment_softmax_quad_kernel<LP, false, kEnv>;
+    c.split = segment_softmax_quad_kernel<LP, true, kEnv>;
+  }
   c.tc = 4 * LP;
   c.tiles = 1;
   c.main_smem = quad_pipelined<LP>() ? kWarpsPerBlock * QuadStage<LP>::kWarpBytes : 0;
@@ -1270,10 +1403,13 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
 
 int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
             const int64_t* offsets, cudaStream_t s, const char* name) {
-  // Tickets and the big-split flag after them start at zero.
-  int st = cuda_check(
-      cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * (L.plan.parts * L.cfg.tiles + 1), s),
-      "segment softmax: ticket reset");
+  // Tickets and the big-split flag after them start at zero (kernels that
+  // split no segment have no second pass and use neither).
+  int st = BYSJ_OK;
+  if (L.cfg.split != nullptr)
+    st = cuda_check(
+        cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * (L.plan.parts * L.cfg.tiles + 1), s),
+        "segment softmax: ticket reset");
   if (st) return st;
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
@@ -1284,7 +1420,7 @@ int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
   L.cfg.main<<<grid, kBlock, L.cfg.main_smem, s>>>(a);
   st = launch_check(name);
-  if (st) return st;
+  if (st || L.cfg.split == nullptr) return st;
   L.cfg.split<<<grid, kBlock, 0, s>>>(a);
   return launch_check(name);
 }
