@@ -230,14 +230,18 @@ __device__ __forceinline__ void quad_set(float4& v, int i, float x) {
   if (i == 0) v.x = x; else if (i == 1) v.y = x; else if (i == 2) v.z = x; else v.w = x;
 }
 
-// Rows of slots base + g + t*G (t < T) that lie below `hi`.
-template <int LP>
-__device__ __forceinline__ int quad_rows(int64_t base, int64_t hi, int g) {
+// Rows of slots base + g + t*G (t < TT) that lie below `hi`.
+template <int LP, int TT>
+__device__ __forceinline__ int quad_rows_n(int64_t base, int64_t hi, int g) {
   using Q = QuadSmx<LP>;
   const int64_t left = hi - base - g;
   if (left <= 0) return 0;
   const int64_t r = (left + Q::G - 1) / Q::G;
-  return r < Q::T ? static_cast<int>(r) : Q::T;
+  return r < TT ? static_cast<int>(r) : TT;
+}
+template <int LP>
+__device__ __forceinline__ int quad_rows(int64_t base, int64_t hi, int g) {
+  return quad_rows_n<LP, QuadSmx<LP>::T>(base, hi, g);
 }
 
 // Loads the gated logits of slots base + g + t*G (t < T) into x (-inf past
@@ -1077,15 +1081,15 @@ __global__ void __launch_bounds__(kBlock) segment_softmax_bwd_split_kernel(SmxAr
 // and the write.  Split segments publish partial S; the last piece combines
 // them and writes segments of up to kSelfWrite edges itself, longer ones in
 // the equally partitioned second pass.
-template <int LP>
+template <int LP, int TT = QuadSmx<LP>::T>
 __device__ __forceinline__ void quad_bwd_load(const SmxArgs& a, int64_t base, int64_t hi, int g,
-                                              int q, bool qok, float4 (&al)[QuadSmx<LP>::T],
-                                              float4 (&gr)[QuadSmx<LP>::T]) {
+                                              int q, bool qok, float4 (&al)[TT],
+                                              float4 (&gr)[TT]) {
   using Q = QuadSmx<LP>;
-  const int mine = qok ? quad_rows<LP>(base, hi, g) : 0;
+  const int mine = qok ? quad_rows_n<LP, TT>(base, hi, g) : 0;
   const int64_t cq = a.channels / 4;
 #pragma unroll
-  for (int t = 0; t < Q::T; ++t) {
+  for (int t = 0; t < TT; ++t) {
     al[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     gr[t] = al[t];
     if (t < mine) {
@@ -1098,16 +1102,15 @@ __device__ __forceinline__ void quad_bwd_load(const SmxArgs& a, int64_t base, in
 }
 
 // Writes grad_logit (and grad_env) of slots base + g + t G from rows in registers.
-template <int LP>
+template <int LP, int TT = QuadSmx<LP>::T>
 __device__ __forceinline__ void quad_bwd_store(const SmxArgs& a, int64_t base, int64_t hi, int g,
-                                               int q, bool qok, const float4 (&al)[QuadSmx<LP>::T],
-                                               const float4 (&gr)[QuadSmx<LP>::T],
-                                               const float (&S)[4]) {
+                                               int q, bool qok, const float4 (&al)[TT],
+                                               const float4 (&gr)[TT], const float (&S)[4]) {
   using Q = QuadSmx<LP>;
-  const int rows = quad_rows<LP>(base, hi, g);
+  const int rows = quad_rows_n<LP, TT>(base, hi, g);
   const int64_t cq = a.channels / 4;
 #pragma unroll
-  for (int t = 0; t < Q::T; ++t) {
+  for (int t = 0; t < TT; ++t) {
     const int64_t slot = base + g + static_cast<int64_t>(t) * Q::G;
     const bool live = t < rows;
     const int64_t e = live ? (a.order ? __ldg(a.order + slot) : slot) : 0;
@@ -1248,6 +1251,79 @@ __global__ void __launch_bounds__(kBlock, 2) segment_softmax_quad_bwd_kernel(Smx
   }
 }
 
+// Backward over whole-segment partitions (as the forward whole kernel): warp
+// p takes every segment whose start diagonal lies in its partition, so no
+// partial S is published and there is no second pass.  A segment of up to one
+// chunk keeps its rows in registers between the sum and the write; a longer
+// one reads its rows twice (the second time from L1).
+// Rows per lane per chunk of the whole backward kernel.  Four rows, at four
+// CTAs per SM (64 registers), measured faster than eight rows kept in
+// registers at two or three CTAs: the kernel waits on memory, and a longer
+// segment re-reads its rows from L1 in the second pass.
+constexpr int kBwdT = 4;
+
+template <int LP>
+__global__ void __launch_bounds__(kBlock, 4) segment_softmax_whole_bwd_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  constexpr int TT = kBwdT;
+  constexpr int64_t kChunk = static_cast<int64_t>(Q::G) * TT;
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t C = a.channels;
+  const bool qok = 4 * q < C;
+  const int64_t n0 = starts_before(a.mp, p * a.mp.ipc);
+  const int64_t n1 = starts_before(a.mp, (p + 1) * a.mp.ipc);
+  if (n0 >= n1) return;
+  const int64_t* off = a.mp.offsets;
+  int64_t lo = __ldg(off + n0);
+  int64_t hi = __ldg(off + n0 + 1);
+  for (int64_t n = n0; n < n1; ++n) {
+    const int64_t nhi = n + 1 < n1 ? __ldg(off + n + 2) : hi;
+    float4 al[TT], gr[TT];
+    float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+    for (int64_t base = lo; base < hi; base += kChunk) {
+      quad_bwd_load<LP, TT>(a, base, hi, g, q, qok, al, gr);
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        S[0] = fmaf(al[t].x, gr[t].x, S[0]);
+        S[1] = fmaf(al[t].y, gr[t].y, S[1]);
+        S[2] = fmaf(al[t].z, gr[t].z, S[2]);
+        S[3] = fmaf(al[t].w, gr[t].w, S[3]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      for (int st = LP; st < kWarp; st <<= 1) S[i] += __shfl_xor_sync(kFull, S[i], st);
+    if (a.xn && qok) {
+      const float4 a0 = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.yn + n * C) + q);
+      S[0] = fmaf(a0.x, g0.x, S[0]);
+      S[1] = fmaf(a0.y, g0.y, S[1]);
+      S[2] = fmaf(a0.z, g0.z, S[2]);
+      S[3] = fmaf(a0.w, g0.w, S[3]);
+      if (g == 0)
+        reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+            make_float4(a0.x * (g0.x - S[0]), a0.y * (g0.y - S[1]), a0.z * (g0.z - S[2]),
+                        a0.w * (g0.w - S[3]));
+    }
+    if (hi - lo <= kChunk) {
+      quad_bwd_store<LP, TT>(a, lo, hi, g, q, qok, al, gr, S);
+    } else {
+#pragma unroll 1
+      for (int64_t base = lo; base < hi; base += kChunk) {
+        quad_bwd_load<LP, TT>(a, base, hi, g, q, qok, al, gr);
+        quad_bwd_store<LP, TT>(a, base, hi, g, q, qok, al, gr, S);
+      }
+    }
+    lo = hi;
+    hi = nhi;
+  }
+}
+
 // grad_env for channel counts wider than one warp tile.
 __global__ void __launch_bounds__(kBlock)
     segment_softmax_env_kernel(const float* __restrict__ grad_logit,
@@ -1316,8 +1392,8 @@ SmxConfig quad_make_lean(bool env) {
 template <int LP>
 SmxConfig quad_bwd_make() {
   SmxConfig c;
-  c.main = segment_softmax_quad_bwd_kernel<LP, false>;
-  c.split = segment_softmax_quad_bwd_kernel<LP, true>;
+  c.main = segment_softmax_whole_bwd_kernel<LP>;
+  c.split = nullptr;  // no segment is split
   c.tc = 4 * LP;
   c.tiles = 1;
   return c;
