@@ -16,9 +16,9 @@
 // partial statistics, the last piece to finish combines them in partition
 // order into a final-statistics slot, and a second, equally partitioned
 // kernel writes the per-edge outputs of those segments.  The forward pass
-// for C = 4 or 8 with rows in storage order (the attention widths) instead
-// gives each warp whole segments (segment_softmax_whole_kernel): no split,
-// no second pass.
+// for C = 4, 8 or 16 with rows in storage order (the attention widths)
+// instead gives each warp whole segments (segment_softmax_whole_kernel): no
+// split, no second pass.
 #include "launch.cuh"
 
 namespace bysj {
@@ -1374,7 +1374,7 @@ SmxConfig quad_make_env() {
   }
   c.tc = 4 * LP;
   c.tiles = 1;
-  c.main_smem = quad_pipelined<LP>() ? kWarpsPerBlock * QuadStage<LP>::kWarpBytes : 0;
+  c.main_smem = (kLean || quad_pipelined<LP>()) ? kWarpsPerBlock * QuadStage<LP>::kWarpBytes : 0;
   return c;
 }
 
@@ -1383,7 +1383,9 @@ SmxConfig quad_make(bool env) {
   return env ? quad_make_env<LP, true>() : quad_make_env<LP, false>();
 }
 
-// C == 4 LP with rows in storage order (LP <= 2, the pipelined widths).
+// C == 4 LP with rows in storage order (C = 4, 8 or 16): whole-segment
+// partitions.  At C = 16 a chunk is 64 rows, so typical segments take the
+// two-read path of lean_big.
 template <int LP>
 SmxConfig quad_make_lean(bool env) {
   return env ? quad_make_env<LP, true, true>() : quad_make_env<LP, false, true>();
@@ -1405,6 +1407,7 @@ SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = t
   if (!backward && quad_ok && lean) {
     if (channels == 4) return quad_make_lean<1>(env);
     if (channels == 8) return quad_make_lean<2>(env);
+    if (channels == 16) return quad_make_lean<4>(env);
   }
   if (backward && quad_ok && channels % 4 == 0 && channels <= 128) {
     switch (next_pow2(channels / 4)) {
