@@ -194,6 +194,28 @@ __device__ __forceinline__ int64_t global_warp() {
   return (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
 }
 
+// Asynchronous global -> shared copies (LDGSTS) of 16 or 4 bytes, committed
+// in groups and waited on by group count.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<unsigned>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Butterfly sum over the lanes that differ in bits [lo_bit, 5).  Every
 // participating lane ends with the same value: each step adds two operands
 // in either order, and fp32 addition is commutative.
@@ -286,6 +308,31 @@ struct MergePath {
     }
     const int64_t probe = lo + lane;
     const bool before = probe < hi && (__ldg(offsets + probe + 1) + probe < d);
+    return lo + __popc(__ballot_sync(kFull, before));
+  }
+
+  // Number of segments whose start diagonal offsets[n] + n lies below d
+  // (warp-wide; every lane returns the same value).  Partition p of a
+  // whole-segment kernel owns segments [starts_before(p ipc),
+  // starts_before((p + 1) ipc)): every segment exactly once, never split.
+  __device__ __forceinline__ int64_t starts_before(int64_t d) const {
+    const int lane = lane_id();
+    if (d > n_edges + n_nodes) d = n_edges + n_nodes;  // the last partition's end
+    int64_t lo = d > n_edges ? d - n_edges : 0;
+    int64_t hi = d < n_nodes ? d : n_nodes;
+    while (hi - lo > kWarp) {
+      const int64_t step = (hi - lo + kWarp - 1) / kWarp;
+      const int64_t probe = lo + lane * step;
+      const bool before = probe < hi && (__ldg(offsets + probe) + probe < d);
+      const int cnt = __popc(__ballot_sync(kFull, before));
+      if (cnt == 0) return lo;
+      const int64_t new_lo = lo + (cnt - 1) * step + 1;
+      const int64_t new_hi = lo + cnt * step;
+      lo = new_lo;
+      hi = new_hi < hi ? new_hi : hi;
+    }
+    const int64_t probe = lo + lane;
+    const bool before = probe < hi && (__ldg(offsets + probe) + probe < d);
     return lo + __popc(__ballot_sync(kFull, before));
   }
 

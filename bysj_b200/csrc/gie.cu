@@ -303,7 +303,9 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
 // 4-channel share of grad_zonal is summed over the LPE lanes of its edge (in
 // lane order).  pre is summed over all the segment's edges (edge groups
 // merged, split pieces combined) before the single dot product, as the
-// forward normalises after its sum.
+// forward normalises after its sum.  The radial rows of the next step
+// (32 / LPE edges) are copied into a shared double buffer (cp.async) while
+// the current step is computed.
 constexpr int kTilePitch = 17;  // floats per lane row of the fold tile
 
 template <int LPE, int L>
@@ -312,7 +314,11 @@ struct GieBwdSmem {
   static constexpr size_t kG = sizeof(float4) * R * LPE;
   static constexpr size_t kZ = sizeof(float) * kZonalChunk * R;
   static constexpr size_t kT = sizeof(float) * kWarp * kTilePitch;
-  static constexpr size_t kWarpBytes = (kG + kZ + kT + 15) / 16 * 16;
+  // Radial quads of one step (32 / LPE edges x L degrees x LPE lanes), two
+  // steps: the next step's rows are copied in while this step is computed.
+  static constexpr int kRadQuads = kWarp * L;
+  static constexpr size_t kRad = 2 * sizeof(float4) * kRadQuads;
+  static constexpr size_t kWarpBytes = (kG + kZ + kT + kRad + 15) / 16 * 16;
 };
 
 template <int LPE, int L>
@@ -329,6 +335,7 @@ __global__ void __launch_bounds__(kBlock, 2)
   float4* gq = reinterpret_cast<float4*>(mine_smem);
   float* zb = reinterpret_cast<float*>(mine_smem + M::kG);
   float* tile = reinterpret_cast<float*>(mine_smem + M::kG + M::kZ);
+  float4* rbuf = reinterpret_cast<float4*>(mine_smem + M::kG + M::kZ + M::kT);
   const int lane = lane_id();
   const int eg = lane / LPE;
   const int c4 = lane % LPE;
@@ -350,6 +357,20 @@ __global__ void __launch_bounds__(kBlock, 2)
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+    // Copies the radial quads of the step whose first edge is `base` into
+    // buffer b; a lane past the segment's end copies the step's first edge
+    // (in range), so its unused quads are finite.
+    auto radial_issue = [&](int64_t base, int b) {
+      const int64_t k = base + eg < cur.hi ? base + eg : base;
+      const int64_t e = a.order ? __ldg(a.order + k) : k;
+      const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
+      float4* dst = rbuf + b * M::kRadQuads + eg * L * LPE + c4;
+#pragma unroll
+      for (int l = 1; l <= L; ++l) cp_async16(dst + (l - 1) * LPE, rr + l * C);
+    };
+    int rb = 0;
+    if (cur.lo < cur.hi) radial_issue(cur.lo, rb);  // an empty piece copies nothing
+    cp_async_commit();
     for (int64_t lo = cur.lo; lo < cur.hi; lo += kZonalChunk) {  // warp-uniform
       const int rows = static_cast<int>(cur.hi - lo < kZonalChunk ? cur.hi - lo : kZonalChunk);
       __syncwarp();
@@ -364,16 +385,21 @@ __global__ void __launch_bounds__(kBlock, 2)
       }
       __syncwarp();
       for (int k0 = 0; k0 < rows; k0 += EG) {  // warp-uniform
+        if (lo + k0 + EG < cur.hi) radial_issue(lo + k0 + EG, rb ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();  // this step's radial quads have landed
+        __syncwarp();
         const int k = k0 + eg;
         const bool valid = k < rows;
         const int kk = valid ? k : 0;
         const int64_t slot = lo + kk;
         const int64_t e = a.order ? __ldg(a.order + slot) : slot;
-        const float* rr = a.radial + e * radial_row + 4 * c4;
         const float* z = zb + kk * R;
+        const float4* qs = rbuf + rb * M::kRadQuads + eg * L * LPE + c4;
+        rb ^= 1;
 #pragma unroll
         for (int l = 1; l <= L; ++l) {
-          const float4 q = ld_stream_f4(rr + (slot_base + l) * C);
+          const float4 q = qs[(l - 1) * LPE];
           float4 gr = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
           for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
@@ -412,6 +438,7 @@ __global__ void __launch_bounds__(kBlock, 2)
         __syncwarp();  // the tile is read before the next edge overwrites it
       }
     }
+    cp_async_wait<0>();
     if constexpr (EG > 1) {
 #pragma unroll
       for (int r = 0; r < R; ++r)

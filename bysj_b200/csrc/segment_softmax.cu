@@ -328,28 +328,6 @@ __device__ __forceinline__ void quad_write(const SmxArgs& a, int64_t base, int64
   quad_store<LP>(a, base, hi, g, q, qok, x);
 }
 
-// Asynchronous global -> shared copies (LDGSTS): 16 bytes of a logit row
-// quad, or one 4-byte envelope value.
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   static_cast<unsigned>(__cvta_generic_to_shared(smem))),
-               "l"(gmem)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
-                   static_cast<unsigned>(__cvta_generic_to_shared(smem))),
-               "l"(gmem)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Reads of a staged chunk through explicit shared-memory addresses (the
 // buffers are picked at run time, which would otherwise leave generic loads).
 // volatile: kept in order with the cp.async waits above them.
@@ -794,29 +772,6 @@ __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
 // there are no partial statistics, tickets or second pass; the imbalance is
 // at most one segment (<= CHUNK rows in the pipelined case).
 
-// Number of segments n < N whose start diagonal offsets[n] + n lies below d
-// (warp-wide; every lane returns the same value).  32-ary search.
-__device__ __forceinline__ int64_t starts_before(const MergePath& mp, int64_t d) {
-  const int lane = lane_id();
-  if (d > mp.n_edges + mp.n_nodes) d = mp.n_edges + mp.n_nodes;  // the last partition's end
-  int64_t lo = d > mp.n_edges ? d - mp.n_edges : 0;
-  int64_t hi = d < mp.n_nodes ? d : mp.n_nodes;
-  while (hi - lo > kWarp) {
-    const int64_t step = (hi - lo + kWarp - 1) / kWarp;
-    const int64_t probe = lo + lane * step;
-    const bool before = probe < hi && (__ldg(mp.offsets + probe) + probe < d);
-    const int cnt = __popc(__ballot_sync(kFull, before));
-    if (cnt == 0) return lo;
-    const int64_t new_lo = lo + (cnt - 1) * step + 1;
-    const int64_t new_hi = lo + cnt * step;
-    lo = new_lo;
-    hi = new_hi < hi ? new_hi : hi;
-  }
-  const int64_t probe = lo + lane;
-  const bool before = probe < hi && (__ldg(mp.offsets + probe) + probe < d);
-  return lo + __popc(__ballot_sync(kFull, before));
-}
-
 // A whole segment longer than one chunk: running (max, sum) per channel over
 // chunks read from global memory, merged over the edge groups, then a second
 // read for the weights (as quad_segment's multi-chunk whole path).
@@ -890,8 +845,8 @@ __global__ void __launch_bounds__(kBlock, 3) segment_softmax_whole_kernel(SmxArg
   const int lane = lane_id();
   const int g = lane / LP;
   const int q = lane % LP;
-  const int64_t n0 = starts_before(a.mp, p * a.mp.ipc);
-  const int64_t n1 = starts_before(a.mp, (p + 1) * a.mp.ipc);
+  const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
+  const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
   if (n0 >= n1) return;
   char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
   float4* bufs[2] = {reinterpret_cast<float4*>(mine), reinterpret_cast<float4*>(mine + S::kBytes)};
@@ -1274,8 +1229,8 @@ __global__ void __launch_bounds__(kBlock, 4) segment_softmax_whole_bwd_kernel(Sm
   const int q = lane % LP;
   const int64_t C = a.channels;
   const bool qok = 4 * q < C;
-  const int64_t n0 = starts_before(a.mp, p * a.mp.ipc);
-  const int64_t n1 = starts_before(a.mp, (p + 1) * a.mp.ipc);
+  const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
+  const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
   if (n0 >= n1) return;
   const int64_t* off = a.mp.offsets;
   int64_t lo = __ldg(off + n0);
