@@ -299,6 +299,17 @@ class Flusher:
 
 
 def time_launches(fn, iters, flush=None):
+    """Trimmed mean CUDA-event time of `fn` over `iters` launches (L2 flushed
+    before each when `flush` is given): the fastest and slowest tenth (at
+    least one each) are dropped.  Single launches of a few tens of
+    microseconds land on a coarse grid of event timestamps, so a median sits
+    on a grid point while a mean does not; the trimming keeps a rare stalled
+    iteration (operators that wait on the host) out of the mean.  One untimed
+    call first: an operator's first call pays for caching its workspace."""
+    if flush is not None:
+        flush()
+    fn()
+    torch.cuda.synchronize()
     times = []
     for _ in range(iters):
         if flush is not None:
@@ -309,7 +320,9 @@ def time_launches(fn, iters, flush=None):
         b.record()
         b.synchronize()
         times.append(a.elapsed_time(b) / 1e3)
-    return statistics.median(times)
+    times.sort()
+    cut = max(1, len(times) // 10) if len(times) > 2 else 0
+    return statistics.mean(times[cut:len(times) - cut])
 
 
 def op_line(name, alg_bytes, seconds, peak, edges=None, extra=None):
@@ -571,7 +584,7 @@ OPS = {
 }
 
 
-def op_context(g, device, peak, logit=None, value32=None, iters=10):
+def op_context(g, device, peak, logit=None, value32=None, iters=20):
     """Shared inputs of the per-op lines; logits / values built on demand."""
     from bysj_b200 import _C
 
@@ -597,7 +610,7 @@ def op_context(g, device, peak, logit=None, value32=None, iters=10):
     }
 
 
-def measure_ops(g, logit, value32, device, peak, iters=10, only=None):
+def measure_ops(g, logit, value32, device, peak, iters=20, only=None):
     ctx = op_context(g, device, peak, logit, value32, iters)
     out = {}
     for name, fn in OPS.items():
