@@ -8,8 +8,9 @@ namespace bysj {
 constexpr int kBlock = 256;           // 8 warps per CTA
 constexpr int kWarpsPerBlock = kBlock / kWarp;
 
-// Resident CTAs per SM for `kernel` at kBlock threads (cached per device).
-int resident_blocks(const void* kernel, size_t dynamic_smem = 0);
+// Resident CTAs per SM for `kernel` at `threads` threads per CTA (cached per
+// device).
+int resident_blocks(const void* kernel, size_t dynamic_smem = 0, int threads = kBlock);
 // Raises the kernel's dynamic shared memory limit to `bytes` (needed above
 // 48 KB) once per kernel and device; BYSJ_OK or an error status.
 int allow_dynamic_smem(const void* kernel, size_t bytes);

@@ -22,14 +22,15 @@ struct OccKey {
   const void* kernel;
   int device;
   size_t smem;
+  int threads;
   bool operator==(const OccKey& o) const {
-    return kernel == o.kernel && device == o.device && smem == o.smem;
+    return kernel == o.kernel && device == o.device && smem == o.smem && threads == o.threads;
   }
 };
 struct OccHash {
   size_t operator()(const OccKey& k) const {
     return std::hash<const void*>()(k.kernel) ^ (size_t(k.device) << 40) ^
-           (k.smem << 8);
+           (k.smem << 8) ^ (size_t(k.threads) << 52);
   }
 };
 std::unordered_map<OccKey, int, OccHash> g_occupancy;
@@ -94,9 +95,9 @@ int allow_dynamic_smem(const void* kernel, size_t bytes) {
   return st;
 }
 
-int resident_blocks(const void* kernel, size_t dynamic_smem) {
+int resident_blocks(const void* kernel, size_t dynamic_smem, int threads) {
   const DeviceInfo& info = current_device_info();
-  OccKey key{kernel, info.device, dynamic_smem};
+  OccKey key{kernel, info.device, dynamic_smem, threads};
   {
     std::lock_guard<std::mutex> lock(g_mutex);
     auto it = g_occupancy.find(key);
@@ -104,7 +105,7 @@ int resident_blocks(const void* kernel, size_t dynamic_smem) {
   }
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-          &blocks, kernel, kBlock, dynamic_smem) != cudaSuccess ||
+          &blocks, kernel, threads, dynamic_smem) != cudaSuccess ||
       blocks < 1) {
     cudaGetLastError();
     blocks = 1;

@@ -1206,29 +1206,79 @@ __global__ void __launch_bounds__(kBlock, 2) segment_softmax_quad_bwd_kernel(Smx
   }
 }
 
+// Adds the null term to S (S += null_alpha g0) and writes grad_null_logit.
+template <int LP>
+__device__ __forceinline__ void bwd_null(const SmxArgs& a, int64_t n, int g, int q, bool qok,
+                                         float (&S)[4]) {
+  if (!a.xn || !qok) return;
+  const int64_t C = a.channels;
+  const float4 a0 = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
+  const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.yn + n * C) + q);
+  S[0] = fmaf(a0.x, g0.x, S[0]);
+  S[1] = fmaf(a0.y, g0.y, S[1]);
+  S[2] = fmaf(a0.z, g0.z, S[2]);
+  S[3] = fmaf(a0.w, g0.w, S[3]);
+  if (g == 0)
+    reinterpret_cast<float4*>(a.out_null + n * C)[q] =
+        make_float4(a0.x * (g0.x - S[0]), a0.y * (g0.y - S[1]), a0.z * (g0.z - S[2]),
+                    a0.w * (g0.w - S[3]));
+}
+
 // Backward over whole-segment partitions (as the forward whole kernel): warp
 // p takes every segment whose start diagonal lies in its partition, so no
 // partial S is published and there is no second pass.  A segment of up to one
 // chunk keeps its rows in registers between the sum and the write; a longer
 // one reads its rows twice (the second time from L1).
-// Rows per lane per chunk of the whole backward kernel.  Four rows, at four
-// CTAs per SM (64 registers), measured faster than eight rows kept in
-// registers at two or three CTAs: the kernel waits on memory, and a longer
-// segment re-reads its rows from L1 in the second pass.
+
+// Rows per lane per chunk of the register form.  Four rows, at four CTAs per
+// SM (64 registers), measured faster than eight rows kept in registers at
+// two or three CTAs: the kernel waits on memory, and a longer segment
+// re-reads its rows from L1 in the second pass.
 constexpr int kBwdT = 4;
+
+// One whole segment [lo, hi) from global memory (register form).
+template <int LP, int TT>
+__device__ __forceinline__ void bwd_segment_global(const SmxArgs& a, int64_t n, int64_t lo,
+                                                   int64_t hi, int g, int q, bool qok) {
+  using Q = QuadSmx<LP>;
+  constexpr int64_t kChunk = static_cast<int64_t>(Q::G) * TT;
+  const int64_t C = a.channels;
+  float4 al[TT], gr[TT];
+  float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+  for (int64_t base = lo; base < hi; base += kChunk) {
+    quad_bwd_load<LP, TT>(a, base, hi, g, q, qok, al, gr);
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      S[0] = fmaf(al[t].x, gr[t].x, S[0]);
+      S[1] = fmaf(al[t].y, gr[t].y, S[1]);
+      S[2] = fmaf(al[t].z, gr[t].z, S[2]);
+      S[3] = fmaf(al[t].w, gr[t].w, S[3]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    for (int st = LP; st < kWarp; st <<= 1) S[i] += __shfl_xor_sync(kFull, S[i], st);
+  bwd_null<LP>(a, n, g, q, qok, S);
+  if (hi - lo <= kChunk) {
+    quad_bwd_store<LP, TT>(a, lo, hi, g, q, qok, al, gr, S);
+  } else {
+#pragma unroll 1
+    for (int64_t base = lo; base < hi; base += kChunk) {
+      quad_bwd_load<LP, TT>(a, base, hi, g, q, qok, al, gr);
+      quad_bwd_store<LP, TT>(a, base, hi, g, q, qok, al, gr, S);
+    }
+  }
+}
 
 template <int LP>
 __global__ void __launch_bounds__(kBlock, 4) segment_softmax_whole_bwd_kernel(SmxArgs a) {
-  using Q = QuadSmx<LP>;
-  constexpr int TT = kBwdT;
-  constexpr int64_t kChunk = static_cast<int64_t>(Q::G) * TT;
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
   const int lane = lane_id();
   const int g = lane / LP;
   const int q = lane % LP;
-  const int64_t C = a.channels;
-  const bool qok = 4 * q < C;
+  const bool qok = 4 * q < a.channels;
   const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
   const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
   if (n0 >= n1) return;
@@ -1237,46 +1287,144 @@ __global__ void __launch_bounds__(kBlock, 4) segment_softmax_whole_bwd_kernel(Sm
   int64_t hi = __ldg(off + n0 + 1);
   for (int64_t n = n0; n < n1; ++n) {
     const int64_t nhi = n + 1 < n1 ? __ldg(off + n + 2) : hi;
-    float4 al[TT], gr[TT];
-    float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-    for (int64_t base = lo; base < hi; base += kChunk) {
-      quad_bwd_load<LP, TT>(a, base, hi, g, q, qok, al, gr);
-#pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        S[0] = fmaf(al[t].x, gr[t].x, S[0]);
-        S[1] = fmaf(al[t].y, gr[t].y, S[1]);
-        S[2] = fmaf(al[t].z, gr[t].z, S[2]);
-        S[3] = fmaf(al[t].w, gr[t].w, S[3]);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      for (int st = LP; st < kWarp; st <<= 1) S[i] += __shfl_xor_sync(kFull, S[i], st);
-    if (a.xn && qok) {
-      const float4 a0 = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.yn + n * C) + q);
-      S[0] = fmaf(a0.x, g0.x, S[0]);
-      S[1] = fmaf(a0.y, g0.y, S[1]);
-      S[2] = fmaf(a0.z, g0.z, S[2]);
-      S[3] = fmaf(a0.w, g0.w, S[3]);
-      if (g == 0)
-        reinterpret_cast<float4*>(a.out_null + n * C)[q] =
-            make_float4(a0.x * (g0.x - S[0]), a0.y * (g0.y - S[1]), a0.z * (g0.z - S[2]),
-                        a0.w * (g0.w - S[3]));
-    }
-    if (hi - lo <= kChunk) {
-      quad_bwd_store<LP, TT>(a, lo, hi, g, q, qok, al, gr, S);
-    } else {
-#pragma unroll 1
-      for (int64_t base = lo; base < hi; base += kChunk) {
-        quad_bwd_load<LP, TT>(a, base, hi, g, q, qok, al, gr);
-        quad_bwd_store<LP, TT>(a, base, hi, g, q, qok, al, gr, S);
-      }
-    }
+    bwd_segment_global<LP, kBwdT>(a, n, lo, hi, g, q, qok);
     lo = hi;
     hi = nhi;
   }
+}
+
+// Backward for C = 4 LP exactly (LP <= 2) with shared-memory staging, as the
+// forward whole kernel: while a warp computes one segment from shared memory
+// (S from one pass over the staged alpha and grad_alpha rows, grad_logit and
+// grad_env from a second), the next segment's rows and envelopes are copied
+// into its other buffer (cp.async).  The rows of a lane are summed in the same
+// order as in the register form, so both give the same bits.  Segments longer
+// than a chunk take the register form.  Four-warp CTAs, 17 KB of buffers per
+// warp at LP = 2 (the width it is used for).
+constexpr int kStagedBwdBlock = 128;
+
+template <int LP>
+struct BwdStage {
+  static constexpr int G = kWarp / LP;
+  static constexpr int T = 8;
+  static constexpr int CHUNK = G * T;
+  static constexpr int kRowsF4 = T * kWarp;  // float4 per staged array
+  static constexpr size_t kBytes = 2 * sizeof(float4) * kRowsF4 + sizeof(float) * CHUNK;
+  static constexpr size_t kWarpBytes = 2 * kBytes;
+  static_assert(kBytes % 16 == 0, "stage buffers must stay 16-byte aligned");
+};
+
+template <int LP>
+__device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t hi, int g, int q,
+                                          char* buf) {
+  using B = BwdStage<LP>;
+  constexpr int C = 4 * LP;
+  const int rows = quad_rows_n<LP, B::T>(lo, hi, g);
+  const int lane = g * LP + q;
+  float4* al = reinterpret_cast<float4*>(buf);
+  float4* gr = al + B::kRowsF4;
+  float* env = reinterpret_cast<float*>(gr + B::kRowsF4);
+#pragma unroll
+  for (int t = 0; t < B::T; ++t) {
+    if (t < rows) {
+      const int64_t slot = lo + g + static_cast<int64_t>(t) * B::G;
+      const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+      cp_async16(al + t * kWarp + lane, a.x + e * C + 4 * q);
+      cp_async16(gr + t * kWarp + lane, a.y + e * C + 4 * q);
+      if (a.env && q == 0) cp_async4(env + t * B::G + g, a.env + e);
+    }
+  }
+}
+
+template <int LP>
+__device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, int64_t lo,
+                                                   int64_t hi, int g, int q, const char* buf) {
+  using B = BwdStage<LP>;
+  constexpr int C = 4 * LP;
+  const int rows = quad_rows_n<LP, B::T>(lo, hi, g);
+  const int lane = g * LP + q;
+  const uint32_t al_s = smem_addr(buf) + 16u * lane;
+  const uint32_t gr_s = al_s + 16u * B::kRowsF4;
+  const uint32_t env_s = smem_addr(buf) + 32u * B::kRowsF4 + 4u * g;
+  float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int t = 0; t < B::T; ++t) {
+    if (t < rows) {
+      const float4 al = lds_f4(al_s + 16u * t * kWarp);
+      const float4 gr = lds_f4(gr_s + 16u * t * kWarp);
+      S[0] = fmaf(al.x, gr.x, S[0]);
+      S[1] = fmaf(al.y, gr.y, S[1]);
+      S[2] = fmaf(al.z, gr.z, S[2]);
+      S[3] = fmaf(al.w, gr.w, S[3]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int st = LP; st < kWarp; st <<= 1) S[i] += __shfl_xor_sync(kFull, S[i], st);
+  bwd_null<LP>(a, n, g, q, true, S);
+#pragma unroll
+  for (int t = 0; t < B::T; ++t) {
+    const bool live = t < rows;
+    float4 al = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gr = al;
+    if (live) {
+      al = lds_f4(al_s + 16u * t * kWarp);
+      gr = lds_f4(gr_s + 16u * t * kWarp);
+    }
+    const float4 gl = make_float4(al.x * (gr.x - S[0]), al.y * (gr.y - S[1]),
+                                  al.z * (gr.z - S[2]), al.w * (gr.w - S[3]));
+    const int64_t slot = lo + g + static_cast<int64_t>(t) * B::G;
+    const int64_t e = live ? (a.order ? __ldg(a.order + slot) : slot) : 0;
+    if (live) reinterpret_cast<float4*>(a.out)[e * LP + q] = gl;
+    if (a.out_env) {
+      float rowsum = (gl.x + gl.y) + (gl.z + gl.w);
+      if constexpr (LP > 1) rowsum = group_sum(rowsum, LP);
+      if (live && q == 0) {
+        const float env = a.env ? lds_f32(env_s + 4u * t * B::G) : 1.0f;
+        a.out_env[e] = env > 0.0f ? rowsum * 2.0f / env : 0.0f;
+      }
+    }
+  }
+}
+
+template <int LP>
+__global__ void __launch_bounds__(kStagedBwdBlock) segment_softmax_staged_bwd_kernel(SmxArgs a) {
+  using B = BwdStage<LP>;
+  extern __shared__ float4 quad_smem[];
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
+  const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
+  if (n0 >= n1) return;
+  char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * B::kWarpBytes;
+  char* bufs[2] = {mine, mine + B::kBytes};
+  const int64_t* off = a.mp.offsets;
+  // Segment n is [lo, hi); the next one ends at nhi.
+  int64_t lo = __ldg(off + n0), hi = __ldg(off + n0 + 1);
+  int64_t nhi = n0 + 1 < n1 ? __ldg(off + n0 + 2) : hi;
+  if (hi - lo <= B::CHUNK) bwd_stage<LP>(a, lo, hi, g, q, bufs[0]);
+  cp_async_commit();
+  int b = 0;
+  for (int64_t n = n0; n < n1; ++n) {
+    const int64_t nnhi = n + 2 < n1 ? __ldg(off + n + 3) : nhi;
+    if (n + 1 < n1 && nhi - hi <= B::CHUNK) bwd_stage<LP>(a, hi, nhi, g, q, bufs[b ^ 1]);
+    cp_async_commit();
+    cp_async_wait<1>();  // this segment's copies have landed
+    __syncwarp();
+    if (hi - lo <= B::CHUNK)
+      bwd_segment_staged<LP>(a, n, lo, hi, g, q, bufs[b]);
+    else
+      bwd_segment_global<LP, kBwdT>(a, n, lo, hi, g, q, true);
+    __syncwarp();  // every lane is done with bufs[b] before it is refilled
+    lo = hi;
+    hi = nhi;
+    nhi = nnhi;
+    b ^= 1;
+  }
+  cp_async_wait<0>();
 }
 
 // grad_env for channel counts wider than one warp tile.
@@ -1305,6 +1453,7 @@ struct SmxConfig {
   SmxKernel main = nullptr, split = nullptr;
   int64_t tc = 0, tiles = 1;
   size_t main_smem = 0;  // dynamic shared memory of the main launch
+  int block = kBlock;    // threads per CTA of the main launch
 };
 
 template <int NC, int G>
@@ -1347,6 +1496,18 @@ SmxConfig quad_make_lean(bool env) {
 }
 
 template <int LP>
+SmxConfig staged_bwd_make() {
+  SmxConfig c;
+  c.main = segment_softmax_staged_bwd_kernel<LP>;
+  c.split = nullptr;  // no segment is split
+  c.tc = 4 * LP;
+  c.tiles = 1;
+  c.block = kStagedBwdBlock;
+  c.main_smem = (kStagedBwdBlock / kWarp) * BwdStage<LP>::kWarpBytes;
+  return c;
+}
+
+template <int LP>
 SmxConfig quad_bwd_make() {
   SmxConfig c;
   c.main = segment_softmax_whole_bwd_kernel<LP>;
@@ -1364,6 +1525,8 @@ SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = t
     if (channels == 8) return quad_make_lean<2>(env);
     if (channels == 16) return quad_make_lean<4>(env);
   }
+  // Staged backward at C = 8 (at C = 4 the register form measured faster).
+  if (backward && quad_ok && channels == 8) return staged_bwd_make<2>();
   if (backward && quad_ok && channels % 4 == 0 && channels <= 128) {
     switch (next_pow2(channels / 4)) {
       case 1: return quad_bwd_make<1>();
@@ -1418,13 +1581,15 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
   L.cfg = smx_config(channels, backward, quad_ok, env, lean);
   const DeviceInfo& dev = current_device_info();
   L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem);
+  const int64_t warps_per_block = L.cfg.block / kWarp;
   const int64_t resident =
       static_cast<int64_t>(dev.sm_count) *
-      resident_blocks(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem) *
-      kWarpsPerBlock;
+      resident_blocks(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem, L.cfg.block) *
+      warps_per_block;
   int64_t warps = resident / L.cfg.tiles;
   if (warps < 1) warps = 1;
   L.plan = plan_partitions(n_edges, n_nodes, warps, 32);
+  L.plan.blocks = static_cast<unsigned>((L.plan.parts + warps_per_block - 1) / warps_per_block);
   L.cpad = (channels + 3) / 4 * 4;
   Carver carve(ws);
   float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * 2 * L.cpad);
@@ -1452,7 +1617,7 @@ int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
   a.cpad = L.cpad;
   if (L.smem_status != BYSJ_OK) return L.smem_status;
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
-  L.cfg.main<<<grid, kBlock, L.cfg.main_smem, s>>>(a);
+  L.cfg.main<<<grid, L.cfg.block, L.cfg.main_smem, s>>>(a);
   st = launch_check(name);
   if (st || L.cfg.split == nullptr) return st;
   L.cfg.split<<<grid, kBlock, 0, s>>>(a);
