@@ -489,16 +489,17 @@ void check_gie(const Tensor& zonal, const Tensor& radial, const Tensor& dst,
 }
 
 // Number of degrees L when radial_slot is the degree-grouped layout
-// slot[r] = floor(sqrt(r+1)) + base with rows == (L+1)^2 - 1 (L <= 3), else 0.
-// Reads the (tiny) slot table back to the host.
-int64_t degree_layout(const Tensor& radial_slot, int64_t rows, int64_t n_radial) {
+// slot[r] = floor(sqrt(r+1)) + base with rows == (L+1)^2 - 1 (L <= 3), else 0;
+// sets `base`.  Reads the (tiny) slot table back to the host once.
+int64_t degree_layout(const Tensor& radial_slot, int64_t rows, int64_t n_radial,
+                      int64_t& base) {
   int64_t degrees = 0;
   for (int64_t l = 1; l <= 3; ++l)
     if ((l + 1) * (l + 1) - 1 == rows) degrees = l;
   if (degrees == 0) return 0;
-  Tensor host = radial_slot.to(torch::kCPU);
+  Tensor host = radial_slot.to(torch::kCPU);  // one read back of the slot table
   const int64_t* slot = host.data_ptr<int64_t>();
-  const int64_t base = slot[0] - 1;
+  base = slot[0] - 1;
   for (int64_t r = 0; r < rows; ++r) {
     int64_t l = 0;
     while ((l + 1) * (l + 1) <= r + 1) ++l;
@@ -518,11 +519,11 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
   Tensor out = torch::empty({nodes, rows + 1, channels}, zonal.options());
   if (nodes == 0) return out;
   auto [offsets, order] = csr_view(dst, nodes);
-  const int64_t degrees = degree_layout(radial_slot, rows, n_radial);
+  int64_t base = 0;
+  const int64_t degrees = degree_layout(radial_slot, rows, n_radial, base);
   if (degrees > 0 && channels % 4 == 0 && channels <= 128 &&
       ((channels / 4) & (channels / 4 - 1)) == 0 &&
       reinterpret_cast<uintptr_t>(radial.data_ptr()) % 16 == 0) {
-    const int64_t base = radial_slot.index({0}).item<int64_t>() - 1;
     Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_degree_workspace_size(edges, nodes,
                                                                               degrees, channels));
     check(bysj_gie_zonal_scatter_forward_degree(
@@ -562,13 +563,13 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
   Tensor gi = torch::empty_like(inv_sqrt_deg);
   if (nodes == 0) return {gz, gr, gi};
   auto [offsets, order] = csr_view(dst, nodes);
-  const int64_t degrees = degree_layout(radial_slot, rows, n_radial);
+  int64_t base = 0;
+  const int64_t degrees = degree_layout(radial_slot, rows, n_radial, base);
   if (degrees > 0 && channels % 4 == 0 && channels <= 64 &&
       ((channels / 4) & (channels / 4 - 1)) == 0 &&
       reinterpret_cast<uintptr_t>(radial.data_ptr()) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(grad_output.data_ptr()) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(gr.data_ptr()) % 16 == 0) {
-    const int64_t base = radial_slot.index({0}).item<int64_t>() - 1;
     Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_degree_workspace_size(
                                      edges, nodes, degrees, channels));
     check(bysj_gie_zonal_scatter_backward_degree(
