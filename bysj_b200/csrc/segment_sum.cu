@@ -315,6 +315,107 @@ __global__ void __launch_bounds__(kBlock)
   }
 }
 
+// grad_src and grad_node_scale in one pass, for fp32 src rows of at most
+// 32 NV float4 (one tile; used up to 256 channels): a warp holds the node's grad_out row in registers;
+// per edge it loads the src row, adds edge_scale * <grad_out, src> to its
+// lane's partial (the lanes' vectors and the order of the products are those
+// of segment_sum_grad_scale_kernel, so grad_node_scale has the same bits) and
+// stores grad_out * (edge_scale * node_scale) (as the rows kernel).  Two
+// edges' src rows are in flight per iteration.  Same partitions, slots and
+// in-order combination of split segments as segment_sum_grad_scale_kernel.
+template <int NV>
+__device__ __forceinline__ float row_dot(const float4 (&row)[NV], const float4 (&v)[NV]) {
+  float dot = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    dot = fmaf(row[k].x, v[k].x, dot);
+    dot = fmaf(row[k].y, v[k].y, dot);
+    dot = fmaf(row[k].z, v[k].z, dot);
+    dot = fmaf(row[k].w, v[k].w, dot);
+  }
+  return dot;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kBlock)
+    segment_sum_bwd_fused_kernel(NodeScaleGradArgs a, const float* __restrict__ node_scale,
+                                 float* __restrict__ grad_src) {
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int64_t C = a.channels;
+  const int64_t lv = C / 4;
+  const float* src = static_cast<const float*>(a.src);
+  SegCursor cur(a.mp, part_range(a.mp, p));
+  while (cur.next()) {
+    const int64_t n = cur.node;
+    const float sn = node_scale ? __ldg(node_scale + n) : 1.0f;
+    float4 row[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int64_t j = lane + k * kWarp;
+      row[k] = j < lv ? __ldg(reinterpret_cast<const float4*>(a.grad_out + n * C) + j)
+                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float acc = 0.0f;
+    auto load = [&](int64_t e, float4 (&v)[NV]) {
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int64_t j = lane + k * kWarp;
+        v[k] = j < lv ? ld_stream_f4(src + e * C + 4 * j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    };
+    auto store = [&](int64_t e, float w) {
+      const float scale = w * sn;
+      float4* out = reinterpret_cast<float4*>(grad_src + e * C);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int64_t j = lane + k * kWarp;
+        if (j < lv)
+          __stcs(out + j, make_float4(row[k].x * scale, row[k].y * scale, row[k].z * scale,
+                                      row[k].w * scale));
+      }
+    };
+    int64_t sl = cur.lo;
+    for (; sl + 1 < cur.hi; sl += 2) {
+      const int64_t e0 = a.order ? __ldg(a.order + sl) : sl;
+      const int64_t e1 = a.order ? __ldg(a.order + sl + 1) : sl + 1;
+      float4 v0[NV], v1[NV];
+      load(e0, v0);
+      load(e1, v1);
+      const float w0 = a.edge_scale ? __ldg(a.edge_scale + e0) : 1.0f;
+      const float w1 = a.edge_scale ? __ldg(a.edge_scale + e1) : 1.0f;
+      acc = fmaf(w0, row_dot<NV>(row, v0), acc);
+      acc = fmaf(w1, row_dot<NV>(row, v1), acc);
+      store(e0, w0);
+      store(e1, w1);
+    }
+    if (sl < cur.hi) {
+      const int64_t e0 = a.order ? __ldg(a.order + sl) : sl;
+      float4 v0[NV];
+      load(e0, v0);
+      const float w0 = a.edge_scale ? __ldg(a.edge_scale + e0) : 1.0f;
+      acc = fmaf(w0, row_dot<NV>(row, v0), acc);
+      store(e0, w0);
+    }
+    acc = xor_sum(acc, 1);
+    if (cur.kind == kWhole) {
+      if (lane == 0) a.grad_node_scale[n] = acc;
+      continue;
+    }
+    if (lane == 0) __stcg(a.ss.slot(p, cur.kind), acc);
+    const int64_t first = a.mp.part_of_first_edge(n);
+    const int64_t last = a.mp.part_of_end(n);
+    if (!arrive_last(a.ss, first, last, 0)) continue;
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int64_t q = first; q <= last; ++q)
+        sum += __ldcg(a.ss.slot(q, q == last ? kHead : kTail));
+      a.grad_node_scale[n] = sum;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host dispatch.
 // ---------------------------------------------------------------------------
@@ -411,6 +512,41 @@ int check_common(int64_t n_edges, int64_t n_nodes, int64_t channels,
   if (n_nodes > 0 && offsets == nullptr)
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "segment sum: offsets is NULL");
   return BYSJ_OK;
+}
+
+int sum_bwd_fused(const float* grad_out, const void* src, const int64_t* offsets,
+                  int64_t n_edges, int64_t n_nodes, int64_t channels, const float* edge_scale,
+                  const float* node_scale, const int64_t* order, float* grad_src,
+                  float* grad_node_scale, void* workspace, size_t workspace_bytes,
+                  cudaStream_t s) {
+  const DeviceInfo& dev = current_device_info();
+  const int64_t resident = static_cast<int64_t>(dev.sm_count) * 8 * kWarpsPerBlock;
+  const PartitionPlan plan = plan_partitions(n_edges, n_nodes, resident, 16);
+  Carver carve(workspace);
+  float* slots = carve.take<float>(static_cast<size_t>(plan.parts) * 2);
+  int* tickets = carve.take<int>(static_cast<size_t>(plan.parts));
+  if (workspace == nullptr || workspace_bytes < carve.need)
+    return fail(BYSJ_ERR_WORKSPACE,
+                "segment sum backward: workspace of %zu bytes needed, %zu given", carve.need,
+                workspace_bytes);
+  int st = cuda_check(cudaMemsetAsync(tickets, 0, sizeof(int) * plan.parts, s),
+                      "segment sum backward: ticket reset");
+  if (st) return st;
+  NodeScaleGradArgs a;
+  a.src = src;
+  a.channels = channels;
+  a.grad_out = grad_out;
+  a.edge_scale = edge_scale;
+  a.order = order;
+  a.grad_node_scale = grad_node_scale;
+  a.mp = MergePath{offsets, n_nodes, n_edges, plan.ipc, plan.parts};
+  a.ss = SplitSlots{slots, tickets, 1, 1};
+  const int64_t lv = channels / 4;  // <= 64
+  if (lv > kWarp)
+    segment_sum_bwd_fused_kernel<2><<<plan.blocks, kBlock, 0, s>>>(a, node_scale, grad_src);
+  else
+    segment_sum_bwd_fused_kernel<1><<<plan.blocks, kBlock, 0, s>>>(a, node_scale, grad_src);
+  return launch_check("segment_sum_bwd_fused_kernel");
 }
 
 }  // namespace
@@ -512,6 +648,15 @@ int bysj_segment_sum_backward(const float* grad_out, const void* src,
     return fail(BYSJ_ERR_INVALID_ARGUMENT,
                 "segment sum backward: a node_scale gradient needs node_scale");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Both gradients in one pass for fp32 rows of up to 256 channels (measured
+  // 1.2-1.3x faster there; at 512 channels even, at 1024 the two separate
+  // streams are faster).
+  const bool fused = grad_node_scale != nullptr && n_edges > 0 && src_dtype != BYSJ_BF16 &&
+                     channels % 4 == 0 && channels <= 256 && aligned16(grad_out) &&
+                     aligned16(grad_src) && aligned16(src);
+  if (fused) return sum_bwd_fused(grad_out, src, offsets, n_edges, n_nodes, channels,
+                                  edge_scale, node_scale, order, grad_src, grad_node_scale,
+                                  workspace, workspace_bytes, s);
   if (n_edges > 0 && channels % 4 == 0 && aligned16(grad_out) && aligned16(grad_src)) {
     const int64_t lv = channels / 4;
     const int nv = lv > 128 ? 8 : lv > 64 ? 4 : lv > 32 ? 2 : 1;

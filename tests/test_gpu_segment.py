@@ -19,6 +19,7 @@ from reference import segment_softmax_reference, segment_sum_reference
 
 pytestmark = pytest.mark.gpu
 
+from bysj_b200 import _C  # noqa: E402
 from bysj_b200 import kernels as K  # noqa: E402
 from bysj_b200 import workloads as W  # noqa: E402
 
@@ -161,6 +162,37 @@ def test_segment_sum_skewed_degrees_split_segments(cuda, channels):
     np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-5, atol=budget(want))
     again = K.segment_sum(src.cuda(), dst, off, None, ns.cuda())
     assert torch.equal(got, again), "repeated runs must be bit-identical"
+
+
+@pytest.mark.parametrize("channels,permuted", [(4, False), (64, True), (256, False), (1024, True)])
+def test_segment_sum_backward_both_gradients(cuda, channels, permuted):
+    # grad_src[e] = upstream[dst e] w[e] s[dst e];  grad_s[n] = sum_e w[e] <upstream[n], src[e]>
+    # on skewed degrees (split segments), rows in storage order or permuted.
+    sizes = skewed_sizes(channels, nodes=200, giant=3000)
+    dst, off = graph(sizes)
+    e, n = dst.numel(), sizes.numel()
+    gen = torch.Generator().manual_seed(channels)
+    src = torch.randn(e, channels, generator=gen)
+    w, s = torch.rand(e, generator=gen) + 0.5, torch.rand(n, generator=gen) + 0.5
+    up = torch.randn(n, channels, generator=gen)
+    order = torch.randperm(e, generator=gen) if permuted else None
+    stored, stored_w = src, w
+    if permuted:  # logical edge i lives at storage row order[i], with its scale
+        stored, stored_w = torch.empty_like(src), torch.empty_like(w)
+        stored[order], stored_w[order] = src, w
+    args = (up.cuda(), stored.cuda(), dst, off, stored_w.cuda(), s.cuda(), True,
+            order.cuda() if permuted else None)
+    gs, gn = _C.segment_sum_backward(*args)
+    d = dst.cpu().numpy()
+    u64, x64, w64, s64 = (t.double().numpy() for t in (up, src, w, s))
+    want_gs = u64[d] * (w64 * s64[d])[:, None]
+    want_gn = np.zeros(n)
+    np.add.at(want_gn, d, w64 * np.einsum("ec,ec->e", u64[d], x64))
+    got_gs = gs.cpu().numpy()[order.numpy()] if permuted else gs.cpu().numpy()
+    np.testing.assert_allclose(got_gs, want_gs, rtol=1e-5, atol=budget(want_gs))
+    np.testing.assert_allclose(gn.cpu().numpy(), want_gn, rtol=1e-4, atol=budget(want_gn))
+    gs2, gn2 = _C.segment_sum_backward(*args)
+    assert torch.equal(gs, gs2) and torch.equal(gn, gn2), "repeated runs must be bit-identical"
 
 
 def test_segment_sum_order_permutation_and_bf16(cuda):
