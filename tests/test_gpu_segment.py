@@ -164,7 +164,7 @@ def test_segment_sum_skewed_degrees_split_segments(cuda, channels):
     assert torch.equal(got, again), "repeated runs must be bit-identical"
 
 
-@pytest.mark.parametrize("channels,permuted", [(4, False), (64, True), (256, False), (1024, True)])
+@pytest.mark.parametrize("channels,permuted", [(4, False), (64, True), (256, False), (512, True), (1024, True)])
 def test_segment_sum_backward_both_gradients(cuda, channels, permuted):
     # grad_src[e] = upstream[dst e] w[e] s[dst e];  grad_s[n] = sum_e w[e] <upstream[n], src[e]>
     # on skewed degrees (split segments), rows in storage order or permuted.
