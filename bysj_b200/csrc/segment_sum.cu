@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kBlock)
 // grad_node_scale[n] = sum_{e in n} edge_scale[e] * <grad_out[n], src[e]>:
 // lanes over the row's vectors, edges in slot order, merge-path pieces
 // combined in partition order.
-template <typename T, int VEC>
+template <typename T, int VEC, bool kVecG = false>
 __global__ void __launch_bounds__(kBlock)
     segment_sum_grad_scale_kernel(NodeScaleGradArgs a) {
   const int64_t p = global_warp();
@@ -290,9 +290,19 @@ __global__ void __launch_bounds__(kBlock)
       for (int64_t j = lane; j < lv; j += kWarp) {
         RowVec<T, VEC> v;
         v.load(src + e * C, j);
+        float gv[VEC];
+        if constexpr (kVecG) {  // 16-byte loads of the grad_out row (L1)
 #pragma unroll
-        for (int i = 0; i < VEC; ++i)
-          dot = fmaf(__ldg(g + j * VEC + i), v.get(i), dot);
+          for (int i = 0; i < VEC; i += 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(g + j * VEC + i));
+            gv[i] = t.x; gv[i + 1] = t.y; gv[i + 2] = t.z; gv[i + 3] = t.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) gv[i] = __ldg(g + j * VEC + i);
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) dot = fmaf(gv[i], v.get(i), dot);
       }
       const float w = a.edge_scale ? __ldg(a.edge_scale + e) : 1.0f;
       acc = fmaf(w, dot, acc);
@@ -323,8 +333,6 @@ __global__ void __launch_bounds__(kBlock)
 // stores grad_out * (edge_scale * node_scale) (as the rows kernel).  Two
 // edges' src rows are in flight per iteration.  Same partitions, slots and
 // in-order combination of split segments as segment_sum_grad_scale_kernel.
-// kStore = false computes grad_node_scale alone (grad_src written by the
-// rows kernel).
 template <int NV>
 __device__ __forceinline__ float row_dot(const float4 (&row)[NV], const float4 (&v)[NV]) {
   float dot = 0.0f;
@@ -338,7 +346,7 @@ __device__ __forceinline__ float row_dot(const float4 (&row)[NV], const float4 (
   return dot;
 }
 
-template <int NV, bool kStore = true>
+template <int NV>
 __global__ void __launch_bounds__(kBlock)
     segment_sum_bwd_fused_kernel(NodeScaleGradArgs a, const float* __restrict__ node_scale,
                                  float* __restrict__ grad_src) {
@@ -368,7 +376,6 @@ __global__ void __launch_bounds__(kBlock)
       }
     };
     auto store = [&](int64_t e, float w) {
-      if constexpr (!kStore) return;
       const float scale = w * sn;
       float4* out = reinterpret_cast<float4*>(grad_src + e * C);
 #pragma unroll
@@ -652,8 +659,7 @@ int bysj_segment_sum_backward(const float* grad_out, const void* src,
                 "segment sum backward: a node_scale gradient needs node_scale");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Both gradients in one pass for fp32 rows of up to 256 channels (measured
-  // 1.2-1.3x faster there; at 512 channels even, at 1024 the two separate
-  // streams are faster).
+  // faster there; from 512 channels on the two separate streams are).
   const bool fused = grad_node_scale != nullptr && n_edges > 0 && src_dtype != BYSJ_BF16 &&
                      channels % 4 == 0 && channels <= 256 && aligned16(grad_out) &&
                      aligned16(grad_src) && aligned16(src);
@@ -730,25 +736,18 @@ int bysj_segment_sum_backward(const float* grad_out, const void* src,
   const bool bf16 = src_dtype == BYSJ_BF16;
   const bool vec = bf16 ? (channels % 8 == 0 && aligned16(src))
                         : (channels % 4 == 0 && aligned16(src));
-  if (!bf16 && vec && channels <= 512) {
-    // The node row in registers (as the one-pass kernel, without its stores):
-    // measured 1.15x faster at 512 channels; at 1024 its registers cost more
-    // occupancy than the row reloads below.
-    if (channels / 4 > 2 * kWarp)
-      segment_sum_bwd_fused_kernel<4, false><<<plan.blocks, kBlock, 0, s>>>(a, nullptr, nullptr);
-    else if (channels / 4 > kWarp)
-      segment_sum_bwd_fused_kernel<2, false><<<plan.blocks, kBlock, 0, s>>>(a, nullptr, nullptr);
-    else
-      segment_sum_bwd_fused_kernel<1, false><<<plan.blocks, kBlock, 0, s>>>(a, nullptr, nullptr);
-    return launch_check("segment_sum_bwd_fused_kernel<scale only>");
-  }
+  const bool vec_g = vec && aligned16(grad_out);
   if (bf16) {
-    if (vec)
+    if (vec_g)
+      segment_sum_grad_scale_kernel<__nv_bfloat16, 8, true><<<plan.blocks, kBlock, 0, s>>>(a);
+    else if (vec)
       segment_sum_grad_scale_kernel<__nv_bfloat16, 8><<<plan.blocks, kBlock, 0, s>>>(a);
     else
       segment_sum_grad_scale_kernel<__nv_bfloat16, 1><<<plan.blocks, kBlock, 0, s>>>(a);
   } else {
-    if (vec)
+    if (vec_g)
+      segment_sum_grad_scale_kernel<float, 4, true><<<plan.blocks, kBlock, 0, s>>>(a);
+    else if (vec)
       segment_sum_grad_scale_kernel<float, 4><<<plan.blocks, kBlock, 0, s>>>(a);
     else
       segment_sum_grad_scale_kernel<float, 1><<<plan.blocks, kBlock, 0, s>>>(a);
