@@ -343,8 +343,17 @@ __device__ __forceinline__ float lds_f32(uint32_t addr) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ int64_t lds_i64(uint32_t addr) {
+  int64_t v;
+  asm volatile("ld.shared.s64 %0, [%1];" : "=l"(v) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(smem)), "l"(gmem)
+               : "memory");
 }
 
 // Shared-memory staging of one chunk of a warp: lane (g, q) copies the quad
@@ -637,7 +646,8 @@ __device__ __forceinline__ void lean_stage(const SmxArgs& a, int64_t lo, int64_t
 
 template <int LP, bool kEnv>
 __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
-                                           int g, int q, const float4* buf, const float* envs) {
+                                           int g, int q, const float4* buf, const float* envs,
+                                           const int64_t* idx = nullptr) {
   using Q = QuadSmx<LP>;
   constexpr int C = 4 * LP;
   const int rows = quad_rows<LP>(lo, hi, g);
@@ -692,6 +702,17 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
   if (g == 0 && a.out_null) {
     reinterpret_cast<float4*>(a.out_null + n * C)[q] =
         make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
+  }
+  if (idx != nullptr) {  // rows in storage order: row of slot lo + i is idx[i]
+    const uint32_t idx_s = smem_addr(idx) + 8u * g;
+#pragma unroll
+    for (int t = 0; t < Q::T; ++t)
+      if (t < rows) {
+        const int64_t e = lds_i64(idx_s + 8u * t * Q::G);
+        reinterpret_cast<float4*>(a.out)[e * LP + q] =
+            make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+      }
+    return;
   }
   float4* dst = reinterpret_cast<float4*>(a.out) + (lo + g) * LP + q;
 #pragma unroll
@@ -877,6 +898,113 @@ __global__ void __launch_bounds__(kBlock, 3) segment_softmax_whole_kernel(SmxArg
     hi = nhi;
     nhi = nnhi;
     b ^= 1;
+  }
+  cp_async_wait<0>();
+}
+
+// ---- forward, whole segments in a permuted storage order (C = 4 or 8) -----
+// The rows of segment n sit at storage rows order[lo..hi): a gather.  A lane
+// that had to load order[slot] before issuing its row copy would wait a full
+// memory round trip; so the warp runs three stages: while it computes segment
+// n from shared memory, segment n+1's rows and envelopes are gathered into
+// its other row buffer (cp.async, indices read from shared memory), and
+// segment n+2's contiguous order[lo..hi) slice is copied into the third index
+// buffer.  Outputs go to the staged storage rows.  Arithmetic as the whole
+// kernel; segments longer than a chunk take lean_big (global, through order).
+constexpr int kGatherBlock = 128;  // four-warp CTAs
+
+template <int LP>
+struct GatherStage {
+  using Q = QuadSmx<LP>;
+  static constexpr size_t kRows = sizeof(float4) * Q::T * kWarp;
+  static constexpr size_t kEnv = sizeof(float) * Q::CHUNK;
+  static constexpr size_t kIdx = sizeof(int64_t) * Q::CHUNK;
+  static constexpr size_t kWarpBytes = 2 * (kRows + kEnv) + 3 * kIdx;
+  static_assert((kRows + kEnv) % 16 == 0 && kIdx % 16 == 0, "16-byte aligned buffers");
+};
+
+template <int LP, bool kEnv>
+__global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  using S = GatherStage<LP>;
+  extern __shared__ float4 quad_smem[];
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
+  const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
+  if (n0 >= n1) return;
+  char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
+  auto rows_buf = [&](int b) { return reinterpret_cast<float4*>(mine + b * (S::kRows + S::kEnv)); };
+  auto env_buf = [&](int b) {
+    return reinterpret_cast<float*>(mine + b * (S::kRows + S::kEnv) + S::kRows);
+  };
+  auto idx_buf = [&](int k) {
+    return reinterpret_cast<int64_t*>(mine + 2 * (S::kRows + S::kEnv) + k * S::kIdx);
+  };
+  // order[lo..hi) -> index buffer k (if the segment fits a chunk).
+  auto stage_idx = [&](int64_t lo, int64_t hi, int k) {
+    if (hi - lo > Q::CHUNK) return;
+    int64_t* dst = idx_buf(k);
+    for (int64_t i = lane; i < hi - lo; i += kWarp) cp_async8(dst + i, a.order + lo + i);
+  };
+  // Rows (and envelopes) of a staged segment, gathered by its staged indices.
+  auto stage_rows = [&](int64_t lo, int64_t hi, int b, int k) {
+    if (hi - lo > Q::CHUNK) return;
+    const int rows = quad_rows<LP>(lo, hi, g);
+    const int64_t* idx = idx_buf(k);
+    float4* rb = rows_buf(b);
+#pragma unroll
+    for (int t = 0; t < Q::T; ++t)
+      if (t < rows) {
+        const int64_t e = idx[g + t * Q::G];
+        cp_async16(rb + t * kWarp + lane, a.x + e * (4 * LP) + 4 * q);
+      }
+    if constexpr (kEnv) {
+      float* eb = env_buf(b);
+#pragma unroll
+      for (int j = 0; j < Q::T / LP; ++j) {
+        const int t = q + j * LP;
+        if (t < rows) cp_async4(eb + t * Q::G + g, a.env + idx[g + t * Q::G]);
+      }
+    }
+  };
+  const int64_t* off = a.mp.offsets;
+  // o[0..3] = offsets[n .. n+3] (clamped at the partition's last end).
+  int64_t o0 = __ldg(off + n0), o1 = __ldg(off + n0 + 1);
+  int64_t o2 = n0 + 1 < n1 ? __ldg(off + n0 + 2) : o1;
+  int64_t o3 = n0 + 2 < n1 ? __ldg(off + n0 + 3) : o2;
+  stage_idx(o0, o1, 0);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
+  if (n0 + 1 < n1) stage_idx(o1, o2, 1);
+  stage_rows(o0, o1, 0, 0);
+  cp_async_commit();
+  int kb = 0;  // index buffer of segment n; rows buffer is (n - n0) & 1
+  int rb = 0;
+  for (int64_t n = n0; n < n1; ++n) {
+    cp_async_wait<0>();  // segment n's rows, segment n+1's indices
+    __syncwarp();
+    const int64_t o4 = n + 3 < n1 ? __ldg(off + n + 4) : o3;
+    const int k1 = kb == 2 ? 0 : kb + 1;
+    const int k2 = k1 == 2 ? 0 : k1 + 1;
+    if (n + 2 < n1) stage_idx(o2, o3, k2);
+    if (n + 1 < n1) stage_rows(o1, o2, rb ^ 1, k1);
+    cp_async_commit();
+    if (o1 - o0 <= Q::CHUNK)
+      lean_whole<LP, kEnv>(a, n, o0, o1, g, q, rows_buf(rb), env_buf(rb), idx_buf(kb));
+    else
+      lean_big<LP, kEnv>(a, n, o0, o1, g, q);
+    __syncwarp();  // buffers of segment n are free for segment n+2 / n+3
+    o0 = o1;
+    o1 = o2;
+    o2 = o3;
+    o3 = o4;
+    kb = k1;
+    rb ^= 1;
   }
   cp_async_wait<0>();
 }
@@ -1487,6 +1615,23 @@ SmxConfig quad_make(bool env) {
   return env ? quad_make_env<LP, true>() : quad_make_env<LP, false>();
 }
 
+// C == 4 LP with a permuted storage order (C = 4 or 8): the gather kernel.
+template <int LP, bool kEnv>
+SmxConfig gather_make_env() {
+  SmxConfig c;
+  c.main = segment_softmax_gather_kernel<LP, kEnv>;
+  c.split = nullptr;  // no segment is split
+  c.tc = 4 * LP;
+  c.tiles = 1;
+  c.block = kGatherBlock;
+  c.main_smem = (kGatherBlock / kWarp) * GatherStage<LP>::kWarpBytes;
+  return c;
+}
+template <int LP>
+SmxConfig gather_make(bool env) {
+  return env ? gather_make_env<LP, true>() : gather_make_env<LP, false>();
+}
+
 // C == 4 LP with rows in storage order (C = 4, 8 or 16): whole-segment
 // partitions.  At C = 16 a chunk is 64 rows, so typical segments take the
 // two-read path of lean_big.
@@ -1518,8 +1663,12 @@ SmxConfig quad_bwd_make() {
 }
 
 SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = true,
-                     bool lean = false) {
+                     bool lean = false, bool gather = false) {
   SmxConfig c;
+  if (!backward && quad_ok && gather) {
+    if (channels == 4) return gather_make<1>(env);
+    if (channels == 8) return gather_make<2>(env);
+  }
   if (!backward && quad_ok && lean) {
     if (channels == 4) return quad_make_lean<1>(env);
     if (channels == 8) return quad_make_lean<2>(env);
@@ -1576,9 +1725,9 @@ struct SmxLayout {
 
 SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
                      bool backward, void* ws, bool quad_ok = true, bool env = true,
-                     bool lean = false) {
+                     bool lean = false, bool gather = false) {
   SmxLayout L;
-  L.cfg = smx_config(channels, backward, quad_ok, env, lean);
+  L.cfg = smx_config(channels, backward, quad_ok, env, lean, gather);
   const DeviceInfo& dev = current_device_info();
   L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.cfg.main), L.cfg.main_smem);
   const int64_t warps_per_block = L.cfg.block / kWarp;
@@ -1647,9 +1796,10 @@ size_t bysj_segment_softmax_workspace_size(int64_t n_edges, int64_t n_nodes,
   // partition count); size for every choice.
   size_t need = smx_layout(n_edges, n_nodes, channels, false, nullptr, false).bytes;
   for (int env = 0; env < 2; ++env)
-    for (int lean = 0; lean < 2; ++lean) {
-      const size_t b =
-          smx_layout(n_edges, n_nodes, channels, false, nullptr, true, env, lean).bytes;
+    for (int form = 0; form < 3; ++form) {  // merge path, lean, gather
+      const size_t b = smx_layout(n_edges, n_nodes, channels, false, nullptr, true, env,
+                                  form == 1, form == 2)
+                           .bytes;
       if (b > need) need = b;
     }
   return need;
@@ -1675,7 +1825,7 @@ int bysj_segment_softmax_forward(const float* logit, const float* env,
                        (null_logit == nullptr || aligned16(null_logit)) &&
                        (null_alpha == nullptr || aligned16(null_alpha));
   SmxLayout L = smx_layout(n_edges, n_nodes, channels, false, workspace, quad_ok,
-                           env != nullptr, order == nullptr);
+                           env != nullptr, order == nullptr, order != nullptr);
   if (workspace == nullptr || workspace_bytes < L.bytes)
     return fail(BYSJ_ERR_WORKSPACE,
                 "segment softmax: workspace of %zu bytes needed, %zu given",
