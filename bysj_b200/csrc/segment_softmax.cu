@@ -1444,7 +1444,7 @@ struct BwdStage {
 
 template <int LP>
 __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t hi, int g, int q,
-                                          char* buf) {
+                                          char* buf, const int64_t* idx = nullptr) {
   using B = BwdStage<LP>;
   constexpr int C = 4 * LP;
   const int rows = quad_rows_n<LP, B::T>(lo, hi, g);
@@ -1456,7 +1456,7 @@ __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t 
   for (int t = 0; t < B::T; ++t) {
     if (t < rows) {
       const int64_t slot = lo + g + static_cast<int64_t>(t) * B::G;
-      const int64_t e = a.order ? __ldg(a.order + slot) : slot;
+      const int64_t e = idx ? idx[g + t * B::G] : a.order ? __ldg(a.order + slot) : slot;
       cp_async16(al + t * kWarp + lane, a.x + e * C + 4 * q);
       cp_async16(gr + t * kWarp + lane, a.y + e * C + 4 * q);
       if (a.env && q == 0) cp_async4(env + t * B::G + g, a.env + e);
@@ -1466,7 +1466,8 @@ __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t 
 
 template <int LP>
 __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, int64_t lo,
-                                                   int64_t hi, int g, int q, const char* buf) {
+                                                   int64_t hi, int g, int q, const char* buf,
+                                                   const int64_t* idx = nullptr) {
   using B = BwdStage<LP>;
   constexpr int C = 4 * LP;
   const int rows = quad_rows_n<LP, B::T>(lo, hi, g);
@@ -1502,7 +1503,9 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
     const float4 gl = make_float4(al.x * (gr.x - S[0]), al.y * (gr.y - S[1]),
                                   al.z * (gr.z - S[2]), al.w * (gr.w - S[3]));
     const int64_t slot = lo + g + static_cast<int64_t>(t) * B::G;
-    const int64_t e = live ? (a.order ? __ldg(a.order + slot) : slot) : 0;
+    const int64_t e = !live ? 0
+                      : idx ? lds_i64(smem_addr(idx) + 8u * (g + t * B::G))
+                      : a.order ? __ldg(a.order + slot) : slot;
     if (live) reinterpret_cast<float4*>(a.out)[e * LP + q] = gl;
     if (a.out_env) {
       float rowsum = (gl.x + gl.y) + (gl.z + gl.w);
@@ -1551,6 +1554,77 @@ __global__ void __launch_bounds__(kStagedBwdBlock) segment_softmax_staged_bwd_ke
     hi = nhi;
     nhi = nnhi;
     b ^= 1;
+  }
+  cp_async_wait<0>();
+}
+
+// Staged backward with a permuted storage order (C = 8): the three-stage
+// pipeline of the forward gather kernel (order slice two segments ahead,
+// gathered alpha / grad_alpha / envelope rows one segment ahead, outputs
+// scattered through the staged indices).
+template <int LP>
+struct GatherBwdStage {
+  using B = BwdStage<LP>;
+  static constexpr size_t kIdx = sizeof(int64_t) * B::CHUNK;
+  static constexpr size_t kWarpBytes = B::kWarpBytes + 3 * kIdx;
+};
+
+template <int LP>
+__global__ void __launch_bounds__(kStagedBwdBlock)
+    segment_softmax_gather_bwd_kernel(SmxArgs a) {
+  using B = BwdStage<LP>;
+  using S = GatherBwdStage<LP>;
+  extern __shared__ float4 quad_smem[];
+  const int64_t p = global_warp();
+  if (p >= a.mp.parts) return;
+  const int lane = lane_id();
+  const int g = lane / LP;
+  const int q = lane % LP;
+  const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
+  const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
+  if (n0 >= n1) return;
+  char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
+  char* bufs[2] = {mine, mine + B::kBytes};
+  auto idx_buf = [&](int k) {
+    return reinterpret_cast<int64_t*>(mine + B::kWarpBytes + k * S::kIdx);
+  };
+  auto stage_idx = [&](int64_t lo, int64_t hi, int k) {
+    if (hi - lo > B::CHUNK) return;
+    int64_t* dst = idx_buf(k);
+    for (int64_t i = lane; i < hi - lo; i += kWarp) cp_async8(dst + i, a.order + lo + i);
+  };
+  const int64_t* off = a.mp.offsets;
+  int64_t o0 = __ldg(off + n0), o1 = __ldg(off + n0 + 1);
+  int64_t o2 = n0 + 1 < n1 ? __ldg(off + n0 + 2) : o1;
+  int64_t o3 = n0 + 2 < n1 ? __ldg(off + n0 + 3) : o2;
+  stage_idx(o0, o1, 0);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
+  if (n0 + 1 < n1) stage_idx(o1, o2, 1);
+  if (o1 - o0 <= B::CHUNK) bwd_stage<LP>(a, o0, o1, g, q, bufs[0], idx_buf(0));
+  cp_async_commit();
+  int kb = 0, rb = 0;
+  for (int64_t n = n0; n < n1; ++n) {
+    cp_async_wait<0>();  // segment n's rows, segment n+1's indices
+    __syncwarp();
+    const int64_t o4 = n + 3 < n1 ? __ldg(off + n + 4) : o3;
+    const int k1 = kb == 2 ? 0 : kb + 1;
+    const int k2 = k1 == 2 ? 0 : k1 + 1;
+    if (n + 2 < n1) stage_idx(o2, o3, k2);
+    if (n + 1 < n1 && o2 - o1 <= B::CHUNK) bwd_stage<LP>(a, o1, o2, g, q, bufs[rb ^ 1], idx_buf(k1));
+    cp_async_commit();
+    if (o1 - o0 <= B::CHUNK)
+      bwd_segment_staged<LP>(a, n, o0, o1, g, q, bufs[rb], idx_buf(kb));
+    else
+      bwd_segment_global<LP, kBwdT>(a, n, o0, o1, g, q, true);
+    __syncwarp();  // buffers of segment n are free for segments n+2 / n+3
+    o0 = o1;
+    o1 = o2;
+    o2 = o3;
+    o3 = o4;
+    kb = k1;
+    rb ^= 1;
   }
   cp_async_wait<0>();
 }
@@ -1653,6 +1727,14 @@ SmxConfig staged_bwd_make() {
 }
 
 template <int LP>
+SmxConfig gather_bwd_make() {
+  SmxConfig c = staged_bwd_make<LP>();
+  c.main = segment_softmax_gather_bwd_kernel<LP>;
+  c.main_smem = (kStagedBwdBlock / kWarp) * GatherBwdStage<LP>::kWarpBytes;
+  return c;
+}
+
+template <int LP>
 SmxConfig quad_bwd_make() {
   SmxConfig c;
   c.main = segment_softmax_whole_bwd_kernel<LP>;
@@ -1674,8 +1756,9 @@ SmxConfig smx_config(int64_t channels, bool backward, bool quad_ok, bool env = t
     if (channels == 8) return quad_make_lean<2>(env);
     if (channels == 16) return quad_make_lean<4>(env);
   }
-  // Staged backward at C = 8 (at C = 4 the register form measured faster).
-  if (backward && quad_ok && channels == 8) return staged_bwd_make<2>();
+  // Staged backward at C = 8 (at C = 4 the register form measured faster);
+  // with a storage order, its gather form.
+  if (backward && quad_ok && channels == 8) return gather ? gather_bwd_make<2>() : staged_bwd_make<2>();
   if (backward && quad_ok && channels % 4 == 0 && channels <= 128) {
     switch (next_pow2(channels / 4)) {
       case 1: return quad_bwd_make<1>();
@@ -1846,10 +1929,14 @@ size_t bysj_segment_softmax_backward_workspace_size(int64_t n_edges,
                                                     int64_t n_nodes,
                                                     int64_t channels) {
   if (n_edges < 0 || n_nodes <= 0 || channels <= 0) return 0;
-  // Pointer alignment picks the quad-vector or the scalar kernel; size for both.
-  const size_t a = smx_layout(n_edges, n_nodes, channels, true, nullptr, true).bytes;
-  const size_t b = smx_layout(n_edges, n_nodes, channels, true, nullptr, false).bytes;
-  return a > b ? a : b;
+  // Pointer alignment and `order` pick the kernel; size for every choice.
+  size_t need = smx_layout(n_edges, n_nodes, channels, true, nullptr, false).bytes;
+  for (int gather = 0; gather < 2; ++gather) {
+    const size_t b =
+        smx_layout(n_edges, n_nodes, channels, true, nullptr, true, true, false, gather).bytes;
+    if (b > need) need = b;
+  }
+  return need;
 }
 
 int bysj_segment_softmax_backward(const float* alpha, const float* grad_alpha,
@@ -1880,7 +1967,8 @@ int bysj_segment_softmax_backward(const float* alpha, const float* grad_alpha,
                        (null_alpha == nullptr || aligned16(null_alpha)) &&
                        (grad_null_alpha == nullptr || aligned16(grad_null_alpha)) &&
                        (grad_null_logit == nullptr || aligned16(grad_null_logit));
-  SmxLayout L = smx_layout(n_edges, n_nodes, channels, true, workspace, quad_ok);
+  SmxLayout L = smx_layout(n_edges, n_nodes, channels, true, workspace, quad_ok, true, false,
+                           order != nullptr);
   if (workspace == nullptr || workspace_bytes < L.bytes)
     return fail(BYSJ_ERR_WORKSPACE,
                 "segment softmax backward: workspace of %zu bytes needed, %zu "
