@@ -318,6 +318,30 @@ def test_segment_softmax_skewed_split_segments(cuda):
                                atol=1e-5)
 
 
+@pytest.mark.parametrize("heads", [4, 8, 16])
+def test_segment_softmax_forward_permuted_storage(cuda, heads):
+    # rows stored in a permuted order and addressed through `order` (the layout
+    # of an edge list that is not grouped by destination), with envelopes,
+    # masked edges, a null logit and one segment longer than a chunk
+    sizes = skewed_sizes(heads, nodes=300, giant=700)
+    dst, off = graph(sizes)
+    e, n = dst.numel(), sizes.numel()
+    gen = torch.Generator().manual_seed(heads)
+    logit = torch.randn(e, heads, generator=gen) * 2
+    env = torch.where(torch.rand(e, generator=gen) < 0.1, torch.tensor(-1.0),
+                      torch.rand(e, generator=gen) + 0.05)
+    null = torch.randn(n, heads, generator=gen)
+    perm = torch.randperm(e, generator=gen)
+    lp, ep = torch.empty_like(logit), torch.empty_like(env)
+    lp[perm], ep[perm] = logit, env
+    a, n0 = K.segment_softmax(lp.cuda(), ep.cuda(), off, null.cuda(), order=perm.cuda())
+    wa, wn = truth.segment_softmax(logit.numpy(), env.numpy(), dst.cpu().numpy(), n, null.numpy())
+    np.testing.assert_allclose(a[perm.cuda()].cpu().numpy(), wa, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(n0.cpu().numpy(), wn, rtol=1e-5, atol=1e-6)
+    a2, _ = K.segment_softmax(lp.cuda(), ep.cuda(), off, null.cuda(), order=perm.cuda())
+    assert torch.equal(a, a2), "repeated runs must be bit-identical"
+
+
 def test_segment_softmax_all_masked_segment_is_zero(cuda):
     dst, off = graph([3, 2])
     logit = torch.randn(5, 4, device="cuda")
