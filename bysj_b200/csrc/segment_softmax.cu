@@ -644,6 +644,40 @@ __device__ __forceinline__ void lean_stage(const SmxArgs& a, int64_t lo, int64_t
   }
 }
 
+// Packed pairs of fp32 (add/sub/mul .f32x2, sm_100: two IEEE
+// round-to-nearest operations per instruction, so a pair gives the same bits
+// as two scalar operations) and 2^t by the approximate PTX ex2.approx.ftz.f32.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float ex2_ftz(float t) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
+  return r;
+}
+
 template <int LP, bool kEnv>
 __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
                                            int g, int q, const float4* buf, const float* envs,
@@ -654,7 +688,8 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
   const int lane = g * LP + q;
   const uint32_t rows_s = smem_addr(buf) + 16u * lane;
   const uint32_t env_s = smem_addr(envs) + 4u * g;
-  float4 x[Q::T];
+  uint64_t x[Q::T][2];  // channel pairs (0,1), (2,3)
+  const uint64_t ninf = pk2(-INFINITY, -INFINITY);
 #pragma unroll
   for (int t = 0; t < Q::T; ++t) {
     float shift = 0.0f;
@@ -664,62 +699,88 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
       keep = keep && e > 0.0f;
       shift = keep ? 2.0f * __logf(e) : 0.0f;
     }
-    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    x[t][0] = ninf;
+    x[t][1] = ninf;
     if (keep) {
       const float4 raw = lds_f4(rows_s + 16u * t * kWarp);
-      v = make_float4(raw.x + shift, raw.y + shift, raw.z + shift, raw.w + shift);
+      const uint64_t sh = pk2(shift, shift);
+      x[t][0] = add2(pk2(raw.x, raw.y), sh);
+      x[t][1] = add2(pk2(raw.z, raw.w), sh);
     }
-    x[t] = v;
   }
   float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   if (a.xn) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
     nl[0] = v.x; nl[1] = v.y; nl[2] = v.z; nl[3] = v.w;
   }
-  float w0[4], inv[4];
+  float m[4], ms[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     float cm = -INFINITY;
 #pragma unroll
-    for (int t = 0; t < Q::T; ++t) cm = fmaxf(cm, quad_get(x[t], i));
-#pragma unroll
-    for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
-    const float m = fmaxf(cm, nl[i]);
-    const float ms = m == -INFINITY ? 0.0f : m;
-    float acc = 0.0f;
-#pragma unroll
     for (int t = 0; t < Q::T; ++t) {
-      const float w = __expf(quad_get(x[t], i) - ms);
-      quad_set(x[t], i, w);
-      acc += w;
+      const float2 v = upk2(x[t][i >> 1]);
+      cm = fmaxf(cm, (i & 1) ? v.y : v.x);
     }
 #pragma unroll
-    for (int st = LP; st < kWarp; st <<= 1) acc += __shfl_xor_sync(kFull, acc, st);
-    w0[i] = shifted_exp(nl[i], m);
-    const float total = acc + w0[i];
+    for (int st = LP; st < kWarp; st <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, st));
+    m[i] = fmaxf(cm, nl[i]);
+    ms[i] = m[i] == -INFINITY ? 0.0f : m[i];
+  }
+  // w = exp(y), y = x - ms <= 0, written as 2^(y log2 e) (base conversion),
+  // two channels per instruction.  The product adds at most |y| log2 e 2^-24
+  // to the exponent (< 1.3e-6 for the y >= -14 whose weights matter to an
+  // absolute 1e-6), ex2.approx adds a few ulp, and weights below 2^-126 flush
+  // to zero; on the C3 frame the results equal __expf(y) bit for bit.  The
+  // tests hold them to rtol 1e-5 against float64.
+  const uint64_t l2e = pk2(1.4426950408889634f, 1.4426950408889634f);
+  uint64_t acc[2] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
+#pragma unroll
+  for (int pr = 0; pr < 2; ++pr) {
+    const uint64_t msp = pk2(ms[2 * pr], ms[2 * pr + 1]);
+#pragma unroll
+    for (int t = 0; t < Q::T; ++t) {
+      const float2 y = upk2(mul2(sub2(x[t][pr], msp), l2e));
+      const uint64_t w = pk2(ex2_ftz(y.x), ex2_ftz(y.y));
+      x[t][pr] = w;
+      acc[pr] = add2(acc[pr], w);
+    }
+  }
+  float w0[4], inv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 ap = upk2(acc[i >> 1]);
+    float s = (i & 1) ? ap.y : ap.x;
+#pragma unroll
+    for (int st = LP; st < kWarp; st <<= 1) s += __shfl_xor_sync(kFull, s, st);
+    w0[i] = shifted_exp(nl[i], m[i]);
+    const float total = s + w0[i];
     inv[i] = total > 0.0f ? __frcp_rn(total) : 0.0f;
   }
   if (g == 0 && a.out_null) {
     reinterpret_cast<float4*>(a.out_null + n * C)[q] =
         make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
   }
+  const uint64_t inv01 = pk2(inv[0], inv[1]), inv23 = pk2(inv[2], inv[3]);
+  auto out_row = [&](int t) {
+    const float2 lo2 = upk2(mul2(x[t][0], inv01));
+    const float2 hi2 = upk2(mul2(x[t][1], inv23));
+    return make_float4(lo2.x, lo2.y, hi2.x, hi2.y);
+  };
   if (idx != nullptr) {  // rows in storage order: row of slot lo + i is idx[i]
     const uint32_t idx_s = smem_addr(idx) + 8u * g;
 #pragma unroll
     for (int t = 0; t < Q::T; ++t)
       if (t < rows) {
         const int64_t e = lds_i64(idx_s + 8u * t * Q::G);
-        reinterpret_cast<float4*>(a.out)[e * LP + q] =
-            make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+        reinterpret_cast<float4*>(a.out)[e * LP + q] = out_row(t);
       }
     return;
   }
   float4* dst = reinterpret_cast<float4*>(a.out) + (lo + g) * LP + q;
 #pragma unroll
   for (int t = 0; t < Q::T; ++t)
-    if (t < rows)
-      dst[t * Q::G * LP] =
-          make_float4(x[t].x * inv[0], x[t].y * inv[1], x[t].z * inv[2], x[t].w * inv[3]);
+    if (t < rows) dst[t * Q::G * LP] = out_row(t);
 }
 
 // Channel counts up to 8 (LP <= 2) hold a typical segment (<= 128 rows) in
