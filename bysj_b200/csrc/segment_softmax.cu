@@ -624,40 +624,40 @@ __device__ __forceinline__ void quad_segment(const SmxArgs& a, int64_t p, const 
 // its lanes (no shuffle).  Same staging layout as quad_stage and the same
 // arithmetic as quad_segment's one-chunk path for a whole segment.
 
-template <int LP, bool kEnv>
+template <int LP, bool kEnv, int TT = QuadSmx<LP>::T>
 __device__ __forceinline__ void lean_stage(const SmxArgs& a, int64_t lo, int64_t hi, int g,
                                            int q, float4* buf, float* env) {
   using Q = QuadSmx<LP>;
-  const int rows = quad_rows<LP>(lo, hi, g);
+  const int rows = quad_rows_n<LP, TT>(lo, hi, g);
   const int lane = g * LP + q;
   const float4* src = reinterpret_cast<const float4*>(a.x) + (lo + g) * LP + q;
 #pragma unroll
-  for (int t = 0; t < Q::T; ++t)
+  for (int t = 0; t < TT; ++t)
     if (t < rows) cp_async16(buf + t * kWarp + lane, src + t * Q::G * LP);
   if constexpr (kEnv) {
     const float* es = a.env + lo + g;
 #pragma unroll
-    for (int j = 0; j < Q::T / LP; ++j) {
+    for (int j = 0; j < TT / LP; ++j) {
       const int t = q + j * LP;
       if (t < rows) cp_async4(env + t * Q::G + g, es + t * Q::G);
     }
   }
 }
 
-template <int LP, bool kEnv>
+template <int LP, bool kEnv, int TT = QuadSmx<LP>::T>
 __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
                                            int g, int q, const float4* buf, const float* envs,
                                            const int64_t* idx = nullptr) {
   using Q = QuadSmx<LP>;
   constexpr int C = 4 * LP;
-  const int rows = quad_rows<LP>(lo, hi, g);
+  const int rows = quad_rows_n<LP, TT>(lo, hi, g);
   const int lane = g * LP + q;
   const uint32_t rows_s = smem_addr(buf) + 16u * lane;
   const uint32_t env_s = smem_addr(envs) + 4u * g;
-  uint64_t x[Q::T][2];  // channel pairs (0,1), (2,3)
+  uint64_t x[TT][2];  // channel pairs (0,1), (2,3)
   const uint64_t ninf = pk2(-INFINITY, -INFINITY);
 #pragma unroll
-  for (int t = 0; t < Q::T; ++t) {
+  for (int t = 0; t < TT; ++t) {
     float shift = 0.0f;
     bool keep = t < rows;
     if constexpr (kEnv) {
@@ -684,7 +684,7 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
   for (int i = 0; i < 4; ++i) {
     float cm = -INFINITY;
 #pragma unroll
-    for (int t = 0; t < Q::T; ++t) {
+    for (int t = 0; t < TT; ++t) {
       const float2 v = upk2(x[t][i >> 1]);
       cm = fmaxf(cm, (i & 1) ? v.y : v.x);
     }
@@ -705,7 +705,7 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
   for (int pr = 0; pr < 2; ++pr) {
     const uint64_t msp = pk2(ms[2 * pr], ms[2 * pr + 1]);
 #pragma unroll
-    for (int t = 0; t < Q::T; ++t) {
+    for (int t = 0; t < TT; ++t) {
       const float2 y = upk2(mul2(sub2(x[t][pr], msp), l2e));
       const uint64_t w = pk2(ex2_ftz(y.x), ex2_ftz(y.y));
       x[t][pr] = w;
@@ -736,7 +736,7 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
   if (idx != nullptr) {  // rows in storage order: row of slot lo + i is idx[i]
     const uint32_t idx_s = smem_addr(idx) + 8u * g;
 #pragma unroll
-    for (int t = 0; t < Q::T; ++t)
+    for (int t = 0; t < TT; ++t)
       if (t < rows) {
         const int64_t e = lds_i64(idx_s + 8u * t * Q::G);
         reinterpret_cast<float4*>(a.out)[e * LP + q] = out_row(t);
@@ -745,7 +745,7 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
   }
   float4* dst = reinterpret_cast<float4*>(a.out) + (lo + g) * LP + q;
 #pragma unroll
-  for (int t = 0; t < Q::T; ++t)
+  for (int t = 0; t < TT; ++t)
     if (t < rows) dst[t * Q::G * LP] = out_row(t);
 }
 
@@ -882,11 +882,31 @@ __device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo
   }
 }
 
-// Three CTAs per SM: 80 registers, 3 x 72 KB of staging buffers.
+// Rows per lane and CTA shape of the whole kernel: a 128-row chunk at every
+// width (4, 8 or 16 rows per lane at LP = 1, 2, 4), so that a typical segment
+// (~90 edges) fits one chunk without lanes idling over most of it.  LP <= 2:
+// eight-warp CTAs, three per SM (80 registers); LP = 4: 17 KB of buffers per
+// warp, four-warp CTAs.  (At LP = 1, 4 rows per lane measured 1.3x faster
+// than 8.)
+template <int LP>
+struct WholeShape {
+  static constexpr int T = LP >= 4 ? 16 : LP == 2 ? 8 : 4;
+  static constexpr int G = kWarp / LP;
+  static constexpr int CHUNK = G * T;
+  static constexpr int kRowsF4 = T * kWarp;
+  static constexpr size_t kBytes = sizeof(float4) * kRowsF4 + sizeof(float) * CHUNK;
+  static constexpr size_t kWarpBytes = 2 * kBytes;
+  static constexpr int kThreads = LP >= 4 ? 128 : kBlock;
+  static constexpr int kMinBlocks = 3;
+  static_assert(kBytes % 16 == 0, "stage buffers must stay 16-byte aligned");
+};
+
 template <int LP, bool kEnv>
-__global__ void __launch_bounds__(kBlock, 3) segment_softmax_whole_kernel(SmxArgs a) {
-  using Q = QuadSmx<LP>;
-  using S = QuadStage<LP>;
+__global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMinBlocks)
+    segment_softmax_whole_kernel(SmxArgs a) {
+  using Q = WholeShape<LP>;
+  using S = WholeShape<LP>;
+  constexpr int TT = S::T;
   extern __shared__ float4 quad_smem[];
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
@@ -904,19 +924,19 @@ __global__ void __launch_bounds__(kBlock, 3) segment_softmax_whole_kernel(SmxArg
   int64_t lo = __ldg(off + n0), hi = __ldg(off + n0 + 1);
   int64_t nhi = n0 + 1 < n1 ? __ldg(off + n0 + 2) : hi;
   if (hi - lo <= Q::CHUNK)
-    lean_stage<LP, kEnv>(a, lo, hi, g, q, bufs[0], reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+    lean_stage<LP, kEnv, TT>(a, lo, hi, g, q, bufs[0], reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
   cp_async_commit();
   int b = 0;
   for (int64_t n = n0; n < n1; ++n) {
     const int64_t nnhi = n + 2 < n1 ? __ldg(off + n + 3) : nhi;
     if (n + 1 < n1 && nhi - hi <= Q::CHUNK)
-      lean_stage<LP, kEnv>(a, hi, nhi, g, q, bufs[b ^ 1],
+      lean_stage<LP, kEnv, TT>(a, hi, nhi, g, q, bufs[b ^ 1],
                            reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
     cp_async_commit();
     cp_async_wait<1>();  // this segment's copies have landed
     __syncwarp();
     if (hi - lo <= Q::CHUNK)
-      lean_whole<LP, kEnv>(a, n, lo, hi, g, q, bufs[b],
+      lean_whole<LP, kEnv, TT>(a, n, lo, hi, g, q, bufs[b],
                            reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
     else
       lean_big<LP, kEnv>(a, n, lo, hi, g, q);
@@ -1701,13 +1721,17 @@ SmxConfig quad_make_env() {
   if constexpr (kLean) {
     c.main = segment_softmax_whole_kernel<LP, kEnv>;
     c.split = nullptr;  // no segment is split
+    c.block = WholeShape<LP>::kThreads;
   } else {
     c.main = segment_softmax_quad_kernel<LP, false, kEnv>;
     c.split = segment_softmax_quad_kernel<LP, true, kEnv>;
   }
   c.tc = 4 * LP;
   c.tiles = 1;
-  c.main_smem = (kLean || quad_pipelined<LP>()) ? kWarpsPerBlock * QuadStage<LP>::kWarpBytes : 0;
+  if constexpr (kLean)
+    c.main_smem = (WholeShape<LP>::kThreads / kWarp) * WholeShape<LP>::kWarpBytes;
+  else
+    c.main_smem = quad_pipelined<LP>() ? kWarpsPerBlock * QuadStage<LP>::kWarpBytes : 0;
   return c;
 }
 
@@ -1734,8 +1758,7 @@ SmxConfig gather_make(bool env) {
 }
 
 // C == 4 LP with rows in storage order (C = 4, 8 or 16): whole-segment
-// partitions.  At C = 16 a chunk is 64 rows, so typical segments take the
-// two-read path of lean_big.
+// partitions.
 template <int LP>
 SmxConfig quad_make_lean(bool env) {
   return env ? quad_make_env<LP, true, true>() : quad_make_env<LP, false, true>();
