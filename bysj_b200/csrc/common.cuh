@@ -84,6 +84,14 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   return v;
 }
 
+// Asks the TMA unit to bring `bytes` at `p` into L2 (no shared memory, no
+// registers, no completion to wait for).  `p` 16-byte aligned, `bytes` a
+// multiple of 16.  Used to put the next loop step's rows in flight while this
+// step's loads are still outstanding.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 word.
 __device__ __forceinline__ float bf16_lo(uint32_t w) {
   return __uint_as_float(w << 16);

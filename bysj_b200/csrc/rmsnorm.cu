@@ -102,6 +102,16 @@ __global__ void __launch_bounds__(kBlock) rmsnorm_fwd_kernel(NormArgs a) {
   const bool pow2_comps = (a.comps & (a.comps - 1)) == 0;
   const float inv_width = 1.0f / static_cast<float>(a.width);
   for (int64_t base = global_warp() * G * R; base < a.rows; base += step) {
+    // bf16 rows: the warp's block of rows two steps ahead (contiguous) is
+    // requested into L2 by one bulk prefetch (C2 bf16: 34.8 -> 32.8 us);
+    // fp32 rows gained nothing from it.
+    if constexpr (sizeof(T) == 2 && VEC * sizeof(T) == 16) {
+      const int64_t nb = base + 2 * step;
+      if (lane == 0 && nb < a.rows) {
+        const int64_t cnt = a.rows - nb < G * R ? a.rows - nb : G * R;
+        prefetch_l2_bulk(x + nb * a.width, static_cast<uint32_t>(cnt * a.width * sizeof(T)));
+      }
+    }
     RowVec<T, VEC> buf[R][NV];
 #pragma unroll
     for (int rr = 0; rr < R; ++rr) {
