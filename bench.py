@@ -24,6 +24,9 @@ segment sum) producing [N, 8, 16, 8].  The metric is edges/s.
   softmax, segment_sum, force_assembly (Morton and random atom order),
   zonal_scatter, RMSNorm fp32/bf16, the backward operators, and a small
   launch-bound step replayed from a CUDA graph.  ``--only OP`` times one.
+* ``--mode chain``: 64 independent frames of the full chain (offsets ->
+  RMSNorm -> fused attention -> zonal scatter -> source grouping -> force
+  assembly, fp32, C = 32) sharded over the ranks; frames/s ("strong").
 * ``--mode partition``: one 500k-atom box split by destination ranges over
   the ranks (strong scaling; force partials reduce-scattered over NCCL).
 
@@ -70,9 +73,12 @@ def parse_args():
                    help="time one operator on its own (per-op line only, no headline)")
     p.add_argument("--atoms", type=int, default=24576,
                    help="atoms of the synthetic box used by --only")
-    p.add_argument("--mode", choices=("frames", "partition"), default="frames",
-                   help="frames: one C3 frame per rank (default); partition: one large box "
-                        "split by destination-atom ranges, force partials reduce-scattered")
+    p.add_argument("--mode", choices=("frames", "chain", "partition"), default="frames",
+                   help="frames: one C3 frame per rank (default); chain: the full operator "
+                        "chain over 64 frames sharded across the ranks; partition: one large "
+                        "box split by destination-atom ranges, force partials reduce-scattered")
+    p.add_argument("--chain-frames", type=int, default=64,
+                   help="frames of the job in --mode chain")
     p.add_argument("--partition-atoms", type=int, default=500_000,
                    help="atoms of the box used by --mode partition")
     return p.parse_args()
@@ -794,15 +800,162 @@ def run_ours(args, dist):
         print(json.dumps(line), flush=True)
 
 
+CHAIN_CHANNELS = 32
+
+
+def chain_inputs(g, seed, device, channels=CHAIN_CHANNELS):
+    """One C5 frame: the C3 geometry with C = 32 features for every operator
+    of the chain (node features [N,16,C], per-degree weights [4,C], logits
+    [E,8], values [E,16,C], zonal [E,15] from the unit vectors, radial
+    [E,4,C], dE/dr [E,3])."""
+    from bysj_b200 import workloads as W
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    n, e = g.n_atoms, g.n_edges
+    return {
+        "g": g, "n": n, "e": e,
+        "x": torch.randn(n, 16, channels, device=device, generator=gen),
+        "scale": torch.rand(4, channels, device=device, generator=gen) + 0.5,
+        "logit": torch.randn(e, 8, device=device, generator=gen) * (2.0 ** 0.5),
+        "value": torch.randn(e, 16, channels, device=device, generator=gen),
+        "zonal": W.real_sph_zonal(g.unit).contiguous(),
+        "radial": torch.randn(e, 4, channels, device=device, generator=gen),
+        "slot": W.degree_slots().to(device),
+        "inv": torch.rsqrt(torch.bincount(g.dst, minlength=n).float() + 1.0),
+        "grad": torch.randn(e, 3, device=device, generator=gen) * 0.1,
+    }
+
+
+def chain_frame(f):
+    """The full chain of one frame through the public API, as a user calls it:
+    CSR of dst -> RMSNorm of the node features -> fused softmax + weighted sum
+    -> GIE zonal scatter -> source grouping -> force assembly."""
+    from bysj_b200 import kernels as K
+
+    g = f["g"]
+    offsets = K.segment_offsets(g.dst, f["n"])
+    h = K.rmsnorm(f["x"], f["scale"], 1.0e-6)
+    agg = K.segment_attention(f["logit"], f["value"], offsets)
+    z = K.zonal_scatter(f["zonal"], f["radial"], g.dst, f["slot"], f["inv"])
+    order, soff = K.group_by_source(g.src, f["n"])
+    force, virial = K.force_assembly(f["grad"], g.unit, g.src, g.dst, offsets, soff, order)
+    return h, agg, z, force, virial
+
+
+def chain_bytes(e, n, c=CHAIN_CHANNELS):
+    """Algorithmic bytes of one chain frame (each input read once, each output
+    written once, per operator)."""
+    offsets = 8 * e + 8 * (n + 1)
+    rms = 2 * n * 16 * c * 4 + 4 * n * 16 + 4 * 4 * c
+    attention = e * (8 * 4 + 16 * c * 4) + n * 16 * c * 4 + 8 * (n + 1)
+    zonal = e * (15 * 4 + 8 + 3 * c * 4) + n * (16 * c * 4 + 4)
+    group = 8 * e + 8 * e + 8 * (n + 1)
+    force = e * (12 + 12 + 8) + n * (16 + 12 + 36)
+    return offsets + rms + attention + zonal + group + force
+
+
+def count_library_kernels(fn) -> int | None:
+    """Kernels of this library (names in namespace bysj) that one call of `fn`
+    launches, from a CUDA-activity profile of that call; None when the
+    profiler is unavailable."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return sum(1 for ev in prof.events()
+                   if ev.device_type == torch.autograd.DeviceType.CUDA and "bysj" in ev.name)
+    except Exception:  # noqa: BLE001 -- the count is a report, not a gate
+        return None
+
+
+def run_chain(args, dist):
+    """C5(a): 64 independent 24576-atom frames of the full chain, fp32, C = 32,
+    frames r, r + P, ... on rank r, no communication ("strong": the 64 frames
+    are the fixed job).  Each rank holds two synthetic frames (two seeded
+    geometries and feature sets) and its frames alternate between them; every
+    frame's inputs (~5.9 GB) exceed L2, so a re-used frame is read from HBM
+    like a new one."""
+    from bysj_b200 import sharding as S
+    from bysj_b200 import workloads as W
+
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    frames = S.frame_share(args.chain_frames, dist.rank, dist.world)
+    sets = []
+    for k in range(2):
+        seed = args.seed + 1000 * dist.rank + 97 * k
+        sets.append(chain_inputs(W.c3_box(device=device, seed=seed), seed + 5, device))
+
+    def step():
+        for i, _ in enumerate(frames):
+            chain_frame(sets[i % 2])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    per_frame_kernels = count_library_kernels(lambda: chain_frame(sets[0]))
+    clocks = ClockSampler(device)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clock_info = clocks.stop()
+    step_max = dist.max(start.elapsed_time(end) / 1e3 / args.steps)
+    frames_total = args.chain_frames
+    e_mean = sum(s["e"] for s in sets) / 2
+    n = sets[0]["n"]
+    peak, peak_src = measured_peak()
+    # per-frame device time on the slowest rank: its frames run back to back
+    frame_s = step_max / max(1, len(S.frame_share(frames_total, 0, dist.world)))
+    achieved = chain_bytes(e_mean, n) / frame_s / 1e9
+    if dist.rank == 0:
+        line = {
+            "metric": "frames/s (full fused chain, 24576-atom frames, fp32, C = 32)",
+            "value": frames_total / step_max, "unit": "frames/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_max * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C5(a) 64 independent frames, full chain",
+                       "chain": "segment_offsets -> rmsnorm -> segment_attention -> "
+                                "zonal_scatter -> group_by_source -> force_assembly",
+                       "frames_per_step": frames_total, "n_atoms": n,
+                       "n_edges_per_frame": int(e_mean), "channels": CHAIN_CHANNELS,
+                       "parallelism": f"frame-sharded x{dist.world} (no collective)",
+                       "l2": "each frame's inputs (~5.9 GB) exceed L2; no flush"},
+            "edges_per_s": frames_total * e_mean / step_max,
+            "ms_per_frame": frame_s * 1e3,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "whole chain: the sum of its operators' algorithmic bytes "
+                                   "per frame over the frame's device time",
+                         "peak_source": peak_src},
+            "clocks": clock_info,
+            "gpu_launches": (None if per_frame_kernels is None
+                             else per_frame_kernels * frames_total * args.steps),
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_partition(args, dist):
     """One large box split by destination-atom ranges over the ranks ("strong").
 
-    Per step and rank: ``force_assembly_src_partial`` over the local edges
-    (all atoms' source sums, written in the padded exchange layout), NCCL
-    reduce-scatter of those partials (asynchronous, on NCCL's stream),
-    ``segment_attention`` over the local edges meanwhile, then the wait and
-    ``force_assembly_dst_add`` for the local atoms.  Values fp32 [E, 16, 32],
-    logits fp32 [E, 8], dE/dr fp32 [E, 3].
+    Per step and rank, the full chain of C5(b): ``force_assembly_src_partial``
+    over the local edges (all atoms' source sums, written in the padded
+    exchange layout), NCCL reduce-scatter of those partials (asynchronous, on
+    NCCL's stream); meanwhile the local operators -- RMSNorm of the local
+    atoms' node features [N_r, 16, 32], ``segment_attention`` over the local
+    edges (values fp32 [E_r, 16, 32], logits [E_r, 8]) and the GIE zonal
+    scatter of the local edges into the local atoms (radial [E_r, 4, 32]);
+    then the wait and ``force_assembly_dst_add`` for the local atoms
+    (dE/dr fp32 [E, 3]).
     """
     from bysj_b200 import _C
     from bysj_b200 import kernels as K
@@ -823,20 +976,37 @@ def run_partition(args, dist):
     gen.manual_seed(args.seed + 1000 * dist.rank + 37)
     logit = torch.randn(e, 8, device=device, generator=gen) * (2.0 ** 0.5)
     value = torch.randn(e, 16, 32, device=device, generator=gen)
+    x_local = torch.randn(part.n_local, 16, 32, device=device, generator=gen)
+    scale = torch.rand(4, 32, device=device, generator=gen) + 0.5
+    zonal = W.real_sph_zonal(part.edges(g.unit).contiguous()).contiguous()
+    radial = torch.randn(e, 4, 32, device=device, generator=gen)
+    dst_local = (part.edges(g.dst) - part.atom_begin).contiguous()
+    inv_local = torch.rsqrt(torch.bincount(dst_local, minlength=part.n_local).float() + 1.0)
+    slot = W.degree_slots().to(device)
     ex = S.ForceExchange(part)
 
-    def step(events=None):
-        ex.start(grad, vec)
+    def local_ops(events=None):
+        h = K.rmsnorm(x_local, scale, 1.0e-6)
         if events is not None:
             events[0].record()
         out = _C.segment_attention_forward(logit, value, part.dst_offsets)
         if events is not None:
             events[1].record()
-        return out, ex.finish()
+        z = K.zonal_scatter(zonal, radial, dst_local, slot, inv_local)
+        return h, out, z
+
+    def step(events=None):
+        ex.start(grad, vec)
+        outs = local_ops(events)
+        return outs, ex.finish()
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # this rank's kernels per step: the local operators (counted from a
+    # profile of one call, no collective inside) + the two force kernels
+    local_kernels = count_library_kernels(local_ops)
+    launches = dist.sum(float(local_kernels + 2)) if local_kernels is not None else None
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(args.steps)]
     clocks = ClockSampler(device)
@@ -868,7 +1038,7 @@ def run_partition(args, dist):
     achieved = alg / kernel_s / 1e9
     if dist.rank == 0:
         line = {
-            "metric": f"edges/s (dst-partitioned {n}-atom box: attention + force assembly)",
+            "metric": f"edges/s (dst-partitioned {n}-atom box: full chain)",
             "value": e_total / step_max, "unit": UNIT, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_max * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -877,8 +1047,11 @@ def run_partition(args, dist):
                        "n_atoms": n, "n_edges": e_total, "edges_rank0": e,
                        "atoms_rank0": part.n_local, "heads": 8, "components": 16,
                        "channels": 32, "exchange_rows": part.world * part.chunk,
+                       "chain": "rmsnorm -> segment_attention -> zonal_scatter (local); "
+                                "force_assembly (source partials reduce-scattered)",
                        "parallelism": f"dst-range partition x{dist.world}, NCCL reduce-scatter "
-                                      "of [N, 12] force partials overlapped with attention",
+                                      "of [N, 12] force partials overlapped with the local "
+                                      "operators",
                        "l2": "inputs larger than L2; no flush"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
@@ -886,7 +1059,7 @@ def run_partition(args, dist):
                          "kernel_ms": kernel_s * 1e3, "peak_source": peak_src},
             "check": {"max_abs_err_vs_single_device": err, "max_abs_force": scale},
             "clocks": clock_info,
-            "gpu_launches": 3 * args.steps * dist.world,
+            "gpu_launches": None if launches is None else int(launches) * args.steps,
         }
         print(json.dumps(line), flush=True)
 
@@ -918,7 +1091,7 @@ def main():
         return
     dist.setup("nccl")
     try:
-        (run_partition if args.mode == "partition" else run_ours)(args, dist)
+        {"partition": run_partition, "chain": run_chain}.get(args.mode, run_ours)(args, dist)
     finally:
         dist.close()
 
