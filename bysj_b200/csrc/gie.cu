@@ -206,9 +206,11 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
       for (; k + EG < rows; k += 2 * EG) {
         // The next step's radial rows (degrees 1..L of each of its edges,
         // one contiguous L*C*4-byte run per edge) are requested into L2
-        // now, so they are in flight while this step's loads are (C4:
-        // 354 -> 335 us).
-        if (c4 == 0) {
+        // now, so they are in flight while this step's loads are (C = 64:
+        // 351 -> 335 us).  With four or more edges side by side (C <= 32)
+        // a step already has enough rows in flight and the extra requests
+        // only cost issue slots (C = 32: 226 us without, 233 us with).
+        if (EG <= 2 && c4 == 0) {
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int64_t t = lo + k + 2 * EG + u * EG;
