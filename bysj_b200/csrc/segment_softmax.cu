@@ -1498,6 +1498,7 @@ struct BwdStage {
   static constexpr size_t kWarpBytes = 2 * kBytes;
   static_assert(kBytes % 16 == 0, "stage buffers must stay 16-byte aligned");
 };
+constexpr int kBwdShort = 6;  // row slots per lane for segments within 3/4 of a chunk
 
 template <int LP>
 __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t hi, int g, int q,
@@ -1521,20 +1522,22 @@ __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t 
   }
 }
 
-template <int LP>
+// TT row slots per lane (<= BwdStage<LP>::T): a segment that fits fewer
+// slots skips the empty ones (they add nothing, so the bits are the same).
+template <int LP, int TT = BwdStage<LP>::T>
 __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, int64_t lo,
                                                    int64_t hi, int g, int q, const char* buf,
                                                    const int64_t* idx = nullptr) {
   using B = BwdStage<LP>;
   constexpr int C = 4 * LP;
-  const int rows = quad_rows_n<LP, B::T>(lo, hi, g);
+  const int rows = quad_rows_n<LP, TT>(lo, hi, g);
   const int lane = g * LP + q;
   const uint32_t al_s = smem_addr(buf) + 16u * lane;
   const uint32_t gr_s = al_s + 16u * B::kRowsF4;
   const uint32_t env_s = smem_addr(buf) + 32u * B::kRowsF4 + 4u * g;
   float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int t = 0; t < B::T; ++t) {
+  for (int t = 0; t < TT; ++t) {
     if (t < rows) {
       const float4 al = lds_f4(al_s + 16u * t * kWarp);
       const float4 gr = lds_f4(gr_s + 16u * t * kWarp);
@@ -1550,7 +1553,7 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
     for (int st = LP; st < kWarp; st <<= 1) S[i] += __shfl_xor_sync(kFull, S[i], st);
   bwd_null<LP>(a, n, g, q, true, S);
 #pragma unroll
-  for (int t = 0; t < B::T; ++t) {
+  for (int t = 0; t < TT; ++t) {
     const bool live = t < rows;
     float4 al = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gr = al;
     if (live) {
@@ -1602,7 +1605,11 @@ __global__ void __launch_bounds__(kStagedBwdBlock) segment_softmax_staged_bwd_ke
     cp_async_commit();
     cp_async_wait<1>();  // this segment's copies have landed
     __syncwarp();
-    if (hi - lo <= B::CHUNK)
+    // Segments that fit 3/4 of the chunk take 6 row slots per lane instead
+    // of 8 (C3, H = 8: 63.6 -> 60.7 us, same bits).
+    if (hi - lo <= kBwdShort * B::G)
+      bwd_segment_staged<LP, kBwdShort>(a, n, lo, hi, g, q, bufs[b]);
+    else if (hi - lo <= B::CHUNK)
       bwd_segment_staged<LP>(a, n, lo, hi, g, q, bufs[b]);
     else
       bwd_segment_global<LP, kBwdT>(a, n, lo, hi, g, q, true);
@@ -1671,7 +1678,9 @@ __global__ void __launch_bounds__(kStagedBwdBlock)
     if (n + 2 < n1) stage_idx(o2, o3, k2);
     if (n + 1 < n1 && o2 - o1 <= B::CHUNK) bwd_stage<LP>(a, o1, o2, g, q, bufs[rb ^ 1], idx_buf(k1));
     cp_async_commit();
-    if (o1 - o0 <= B::CHUNK)
+    if (o1 - o0 <= kBwdShort * B::G)
+      bwd_segment_staged<LP, kBwdShort>(a, n, o0, o1, g, q, bufs[rb], idx_buf(kb));
+    else if (o1 - o0 <= B::CHUNK)
       bwd_segment_staged<LP>(a, n, o0, o1, g, q, bufs[rb], idx_buf(kb));
     else
       bwd_segment_global<LP, kBwdT>(a, n, o0, o1, g, q, true);
