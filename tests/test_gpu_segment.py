@@ -342,6 +342,49 @@ def test_segment_softmax_forward_permuted_storage(cuda, heads):
     assert torch.equal(a, a2), "repeated runs must be bit-identical"
 
 
+# Segment lengths at the edges of the per-lane row-slot forms: the whole-
+# segment kernels take a shorter unrolled form for segments within 3/4 (H =
+# 4, 16: 96 rows) or 7/8 (H = 8: 112 rows) of a 128-row chunk, the staged
+# backward within 96 rows, the permuted-storage forward within 112 (H = 8) or
+# 96 (H = 4, chunk 256) rows; longer segments take the full form or the
+# multi-chunk path.
+BOUNDARY_SIZES = [1, 95, 96, 97, 111, 112, 113, 127, 128, 129, 255, 256, 257, 40, 0, 3]
+
+
+@pytest.mark.parametrize("heads", [4, 8, 16])
+def test_segment_softmax_row_slot_boundaries(cuda, heads):
+    dst, off = graph(BOUNDARY_SIZES)
+    e, n = dst.numel(), len(BOUNDARY_SIZES)
+    gen = torch.Generator().manual_seed(100 + heads)
+    logit = torch.randn(e, heads, generator=gen) * 2
+    env = torch.where(torch.rand(e, generator=gen) < 0.1, torch.tensor(-1.0),
+                      torch.rand(e, generator=gen) + 0.05)
+    null = torch.randn(n, heads, generator=gen)
+    a, n0 = K.segment_softmax(logit.cuda(), env.cuda(), off, null.cuda())
+    wa, wn = segment_softmax_reference(logit, env, dst.cpu(), off.cpu(), null)
+    torch.testing.assert_close(a.cpu(), wa, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(n0.cpu(), wn, rtol=1e-5, atol=1e-6)
+    # backward through the closed-form kernels
+    lg = logit.cuda().requires_grad_(True)
+    ev = env.abs().cuda().requires_grad_(True)
+    nl = null.cuda().requires_grad_(True)
+    a, n0 = K.segment_softmax(lg, ev, off, nl)
+    ua, un = torch.randn_like(a), torch.randn_like(n0)
+    got = torch.autograd.grad((a, n0), (lg, ev, nl), (ua, un))
+    rl, re, rn = (x.detach().cpu().requires_grad_(True) for x in (lg, ev, nl))
+    ra, rnull = segment_softmax_reference(rl, re, dst.cpu(), off.cpu(), rn)
+    want = torch.autograd.grad((ra, rnull), (rl, re, rn), (ua.cpu(), un.cpu()))
+    for x, y in zip(got, want):
+        torch.testing.assert_close(x.cpu(), y, rtol=2e-4, atol=2e-5)
+    # the same rows in a permuted storage order
+    perm = torch.randperm(e, generator=gen)
+    lp, ep = torch.empty_like(logit), torch.empty_like(env)
+    lp[perm], ep[perm] = logit, env
+    ap, np0 = K.segment_softmax(lp.cuda(), ep.cuda(), off, null.cuda(), order=perm.cuda())
+    torch.testing.assert_close(ap[perm.cuda()].cpu(), wa, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(np0.cpu(), wn, rtol=1e-5, atol=1e-6)
+
+
 def test_segment_softmax_all_masked_segment_is_zero(cuda):
     dst, off = graph([3, 2])
     logit = torch.randn(5, 4, device="cuda")
