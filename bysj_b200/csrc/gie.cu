@@ -30,6 +30,7 @@ struct GieArgs {
   float* grad_radial;    // [E, NR, C]
   int64_t rows, n_radial, channels;
   int64_t lv;            // R*C/VEC
+  int64_t skip_degrees;  // generic kernels: > 0 = return if slot[] is the degree table of that L
   MergePath mp;
   SplitSlots ss;
 };
@@ -44,6 +45,29 @@ __device__ __forceinline__ void ld_l1(const float* p, float (&v)[VEC]) {
     for (int i = 0; i < VEC; ++i) v[i] = __ldg(p + i);
   }
 }
+
+// True when slot[0..R), R = (L+1)^2 - 1, is the degree-grouped table
+// slot[r] = l(r) + base, l(r) = floor(sqrt(r + 1)), with degrees 1..L inside
+// the n_radial slots; sets base.  It is the test the host applies before it
+// calls the degree entry points itself; the generic entry points, which are
+// handed a slot table they do not read back, launch both kernels and let
+// every warp of each make it (R <= 15 loads that hit L2).
+__device__ __forceinline__ bool degree_table(const int64_t* slot, int degrees,
+                                             int64_t n_radial, int64_t& base) {
+  const int rows = (degrees + 1) * (degrees + 1) - 1;
+  base = __ldg(slot) - 1;
+  bool ok = base >= -1 && base + degrees <= n_radial - 1;
+  int l = 1;
+  for (int r = 0; r < rows; ++r) {
+    if ((l + 1) * (l + 1) <= r + 1) ++l;
+    ok = ok && __ldg(slot + r) == l + base;
+  }
+  return ok;
+}
+
+// slot_base value that tells a degree kernel to take its base from a.slot
+// (and to do nothing unless a.slot is the degree table).
+constexpr int64_t kSlotBaseOnDevice = INT64_MIN;
 
 // Per-lane geometry of vector k: output row r, radial offset slot*C + c.
 template <int VEC, int NV>
@@ -95,6 +119,10 @@ __global__ void __launch_bounds__(kBlock, 2) gie_fwd_kernel(GieArgs a) {
   constexpr int TV = kWarp * NV;
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
+  if (a.skip_degrees > 0) {
+    int64_t base;
+    if (degree_table(a.slot, static_cast<int>(a.skip_degrees), a.n_radial, base)) return;
+  }
   const int lane = lane_id();
   const int tile = blockIdx.y;
   const int64_t jt = static_cast<int64_t>(tile) * TV;
@@ -174,6 +202,7 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
   __shared__ float zstage[kWarpsPerBlock][kZonalChunk * R];
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
+  if (slot_base == kSlotBaseOnDevice && !degree_table(a.slot, L, a.n_radial, slot_base)) return;
   float* zb = zstage[threadIdx.x >> 5];
   const int lane = lane_id();
   const int eg = lane / LPE;
@@ -347,6 +376,7 @@ __global__ void __launch_bounds__(kBlock, 2)
   extern __shared__ float4 gie_bwd_smem[];
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
+  if (slot_base == kSlotBaseOnDevice && !degree_table(a.slot, L, a.n_radial, slot_base)) return;
   char* mine_smem = reinterpret_cast<char*>(gie_bwd_smem) + (threadIdx.x >> 5) * M::kWarpBytes;
   float4* gq = reinterpret_cast<float4*>(mine_smem);
   float* zb = reinterpret_cast<float*>(mine_smem + M::kG);
@@ -507,6 +537,10 @@ __global__ void __launch_bounds__(kBlock, 2) gie_bwd_kernel(GieArgs a) {
   extern __shared__ float s_dot[];  // [warps][TV]
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
+  if (a.skip_degrees > 0) {
+    int64_t base;
+    if (degree_table(a.slot, static_cast<int>(a.skip_degrees), a.n_radial, base)) return;
+  }
   float* sdot = s_dot + (threadIdx.x >> 5) * TV;
   const int lane = lane_id();
   const int64_t block = (a.rows + 1) * a.channels;
@@ -754,6 +788,22 @@ int gie_check(int64_t n_edges, int64_t n_nodes, int64_t rows, int64_t n_radial,
   return BYSJ_OK;
 }
 
+// Degrees L when a generic call has the shape of the degree-grouped layout
+// (R = (L+1)^2 - 1 rows, channels = 4 * 2^k <= max_channels, 16-byte aligned
+// rows), else 0.  Such a call launches the degree kernel with the slot table
+// left on the device (it returns unless the table is the degree table) and
+// then the generic kernel (it returns if the table is): no read back.
+int64_t degree_candidate(int64_t rows, int64_t channels, int64_t max_channels, bool aligned) {
+  if (!aligned || channels % 4 != 0 || channels > max_channels ||
+      ((channels / 4) & (channels / 4 - 1)) != 0)
+    return 0;
+  for (int64_t l = 1; l <= 3; ++l)
+    if ((l + 1) * (l + 1) - 1 == rows) return l;
+  return 0;
+}
+
+size_t after256(size_t bytes) { return (bytes + 255) & ~size_t(255); }
+
 }  // namespace
 }  // namespace bysj
 
@@ -766,7 +816,11 @@ size_t bysj_gie_zonal_scatter_workspace_size(int64_t n_edges, int64_t n_nodes,
   if (n_edges < 0 || n_nodes <= 0 || n_rows <= 0 || channels <= 0) return 0;
   const size_t a = gie_layout(true, n_edges, n_nodes, n_rows, channels, false, nullptr).bytes;
   const size_t b = gie_layout(false, n_edges, n_nodes, n_rows, channels, false, nullptr).bytes;
-  return a > b ? a : b;
+  const size_t generic = a > b ? a : b;
+  const int64_t degrees = degree_candidate(n_rows, channels, 128, true);
+  if (degrees == 0) return generic;
+  return after256(generic) +
+         gie_degree_layout(n_edges, n_nodes, degrees, channels, nullptr).bytes;
 }
 
 int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
@@ -794,10 +848,18 @@ int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
     return fail(BYSJ_ERR_INVALID_ARGUMENT, "zonal scatter: NULL pointer");
   const bool vec_ok = aligned16(radial) && aligned16(out);
   GieLayout L = gie_layout(vec_ok, n_edges, n_nodes, n_rows, channels, false, workspace);
-  if (workspace == nullptr || workspace_bytes < L.bytes)
+  const int64_t degrees = degree_candidate(n_rows, channels, 128, vec_ok);
+  GieDegreeLayout D;
+  size_t need = L.bytes;
+  if (degrees > 0) {
+    D = gie_degree_layout(n_edges, n_nodes, degrees, channels,
+                          workspace ? static_cast<char*>(workspace) + after256(L.bytes) : nullptr);
+    need = after256(L.bytes) + D.bytes;
+  }
+  if (workspace == nullptr || workspace_bytes < need)
     return fail(BYSJ_ERR_WORKSPACE,
                 "zonal scatter: workspace of %zu bytes needed, %zu given",
-                L.bytes, workspace_bytes);
+                need, workspace_bytes);
   st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0,
                                   sizeof(int) * L.plan.parts * L.cfg.tiles, s),
                   "zonal scatter: ticket reset");
@@ -815,6 +877,19 @@ int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
   a.lv = L.cfg.lv;
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
+  if (degrees > 0) {
+    st = cuda_check(cudaMemsetAsync(D.ss.tickets, 0, sizeof(int) * D.plan.parts, s),
+                    "zonal scatter: ticket reset (degree rows)");
+    if (st) return st;
+    GieArgs d = a;
+    d.lv = 0;
+    d.mp = MergePath{offsets, n_nodes, n_edges, D.plan.ipc, D.plan.parts};
+    d.ss = D.ss;
+    D.kernel<<<D.plan.blocks, kBlock, 0, s>>>(d, kSlotBaseOnDevice);
+    st = launch_check("gie_fwd_degree_kernel");
+    if (st) return st;
+    a.skip_degrees = degrees;
+  }
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
   L.cfg.kernel<<<grid, kBlock, 0, s>>>(a);
   return launch_check("gie_fwd_kernel");
@@ -882,7 +957,11 @@ size_t bysj_gie_zonal_scatter_backward_workspace_size(int64_t n_edges,
   if (n_edges < 0 || n_nodes <= 0 || n_rows <= 0 || channels <= 0) return 0;
   const size_t a = gie_layout(true, n_edges, n_nodes, n_rows, channels, true, nullptr).bytes;
   const size_t b = gie_layout(false, n_edges, n_nodes, n_rows, channels, true, nullptr).bytes;
-  return a > b ? a : b;
+  const size_t generic = a > b ? a : b;
+  const int64_t degrees = degree_candidate(n_rows, channels, 64, true);
+  if (degrees == 0) return generic;
+  return after256(generic) +
+         gie_degree_layout(n_edges, n_nodes, degrees, channels, nullptr, true).bytes;
 }
 
 int bysj_gie_zonal_scatter_backward(
@@ -924,10 +1003,20 @@ int bysj_gie_zonal_scatter_backward(
     return fail(BYSJ_ERR_UNSUPPORTED,
                 "zonal scatter backward: rows*channels = %lld exceeds %d",
                 (long long)(n_rows * channels), kWarp * 8 * L.cfg.vec);
-  if (workspace == nullptr || workspace_bytes < L.bytes)
+  const int64_t degrees = degree_candidate(n_rows, channels, 64, vec_ok);
+  GieDegreeLayout D;
+  size_t need = L.bytes;
+  if (degrees > 0) {
+    D = gie_degree_layout(n_edges, n_nodes, degrees, channels,
+                          workspace ? static_cast<char*>(workspace) + after256(L.bytes) : nullptr,
+                          true);
+    need = after256(L.bytes) + D.bytes;
+    if (D.smem_status != BYSJ_OK) return D.smem_status;
+  }
+  if (workspace == nullptr || workspace_bytes < need)
     return fail(BYSJ_ERR_WORKSPACE,
                 "zonal scatter backward: workspace of %zu bytes needed, %zu given",
-                L.bytes, workspace_bytes);
+                need, workspace_bytes);
   st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts, s),
                   "zonal scatter backward: ticket reset");
   if (st) return st;
@@ -947,6 +1036,19 @@ int bysj_gie_zonal_scatter_backward(
   a.lv = L.cfg.lv;
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
+  if (degrees > 0) {
+    st = cuda_check(cudaMemsetAsync(D.ss.tickets, 0, sizeof(int) * D.plan.parts, s),
+                    "zonal scatter backward: ticket reset (degree rows)");
+    if (st) return st;
+    GieArgs d = a;
+    d.lv = 0;
+    d.mp = MergePath{offsets, n_nodes, n_edges, D.plan.ipc, D.plan.parts};
+    d.ss = D.ss;
+    D.kernel<<<D.plan.blocks, kBlock, D.smem, s>>>(d, kSlotBaseOnDevice);
+    st = launch_check("gie_bwd_degree_kernel");
+    if (st) return st;
+    a.skip_degrees = degrees;
+  }
   const size_t smem = sizeof(float) * kBlock * L.cfg.nv;
   L.cfg.kernel<<<L.plan.blocks, kBlock, smem, s>>>(a);
   return launch_check("gie_bwd_kernel");

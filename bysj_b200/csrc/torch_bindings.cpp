@@ -488,27 +488,6 @@ void check_gie(const Tensor& zonal, const Tensor& radial, const Tensor& dst,
               "GIE inv_sqrt_deg must have shape (n_nodes,) or (n_nodes, 1, 1)");
 }
 
-// Number of degrees L when radial_slot is the degree-grouped layout
-// slot[r] = floor(sqrt(r+1)) + base with rows == (L+1)^2 - 1 (L <= 3), else 0;
-// sets `base`.  Reads the (tiny) slot table back to the host once.
-int64_t degree_layout(const Tensor& radial_slot, int64_t rows, int64_t n_radial,
-                      int64_t& base) {
-  int64_t degrees = 0;
-  for (int64_t l = 1; l <= 3; ++l)
-    if ((l + 1) * (l + 1) - 1 == rows) degrees = l;
-  if (degrees == 0) return 0;
-  Tensor host = radial_slot.to(torch::kCPU);  // one read back of the slot table
-  const int64_t* slot = host.data_ptr<int64_t>();
-  base = slot[0] - 1;
-  for (int64_t r = 0; r < rows; ++r) {
-    int64_t l = 0;
-    while ((l + 1) * (l + 1) <= r + 1) ++l;
-    if (slot[r] != l + base) return 0;
-  }
-  if (base < -1 || base + degrees > n_radial - 1) return 0;
-  return degrees;
-}
-
 Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor radial_slot,
                                  Tensor inv_sqrt_deg) {
   check_gie(zonal, radial, dst, radial_slot, inv_sqrt_deg);
@@ -518,22 +497,10 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
   const int64_t nodes = inv_sqrt_deg.size(0);
   Tensor out = torch::empty({nodes, rows + 1, channels}, zonal.options());
   if (nodes == 0) return out;
+  // The slot table stays on the device: for the degree-grouped shape the
+  // library launches the degree kernel and the generic one, and each checks
+  // the table itself (no read back here).
   auto [offsets, order] = csr_view(dst, nodes);
-  int64_t base = 0;
-  const int64_t degrees = degree_layout(radial_slot, rows, n_radial, base);
-  if (degrees > 0 && channels % 4 == 0 && channels <= 128 &&
-      ((channels / 4) & (channels / 4 - 1)) == 0 &&
-      reinterpret_cast<uintptr_t>(radial.data_ptr()) % 16 == 0) {
-    Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_degree_workspace_size(edges, nodes,
-                                                                              degrees, channels));
-    check(bysj_gie_zonal_scatter_forward_degree(
-              zonal.data_ptr<float>(), radial.data_ptr<float>(), offsets.data_ptr<int64_t>(),
-              opt_ptr<int64_t>(order), base, inv_sqrt_deg.data_ptr<float>(), edges, nodes,
-              degrees, n_radial, channels, out.data_ptr<float>(), ws.data_ptr(),
-              static_cast<size_t>(ws.numel()), stream_of(zonal)),
-          "gie_zonal_scatter_forward");
-    return out;
-  }
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_workspace_size(edges, nodes, rows, channels));
   check(bysj_gie_zonal_scatter_forward(
             zonal.data_ptr<float>(), radial.data_ptr<float>(), offsets.data_ptr<int64_t>(),
@@ -563,24 +530,6 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
   Tensor gi = torch::empty_like(inv_sqrt_deg);
   if (nodes == 0) return {gz, gr, gi};
   auto [offsets, order] = csr_view(dst, nodes);
-  int64_t base = 0;
-  const int64_t degrees = degree_layout(radial_slot, rows, n_radial, base);
-  if (degrees > 0 && channels % 4 == 0 && channels <= 64 &&
-      ((channels / 4) & (channels / 4 - 1)) == 0 &&
-      reinterpret_cast<uintptr_t>(radial.data_ptr()) % 16 == 0 &&
-      reinterpret_cast<uintptr_t>(grad_output.data_ptr()) % 16 == 0 &&
-      reinterpret_cast<uintptr_t>(gr.data_ptr()) % 16 == 0) {
-    Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_degree_workspace_size(
-                                     edges, nodes, degrees, channels));
-    check(bysj_gie_zonal_scatter_backward_degree(
-              grad_output.data_ptr<float>(), zonal.data_ptr<float>(), radial.data_ptr<float>(),
-              offsets.data_ptr<int64_t>(), opt_ptr<int64_t>(order), base,
-              inv_sqrt_deg.data_ptr<float>(), edges, nodes, degrees, n_radial, channels,
-              gz.data_ptr<float>(), gr.data_ptr<float>(), gi.data_ptr<float>(), ws.data_ptr(),
-              static_cast<size_t>(ws.numel()), stream_of(zonal)),
-          "gie_zonal_scatter_backward");
-    return {gz, gr, gi};
-  }
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_workspace_size(edges, nodes, rows,
                                                                               channels));
   check(bysj_gie_zonal_scatter_backward(

@@ -292,7 +292,10 @@ BYSJ_API int bysj_rmsnorm_backward(const float* grad_out, const float* x,
  *                    radial[e, radial_slot[r], c]      (normalise after sum)
  * zonal [n_edges, n_rows], radial [n_edges, n_radial, channels],
  * radial_slot int64 [n_rows], inv_sqrt_deg [n_nodes], out [n_nodes, n_rows+1,
- * channels].
+ * channels].  When the shape allows DPA4's degree-grouped layout (3, 8 or 15
+ * rows, channels = 4 * 2^k, 16-byte aligned rows) the forward and backward
+ * also launch the degree kernel; each kernel checks radial_slot on the device
+ * and only the matching one computes (radial_slot is not read back).
  * ------------------------------------------------------------------------ */
 BYSJ_API size_t bysj_gie_zonal_scatter_workspace_size(int64_t n_edges, int64_t n_nodes,
                                              int64_t n_rows, int64_t channels);
