@@ -230,6 +230,41 @@ def test_gie_degree_layout_backward(cuda, zero_based, channels, shuffled):
     assert all(torch.equal(a, b) for a, b in zip(got, again))
 
 
+@pytest.mark.parametrize("table", ["degree", "shuffled", "base1"])
+def test_gie_degree_shape_slot_table_checked_on_device(cuda, table):
+    # 15 rows and 64 channels: the shape of DPA4's degree layout, so the
+    # library launches both the degree kernel and the generic one and each
+    # decides on the device from the slot table.  The degree table (base 0,
+    # or base 1 over five radial slots) must be taken by the degree kernel
+    # with that base, a shuffled table by the generic kernel.
+    gen = torch.Generator().manual_seed({"degree": 1, "shuffled": 2, "base1": 3}[table])
+    sizes = torch.randint(0, 40, (300,), generator=gen)
+    sizes[7] = 900
+    dst = torch.repeat_interleave(torch.arange(300), sizes)
+    e = dst.numel()
+    n_radial = 4
+    slot = W.degree_slots()
+    if table == "shuffled":
+        slot = slot[torch.randperm(15, generator=gen)]
+    elif table == "base1":
+        slot = slot + 1  # degrees 1..3 read radial slots 2..4
+        n_radial = 5
+    z = torch.randn(e, 15, generator=gen)
+    r = torch.randn(e, n_radial, 64, generator=gen)
+    inv = torch.rand(300, generator=gen) + 0.2
+    up = torch.randn(300, 16, 64, generator=gen)
+    zc, rc, ic = (t.cuda().requires_grad_(True) for t in (z, r, inv))
+    out = K.zonal_scatter(zc, rc, dst.cuda(), slot.cuda(), ic)
+    zr, rr, ir = (t.clone().requires_grad_(True) for t in (z, r, inv))
+    want = zonal_scatter_reference(zr, rr, dst, slot, ir)
+    torch.testing.assert_close(out.detach().cpu(), want.detach(), rtol=1e-5,
+                               atol=1e-5 * float(want.detach().abs().max()))
+    got = torch.autograd.grad(out, (zc, rc, ic), up.cuda())
+    wg = torch.autograd.grad(want, (zr, rr, ir), up)
+    for a, b in zip(got, wg):
+        torch.testing.assert_close(a.cpu(), b, rtol=4e-4, atol=2e-5 * float(b.abs().max()) + 2e-5)
+
+
 def test_gie_degree_backward_inverse_gradient_sums_first(cuda):
     # Degree layout with L = 1 (rows 0..2 read radial slot 1): the three
     # edges' unnormalised sums cancel exactly before the dot with g.
