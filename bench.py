@@ -18,7 +18,12 @@ segment sum) producing [N, 8, 16, 8].  The metric is edges/s.
 * ``roofline``: the attention kernel's algorithmic bytes per launch over its
   average launch time (events on its stream), against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the reference's PyTorch oracle (restated under
-  ``oracle/``) on the host cores, on a bounded sample of the same frame.
+  ``oracle/``) on the host cores, on the whole frame; ``check``: the public
+  API's output of the e2e steps against that oracle output, elementwise at
+  rtol 1e-5 / atol 1e-6 (computed outside every timed region).
+* ``chain`` and ``partition``: the default run also measures the two other
+  multi-GPU workloads (below) on the same ranks, at most 10 timed steps each,
+  and attaches their lines.
 * ``ops``: per-operator roofline lines for the other configs at N = 1:
   segment_offsets, group_by_source, bf16-value attention, standalone
   softmax, segment_sum, force_assembly (Morton and random atom order),
@@ -30,9 +35,8 @@ segment sum) producing [N, 8, 16, 8].  The metric is edges/s.
 * ``--mode partition``: one 500k-atom box split by destination ranges over
   the ranks (strong scaling; force partials reduce-scattered over NCCL).
 
-``--impl reference`` times the CPU oracle instead (rank 0 only) and reports
-the same metric and config, its bounded sample described in
-``cpu_baseline.sample``.
+``--impl reference`` times the CPU oracle instead (rank 0 only) on the whole
+frame every step and reports the same metric and config.
 """
 from __future__ import annotations
 
@@ -67,6 +71,8 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-ops", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-extra", action="store_true",
+                   help="skip the chain and partition lines of the default run")
     p.add_argument("--profile-small", action="store_true",
                    help="tiny frame for ncu captures (not a bench number)")
     p.add_argument("--only", choices=sorted(OPS),
@@ -249,8 +255,15 @@ def attention_bytes(e, n, value_elem_bytes):
     return e * (8 * 4 + 16 * 64 * value_elem_bytes) + n * 16 * 64 * 4 + 8 * (n + 1)
 
 
-def cpu_sample_rate(g, logit, value, sample_nodes=2048, repeats=3):
-    """Oracle edges/s on the first ``sample_nodes`` segments of the frame."""
+def cpu_frame_rate(g, logit, value, out_public=None, repeats=2):
+    """The reference's PyTorch oracle on the WHOLE frame on the host cores.
+
+    Returns the ``cpu_baseline`` object (edges/s of one full frame, median of
+    ``repeats`` after one untimed run) and, when ``out_public`` (the public
+    API's [N, 8, 16, 8] output of the same frame, on the host) is given, the
+    ``check`` object: that output against the oracle's, elementwise at the
+    spec's rtol 1e-5 / atol 1e-6.  The oracle is only the checker here and
+    the timed CPU baseline; nothing on the GPU path calls it."""
     sys.path.insert(0, str(ROOT / "oracle"))
     from reference import segment_attention_reference
 
@@ -259,28 +272,39 @@ def cpu_sample_rate(g, logit, value, sample_nodes=2048, repeats=3):
     dst = g.dst.cpu()
     offsets = torch.zeros(g.n_atoms + 1, dtype=torch.int64)
     offsets[1:] = torch.cumsum(torch.bincount(dst, minlength=g.n_atoms), 0)
-    e_s = int(offsets[sample_nodes])
-    d = dst[:e_s].contiguous()
-    off = offsets[: sample_nodes + 1].contiguous()
-    lg = logit[:e_s].cpu()
-    val = value[:e_s].float().cpu()
-    segment_attention_reference(lg, val, d, off)  # warm-up
+    lg = logit.cpu()
+    val = value.float().cpu()
+    want = segment_attention_reference(lg, val, dst, offsets)  # untimed first run
     times = []
     for _ in range(repeats):
         t0 = time.perf_counter()
-        segment_attention_reference(lg, val, d, off)
+        segment_attention_reference(lg, val, dst, offsets)
         times.append(time.perf_counter() - t0)
     per = statistics.median(times)
-    return {
-        "value": e_s / per,
+    cpu = {
+        "value": g.n_edges / per,
         "unit": UNIT,
         "cores": cores,
         "kind": "port",
-        "sample": f"first {sample_nodes} of {g.n_atoms} segments ({e_s} edges), "
-                  f"oracle.reference.segment_attention_reference on CPU, "
-                  f"torch threads={torch.get_num_threads()}, median of {repeats}",
-        "seconds_per_sample": per,
+        "sample": f"the whole frame ({g.n_atoms} segments, {g.n_edges} edges): "
+                  f"oracle.reference.segment_attention_reference (the reference's "
+                  f"python/reference chain, restated) on CPU, torch threads="
+                  f"{torch.get_num_threads()}, median of {repeats} after one untimed run",
+        "seconds_per_frame": per,
     }
+    check = None
+    if out_public is not None:
+        got = out_public.reshape(want.shape)
+        diff = (got.double() - want.double()).abs()
+        bound = 1e-6 + 1e-5 * want.double().abs()
+        check = {"against": "fp32 oracle (reference.segment_attention_reference) on the whole "
+                            "frame, output of the public API (e2e path)",
+                 "elements": int(want.numel()), "rtol": 1e-5, "atol": 1e-6,
+                 "outside_tolerance": int((diff > bound).sum()),
+                 "max_abs_err": float(diff.max()),
+                 "max_err_over_bound": float((diff / bound).max()),
+                 "max_abs_value": float(want.abs().max())}
+    return cpu, check
 
 
 # ---------------------------------------------------------------------------
@@ -632,34 +656,41 @@ def measure_ops(g, logit, value32, device, peak, iters=20, only=None):
 # ---------------------------------------------------------------------------
 
 def run_reference(args, dist):
+    """The reference's CPU path on the whole C3 frame, rank 0 only.
+
+    The reference's own implementation of this path is its PyTorch
+    ``reference.*`` chain (its HIP kernels need a Hygon DCU); it is restated
+    under ``oracle/`` and timed here with all host threads on every step's full
+    frame (2.2 M edges, 9.1 GB of fp32 values), inputs drawn from a CPU
+    generator with the headline's shapes and distributions."""
     if dist.rank != 0:
         return
     from bysj_b200 import workloads as W
 
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
     g = W.c3_box(device="cpu", seed=args.seed)
     gen = torch.Generator().manual_seed(args.seed + 17)
-    sample_nodes = 1024
-    e_s = int((g.dst < sample_nodes).sum())
-    logit = torch.randn(e_s, 8, generator=gen) * (2.0 ** 0.5)
-    value = torch.randn(e_s, 16, 64, generator=gen)
+    e = g.n_edges
+    logit = torch.randn(e, 8, generator=gen) * (2.0 ** 0.5)
+    value = torch.randn(e, 16, 64, generator=gen)
     sys.path.insert(0, str(ROOT / "oracle"))
     from reference import segment_attention_reference
 
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    dst = g.dst[:e_s].contiguous()
-    off = torch.zeros(sample_nodes + 1, dtype=torch.int64)
-    off[1:] = torch.cumsum(torch.bincount(dst, minlength=sample_nodes), 0)
+    dst = g.dst.contiguous()
+    off = torch.zeros(g.n_atoms + 1, dtype=torch.int64)
+    off[1:] = torch.cumsum(torch.bincount(dst, minlength=g.n_atoms), 0)
     for _ in range(args.warmup):
         segment_attention_reference(logit, value, dst, off)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         segment_attention_reference(logit, value, dst, off)
     per = (time.perf_counter() - t0) / args.steps
-    rate = e_s / per
-    sample = (f"first {sample_nodes} of {g.n_atoms} segments ({e_s} edges) per step; "
-              "oracle.reference.segment_attention_reference (the reference's PyTorch "
-              "oracle, restated) on CPU")
+    rate = e / per
+    sample = (f"the whole frame per step ({g.n_atoms} segments, {e} edges); "
+              "oracle.reference.segment_attention_reference (the reference's python/reference "
+              f"softmax + weighted segment_sum chain, restated) on CPU, torch threads="
+              f"{torch.get_num_threads()}")
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -779,8 +810,11 @@ def run_ours(args, dist):
         torch.cuda.profiler.start()
         ops = measure_ops(g, logit, value32, device, peak)
         torch.cuda.profiler.stop()
+    check = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu and not args.profile_small:
-        cpu = cpu_sample_rate(g, logit, value)
+        # the public API's output of the e2e steps (or one more device step)
+        out_public = h_out if e2e is not None else step().cpu()
+        cpu, check = cpu_frame_rate(g, logit, value, out_public)
 
     if dist.rank == 0:
         line = {
@@ -795,9 +829,12 @@ def run_ours(args, dist):
             "clocks": clock_info,
             "gpu_launches": 3 * args.steps * dist.world,
         }
+        if check is not None:
+            line["check"] = check
         if ops:
             line["ops"] = ops
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
 CHAIN_CHANNELS = 32
@@ -941,7 +978,8 @@ def run_chain(args, dist):
             "gpu_launches": (None if per_frame_kernels is None
                              else per_frame_kernels * frames_total * args.steps),
         }
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
 def run_partition(args, dist):
@@ -1024,7 +1062,16 @@ def run_partition(args, dist):
     step_max = dist.max(start.elapsed_time(end) / 1e3 / args.steps)
     kernel_s = statistics.mean(a.elapsed_time(b) for a, b in pairs) / 1e3
 
-    # check: this rank's forces against the single-device assembly of the whole box
+    # check: repeated steps give bit-identical forces (fixed reduction orders
+    # on every rank and in the collective) ...
+    force = force.clone()
+    virial = virial.clone()
+    _, (force2, virial2) = step()
+    torch.cuda.synchronize()
+    same = float(torch.equal(force, force2) and torch.equal(virial, virial2))
+    repeat_same = dist.sum(same) == float(dist.world)
+    del force2, virial2
+    # ... and this rank's forces match the single-device assembly of the whole box
     order, soff = K.group_by_source(g.src, n)
     f_ref, v_ref = _C.force_assembly(grad_all, vec_all, offsets, soff, order)
     err = max(float((force - part.atoms(f_ref)).abs().max()) if part.n_local else 0.0,
@@ -1057,11 +1104,16 @@ def run_partition(args, dist):
                          "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                          "kernel": "segment_attention_kernel (rank 0)",
                          "kernel_ms": kernel_s * 1e3, "peak_source": peak_src},
-            "check": {"max_abs_err_vs_single_device": err, "max_abs_force": scale},
+            "check": {"max_abs_err_vs_single_device": err, "max_abs_force": scale,
+                      "bit_identical_repeat": repeat_same,
+                      "exchange": "float64 source partials, NCCL reduce-scatter (sum)",
+                      "nccl_algo": os.environ.get("NCCL_ALGO", "default"),
+                      "nccl_proto": os.environ.get("NCCL_PROTO", "default")},
             "clocks": clock_info,
             "gpu_launches": None if launches is None else int(launches) * args.steps,
         }
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
 def run_only(args):
@@ -1080,6 +1132,15 @@ def run_only(args):
           flush=True)
 
 
+def extra_args(args):
+    """Arguments of the chain and partition lines that the default run adds:
+    the same job, at most 10 timed steps after 3-5 warm-up steps."""
+    extra = argparse.Namespace(**vars(args))
+    extra.steps = max(1, min(args.steps, 10))
+    extra.warmup = max(3, min(args.warmup, 5))
+    return extra
+
+
 def main():
     args = parse_args()
     dist = Dist()
@@ -1091,7 +1152,22 @@ def main():
         return
     dist.setup("nccl")
     try:
-        {"partition": run_partition, "chain": run_chain}.get(args.mode, run_ours)(args, dist)
+        if args.mode == "frames":
+            line = run_ours(args, dist)
+            if not args.no_extra and not args.profile_small:
+                # the two other multi-GPU workloads, same ranks, same
+                # collective order on every rank; their own timings and checks
+                torch.cuda.empty_cache()
+                chain = run_chain(extra_args(args), dist)
+                torch.cuda.empty_cache()
+                part = run_partition(extra_args(args), dist)
+                if line is not None:
+                    line["chain"] = chain
+                    line["partition"] = part
+        else:
+            line = {"partition": run_partition, "chain": run_chain}[args.mode](args, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
     finally:
         dist.close()
 

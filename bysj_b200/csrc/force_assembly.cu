@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kBlock, kForceMinBlocks)
                           const int64_t* __restrict__ src_order,
                           int64_t n_nodes, float* __restrict__ force,
                           float* __restrict__ virial,
-                          float* __restrict__ partial) {
+                          double* __restrict__ partial) {
   __shared__ double fold[kWarpsPerBlock][kTriplets * 12];
   const int lane = lane_id();
   const int T = lane / 3;
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kBlock, kForceMinBlocks)
         if (lane < 3) force[atom * 3 + lane] = static_cast<float>(v);
         else if (virial) virial[atom * 9 + (lane - 3)] = static_cast<float>(v);
       } else {
-        partial[atom * 12 + lane] = static_cast<float>(v);
+        partial[atom * 12 + lane] = v;
       }
     }
     __syncwarp();
@@ -191,10 +191,11 @@ __global__ void __launch_bounds__(kBlock, kForceMinBlocks)
 bool force_index32(int64_t n_edges) { return n_edges < (int64_t{1} << 31) / 3 - 1; }
 
 // force[k] = sum_{dst(e)=k} g_e + summed[k, 0:3];  virial[k] = summed[k, 3:12]
+// (summed in fp64: the partials of all ranks, added before one rounding)
 __global__ void __launch_bounds__(kBlock)
     force_dst_add_kernel(const float* __restrict__ grad_edge,
                          const int64_t* __restrict__ dst_offsets,
-                         int64_t n_local, const float* __restrict__ summed,
+                         int64_t n_local, const double* __restrict__ summed,
                          float* __restrict__ force, float* __restrict__ virial) {
   const int lane = lane_id();
   const int sub = lane & (kLanesPerAtom - 1);
@@ -220,11 +221,11 @@ __global__ void __launch_bounds__(kBlock)
     if (sub < 3) {
       const double v = sub == 0 ? acc[0] : sub == 1 ? acc[1] : acc[2];
       force[atom * 3 + sub] =
-          static_cast<float>(v + static_cast<double>(summed[atom * 12 + sub]));
+          static_cast<float>(v + summed[atom * 12 + sub]);
     }
     if (virial) {
-      virial[atom * 9 + sub] = summed[atom * 12 + 3 + sub];
-      if (sub == 0) virial[atom * 9 + 8] = summed[atom * 12 + 11];
+      virial[atom * 9 + sub] = static_cast<float>(summed[atom * 12 + 3 + sub]);
+      if (sub == 0) virial[atom * 9 + 8] = static_cast<float>(summed[atom * 12 + 11]);
     }
   }
 }
@@ -284,7 +285,7 @@ int bysj_force_assembly_src_partial(const float* grad_edge,
                                     const float* edge_vec,
                                     const int64_t* src_offsets,
                                     const int64_t* src_order, int64_t n_edges,
-                                    int64_t n_nodes, float* partial,
+                                    int64_t n_nodes, double* partial,
                                     void* stream) {
   clear_error();
   if (n_edges < 0 || n_nodes < 0)
@@ -308,7 +309,7 @@ int bysj_force_assembly_src_partial(const float* grad_edge,
 
 int bysj_force_assembly_dst_add(const float* grad_edge,
                                 const int64_t* dst_offsets, int64_t n_local,
-                                const float* summed_partial, float* force,
+                                const double* summed_partial, float* force,
                                 float* virial, void* stream) {
   clear_error();
   if (n_local < 0)

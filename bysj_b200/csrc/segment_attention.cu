@@ -17,6 +17,7 @@
 // sum; the last piece to finish rescales them by exp(m_q - m) in partition
 // order, so results are deterministic.
 #include <mutex>
+#include <utility>
 
 #include "launch.cuh"
 
@@ -465,11 +466,48 @@ namespace bysj {
 namespace {
 
 std::mutex g_noalloc_mutex;
-void* g_noalloc_address[64] = {};
+struct NoallocSlot {
+  unsigned long long context = 0;  // unique id of the context the address belongs to
+  void* address = nullptr;
+};
+NoallocSlot g_noalloc_slot[64];
 
-// Device address of the scratch array for the current device.  In host code
-// the array's name is only a host-side handle, so the address is looked up
-// once per device (with that device current) and cached.
+// Unique id of the calling thread's current CUDA context (0 if none or if the
+// driver entry points are unavailable).  Context ids are never reused within a
+// process, so an address cached under one stays valid exactly as long as that
+// context: after cudaDeviceReset the runtime creates a new context on the
+// next call, the library's module is loaded again and the array may move.
+// The driver functions are looked up through the runtime, so the library needs
+// no link-time dependency on the driver library.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static const std::pair<GetCurrent, GetId> fns = [] {
+    void* cur = nullptr;
+    void* id = nullptr;
+    cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound;
+    cudaDriverEntryPointQueryResult q2 = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &cur, 12000, cudaEnableDefault,
+                                         &q1) != cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess)
+      cur = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &id, 12000, cudaEnableDefault, &q2) !=
+            cudaSuccess ||
+        q2 != cudaDriverEntryPointSuccess)
+      id = nullptr;
+    return std::make_pair(reinterpret_cast<GetCurrent>(cur), reinterpret_cast<GetId>(id));
+  }();
+  if (fns.first == nullptr || fns.second == nullptr) return 0;
+  void* ctx = nullptr;
+  if (fns.first(&ctx) != 0 || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (fns.second(ctx, &id) != 0) return 0;
+  return id;
+}
+
+// Device address of the scratch array in the current device's context.  In
+// host code the array's name is only a host-side handle, so the address is
+// looked up (with the device current) once per device and context and cached.
 int noalloc_scratch_address(void** address) {
   int device = 0;
   int st = cuda_check(cudaGetDevice(&device), "segment attention (no-alloc): current device");
@@ -477,14 +515,17 @@ int noalloc_scratch_address(void** address) {
   if (device < 0 || device >= 64)
     return fail(BYSJ_ERR_UNSUPPORTED, "segment attention (no-alloc): device %d", device);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_address[device] == nullptr) {
+  NoallocSlot& slot = g_noalloc_slot[device];
+  const unsigned long long ctx = current_context_id();
+  if (slot.address == nullptr || ctx == 0 || ctx != slot.context) {
     void* ptr = nullptr;
     st = cuda_check(cudaGetSymbolAddress(&ptr, bysj_attention_noalloc_scratch),
                     "segment attention (no-alloc): scratch address");
     if (st) return st;
-    g_noalloc_address[device] = ptr;
+    slot.address = ptr;
+    slot.context = current_context_id();  // the lookup made the context current
   }
-  *address = g_noalloc_address[device];
+  *address = slot.address;
   return BYSJ_OK;
 }
 

@@ -378,11 +378,11 @@ Tensor force_assembly_src_partial(Tensor grad_edge, Tensor edge_vec, Tensor src_
   i64(src_order, "src_order");
   const int64_t nodes = src_offsets.size(0) - 1;
   c10::cuda::CUDAGuard guard(grad_edge.device());
-  Tensor partial = torch::empty({nodes, 12}, grad_edge.options());
+  Tensor partial = torch::empty({nodes, 12}, grad_edge.options().dtype(torch::kFloat64));
   check(bysj_force_assembly_src_partial(grad_edge.data_ptr<float>(), edge_vec.data_ptr<float>(),
                                         src_offsets.data_ptr<int64_t>(),
                                         src_order.data_ptr<int64_t>(), grad_edge.size(0), nodes,
-                                        partial.data_ptr<float>(), stream_of(grad_edge)),
+                                        partial.data_ptr<double>(), stream_of(grad_edge)),
         "force_assembly_src_partial");
   return partial;
 }
@@ -391,14 +391,15 @@ std::tuple<Tensor, Tensor> force_assembly_dst_add(Tensor grad_edge, Tensor dst_o
                                                   Tensor summed_partial) {
   f32(grad_edge, "grad_edge");
   i64(dst_offsets, "dst_offsets");
-  f32(summed_partial, "summed_partial");
+  TORCH_CHECK(summed_partial.scalar_type() == torch::kFloat64 && summed_partial.is_contiguous(),
+              "summed_partial must be a contiguous float64 tensor");
   const int64_t local = dst_offsets.size(0) - 1;
   TORCH_CHECK(summed_partial.numel() == local * 12, "summed_partial must have shape (n_local, 12)");
   c10::cuda::CUDAGuard guard(grad_edge.device());
   Tensor force = torch::empty({local, 3}, grad_edge.options());
   Tensor virial = torch::empty({local, 9}, grad_edge.options());
   check(bysj_force_assembly_dst_add(grad_edge.data_ptr<float>(), dst_offsets.data_ptr<int64_t>(),
-                                    local, summed_partial.data_ptr<float>(),
+                                    local, summed_partial.data_ptr<double>(),
                                     force.data_ptr<float>(), virial.data_ptr<float>(),
                                     stream_of(grad_edge)),
         "force_assembly_dst_add");

@@ -246,17 +246,19 @@ BYSJ_API int bysj_force_assembly(const float* grad_edge, const float* edge_vec,
  * where the edges given here are only this partition's; the destination side
  * force[k] += sum_{dst(e)=k} g_e is added by bysj_force_assembly_dst_add for
  * the local atoms [node_begin, node_begin + n_local) after the partials of all
- * partitions have been summed (reduce-scattered).  No reference counterpart:
- * this is the multi-GPU decomposition of csrc/force_assembly.cpp:64-96. */
+ * partitions have been summed (reduce-scattered).  The partials are float64
+ * (the per-partition fp64 sums, unrounded), so the exchanged sums are rounded
+ * to float32 once, as on one device.  No reference counterpart: this is the
+ * multi-GPU decomposition of csrc/force_assembly.cpp:64-96. */
 BYSJ_API int bysj_force_assembly_src_partial(const float* grad_edge,
                                     const float* edge_vec,
                                     const int64_t* src_offsets,
                                     const int64_t* src_order, int64_t n_edges,
-                                    int64_t n_nodes, float* partial,
+                                    int64_t n_nodes, double* partial,
                                     void* stream);
 BYSJ_API int bysj_force_assembly_dst_add(const float* grad_edge,
                                 const int64_t* dst_offsets, int64_t n_local,
-                                const float* summed_partial, float* force,
+                                const double* summed_partial, float* force,
                                 float* virial, void* stream);
 
 /* ------------------------------------------------------------------------

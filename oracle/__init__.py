@@ -7,11 +7,13 @@ Nothing in ``bysj_b200`` imports this package.  Only ``tests/``,
 Contents
 --------
 ``oracle.reference``
-    A restatement, in PyTorch fp32 on the CPU, of the reference project's
+    The restatement, in PyTorch fp32, of the reference project's
     ``python/reference`` package (lipengfei1409/bysj): same function names,
     arguments, validation and results (``segment_sum_reference``,
     ``segment_softmax_reference``, ``force_assembly_reference``, ``rmsnorm``,
-    ``zonal_scatter_reference``) plus the two compositions the reference has no
+    ``zonal_scatter_reference``).  Its one copy ships as
+    ``bysj_b200.reference``; this package re-exports it.  Plus the two
+    compositions the reference has no
     single function for (fused softmax + weighted sum, per-degree RMSNorm).
 ``oracle.truth``
     float64 NumPy ground truth of every operator, and the integer CSR helpers

@@ -130,7 +130,8 @@ def test_force_c1_matches_oracle_and_conserves_momentum(cuda):
 
 
 def test_force_heavy_atoms_use_several_slot_rounds(cuda):
-    # more than 12 slots per lane (8 lanes per atom): the slot loop repeats
+    # 64 atoms of 80-400 edges per side: every atom runs several 60-slot
+    # chunks of its triplet loop
     gen = torch.Generator().manual_seed(21)
     sizes = torch.randint(80, 400, (64,), generator=gen)
     dst = torch.repeat_interleave(torch.arange(64), sizes)
@@ -141,8 +142,9 @@ def test_force_heavy_atoms_use_several_slot_rounds(cuda):
     grad, vec = torch.randn(e, 3, generator=gen), torch.randn(e, 3, generator=gen)
     force, virial = K.force_assembly(grad.cuda(), vec.cuda(), src.cuda(), dst.cuda(), off.cuda())
     tf, tv = truth.force_assembly(grad.numpy(), vec.numpy(), src.numpy(), dst.numpy(), 64)
-    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=1e-6, atol=1e-4)
-    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=1e-6, atol=1e-4)
+    # fp64 sums rounded once to fp32: within 2 ulp of the float64 truth
+    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=2.0 ** -22, atol=1e-7)
+    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=2.0 ** -22, atol=1e-7)
 
 
 def test_force_skewed_and_empty_atom(cuda):
@@ -156,8 +158,43 @@ def test_force_skewed_and_empty_atom(cuda):
     force, virial = K.force_assembly(grad.cuda(), vec.cuda(), src.cuda(), dst, off)
     tf, tv = truth.force_assembly(grad.numpy(), vec.numpy(), src.numpy(), dst.cpu().numpy(),
                                   sizes.numel())
-    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=1e-6, atol=1e-5)
-    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=1e-6, atol=1e-5)
+    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=2.0 ** -22, atol=1e-7)
+    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=2.0 ** -22, atol=1e-7)
+
+
+def test_force_hub_source_atom_and_unsorted_sources(cuda):
+    # Atom 37 is the source of 4000 extra edges (a hub on the gathered side),
+    # sources are in random order inside each destination segment, and edge
+    # vectors are long (|v| ~ 5): forces and virials stay within 2 ulp of the
+    # float64 truth, repeats are bit-identical, and the source-side partial
+    # used by the multi-GPU partition agrees with the truth in fp64.
+    gen = torch.Generator().manual_seed(33)
+    n = 200
+    sizes = torch.randint(50, 120, (n,), generator=gen)
+    dst = torch.repeat_interleave(torch.arange(n), sizes)
+    off = torch.zeros(n + 1, dtype=torch.int64)
+    off[1:] = torch.cumsum(sizes, 0)
+    e = dst.numel()
+    src = torch.randint(0, n, (e,), generator=gen)
+    src[torch.randperm(e, generator=gen)[:4000]] = 37
+    grad = torch.randn(e, 3, generator=gen) * 0.1
+    vec = torch.randn(e, 3, generator=gen) * 3.0
+    force, virial = K.force_assembly(grad.cuda(), vec.cuda(), src.cuda(), dst.cuda(), off.cuda())
+    tf, tv = truth.force_assembly(grad.numpy(), vec.numpy(), src.numpy(), dst.numpy(), n)
+    np.testing.assert_allclose(force.cpu().numpy(), tf, rtol=2.0 ** -22, atol=1e-7)
+    np.testing.assert_allclose(virial.cpu().numpy(), tv, rtol=2.0 ** -22, atol=1e-7)
+    f2, v2 = K.force_assembly(grad.cuda(), vec.cuda(), src.cuda(), dst.cuda(), off.cuda())
+    assert torch.equal(force, f2) and torch.equal(virial, v2)
+    # the source-side partial (multi-GPU form) takes the same two paths
+    order, soff = K.group_by_source(src.cuda(), n)
+    part = _C().force_assembly_src_partial(grad.cuda(), vec.cuda(), soff, order)
+    src_only = truth.force_assembly(grad.numpy(), vec.numpy(), src.numpy(), dst.numpy(), n)
+    dst_side = np.zeros((n, 3))
+    np.add.at(dst_side, dst.numpy(), grad.numpy().astype(np.float64))
+    np.testing.assert_allclose(part[:, :3].cpu().numpy(), src_only[0] - dst_side,
+                               rtol=2.0 ** -22, atol=1e-7)
+    np.testing.assert_allclose(part[:, 3:].cpu().numpy(), src_only[1], rtol=2.0 ** -22,
+                               atol=1e-7)
 
 
 @pytest.mark.parametrize("parts", [2, 3])
@@ -173,7 +210,7 @@ def test_force_dst_range_partition_matches_single_device(cuda, parts):
     plan = [S.make_partition(off, g.src, r, parts) for r in range(parts)]
     partials = [_C().force_assembly_src_partial(p.edges(grad), p.edges(g.edge_vec),
                                                 p.src_offsets, p.src_order) for p in plan]
-    total = torch.stack(partials).double().sum(0).float()
+    total = torch.stack(partials).sum(0)
     got_f, got_v = [], []
     for p in plan:
         f, v = S.force_assembly_partitioned(
@@ -181,8 +218,9 @@ def test_force_dst_range_partition_matches_single_device(cuda, parts):
             combine=lambda _, q: total[q.rank * q.chunk:(q.rank + 1) * q.chunk])
         got_f.append(f)
         got_v.append(v)
-    torch.testing.assert_close(torch.cat(got_f), force, rtol=1e-5, atol=1e-5)
-    torch.testing.assert_close(torch.cat(got_v), virial, rtol=1e-5, atol=1e-5)
+    # fp64 partials: the partitioned sums round to fp32 once, as on one device
+    torch.testing.assert_close(torch.cat(got_f), force, rtol=2.0 ** -22, atol=1e-7)
+    torch.testing.assert_close(torch.cat(got_v), virial, rtol=2.0 ** -22, atol=1e-7)
 
 
 def _C():

@@ -35,14 +35,14 @@ def cpu_src_partial(g, v, soff, order):
     part = torch.zeros(n, 12, dtype=torch.float64)
     part[:, :3].index_add_(0, owner, -gs)
     part[:, 3:].index_add_(0, owner, -(gs[:, :, None] * vs[:, None, :]).reshape(-1, 9))
-    return part.float()
+    return part
 
 
 def cpu_dst_add(g, doff, summed):
     n = doff.numel() - 1
     owner = torch.repeat_interleave(torch.arange(n), doff[1:] - doff[:-1])
-    force = summed[:, :3].double().index_add(0, owner, g.double())
-    return force.float(), summed[:, 3:].clone()
+    force = summed[:, :3].index_add(0, owner, g.double())
+    return force.float(), summed[:, 3:].float()
 
 
 def offsets_of(dst, n):
@@ -97,7 +97,7 @@ def test_partition_single_rank_matches_truth():
     partials = [cpu_src_partial(p.edges(grad), p.edges(g.edge_vec), p.src_offsets, p.src_order)
                 for p in parts]
     assert all(x.shape == (3 * parts[0].chunk, 12) for x in partials)
-    total = torch.stack(partials).double().sum(0).float()
+    total = torch.stack(partials).sum(0)
     force, virial = [], []
     for p in parts:
         f, v = S.force_assembly_partitioned(

@@ -51,18 +51,18 @@ def stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def make_case(seed, value_dtype, skewed):
+def make_case(seed, value_dtype, skewed, comps=16, channels=64, sizes=None):
     gen = torch.Generator().manual_seed(seed)
-    if skewed:
+    if sizes is None and skewed:
         sizes = torch.randint(0, 12, (400,), generator=gen)
         sizes[100], sizes[-1] = 6000, 2500
-    else:
+    elif sizes is None:
         sizes = torch.randint(60, 120, (192,), generator=gen)
     offsets = torch.zeros(sizes.numel() + 1, dtype=torch.int64)
     offsets[1:] = torch.cumsum(sizes, 0)
     e, n = int(offsets[-1]), sizes.numel()
     logit = torch.randn(e, 8, generator=gen) * 2
-    value = torch.randn(e, 16, 64, generator=gen).to(value_dtype)
+    value = torch.randn(e, comps, channels, generator=gen).to(value_dtype)
     env = torch.rand(e, generator=gen) + 0.05
     null = torch.randn(n, 8, generator=gen)
     return [t.cuda() for t in (logit, value, env, null, offsets)]
@@ -72,26 +72,35 @@ def dtype_code(t):
     return 1 if t.dtype == torch.bfloat16 else 0
 
 
+def workspace_bytes(lib, logit, value, offsets):
+    e, h = logit.shape
+    _, comps, channels = value.shape
+    return lib.bysj_segment_attention_workspace_size(e, offsets.numel() - 1, h, comps, channels,
+                                                     dtype_code(value))
+
+
 def with_workspace(lib, logit, value, env, null, offsets):
     e, h = logit.shape
+    _, comps, channels = value.shape
     n = offsets.numel() - 1
-    out = torch.empty(n, h, 16, 64 // h, device="cuda")
-    size = lib.bysj_segment_attention_workspace_size(e, n, h, 16, 64, dtype_code(value))
+    out = torch.empty(n, h, comps, channels // h, device="cuda")
+    size = workspace_bytes(lib, logit, value, offsets)
     ws = torch.empty(max(size, 1), dtype=torch.uint8, device="cuda")
     status = lib.bysj_segment_attention_forward(
         ptr(logit), ptr(value), dtype_code(value), ptr(env), ptr(null), ptr(offsets), None,
-        e, n, h, 16, 64, ptr(out), ptr(ws), size, stream())
+        e, n, h, comps, channels, ptr(out), ptr(ws), size, stream())
     assert status == 0, lib.bysj_last_error()
     return out
 
 
 def without_workspace(lib, logit, value, env, null, offsets):
     e, h = logit.shape
+    _, comps, channels = value.shape
     n = offsets.numel() - 1
-    out = torch.empty(n, h, 16, 64 // h, device="cuda")
+    out = torch.empty(n, h, comps, channels // h, device="cuda")
     status = lib.bysj_segment_attention_forward_noalloc(
         ptr(logit), ptr(value), dtype_code(value), ptr(env), ptr(null), ptr(offsets), None,
-        e, n, h, 16, 64, ptr(out), stream())
+        e, n, h, comps, channels, ptr(out), stream())
     assert status == 0, lib.bysj_last_error()
     return out
 
@@ -106,6 +115,29 @@ def test_noalloc_matches_the_workspace_entry_point_on_two_calls_in_a_row(lib):
     torch.testing.assert_close(out2, with_workspace(lib, *second), rtol=1e-5, atol=1e-6)
     # Leftovers of the previous call in the shared scratch do not leak into results.
     assert torch.equal(without_workspace(lib, *first), out1)
+
+
+def test_noalloc_capped_plan_matches_the_workspace_entry_point(lib):
+    # Cases whose workspace plan (one partition per resident warp) needs more
+    # than the fixed 16 MiB, so the entry point runs the capped plan: fewer,
+    # longer partitions and segments split over several of them.
+    cap = 16 * 1024 * 1024
+    gen = torch.Generator().manual_seed(7)
+    # about 54k edges with the headline's [16, 64] rows
+    frame = make_case(3, torch.float32, False,
+                      sizes=torch.randint(60, 120, (600,), generator=gen))
+    # 16 x 1024 rows (cap of ~127 partitions) with one 3000-edge hub segment
+    sizes = torch.randint(0, 12, (300,), generator=gen)
+    sizes[150] = 3000
+    wide = make_case(4, torch.float32, False, comps=16, channels=1024, sizes=sizes)
+    for case in (frame, wide):
+        logit, value, _, _, offsets = case
+        assert workspace_bytes(lib, logit, value, offsets) > cap
+        first = without_workspace(lib, *case)
+        second = without_workspace(lib, *case)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(first, with_workspace(lib, *case), rtol=1e-5, atol=1e-6)
+        assert torch.equal(first, second)
 
 
 def test_noalloc_refuses_rows_too_wide_for_the_fixed_scratch(lib):
