@@ -548,6 +548,38 @@ def _op_zonal_bwd(ctx):
                             "the device CSR view of dst"})
 
 
+def _op_rotate(ctx):
+    """Fused rotate-back aggregation on the C3 frame: messages [E,16,64] fp32
+    (the value rows), packed orthogonal rotations [E,84], attention weights
+    [E,8] normalised per segment, per-edge rescale -> [N,16,64]."""
+    from bysj_b200 import kernels as K
+
+    g, e, n = ctx["g"], ctx["g"].n_edges, ctx["g"].n_atoms
+    device = ctx["device"]
+    gen = torch.Generator().manual_seed(96)
+    blocks = []
+    for l in range(4):
+        q, _ = torch.linalg.qr(torch.randn(4096, 2 * l + 1, 2 * l + 1, generator=gen,
+                                           dtype=torch.float64))
+        blocks.append(q.reshape(4096, -1))
+    pool = torch.cat(blocks, 1).float().to(device)
+    rot = pool[torch.arange(e, device=device) % 4096].contiguous()
+    logit = ctx["logit"]()
+    peak = torch.full((n, 8), -float("inf"), device=device).scatter_reduce(
+        0, g.dst[:, None].expand(-1, 8), logit, "amax")
+    w = torch.exp(logit - peak[g.dst])
+    alpha = (w / torch.zeros_like(peak).index_add_(0, g.dst, w)[g.dst]).contiguous()
+    scale = torch.rand(e, device=device) + 0.5
+    x = ctx["value32"]()
+    off = ctx["offsets"]
+    t = time_launches(lambda: K.rotate_back_aggregate(x, rot, scale, alpha, None, off, g.dst, 3,
+                                                      8), ctx["iters"])
+    return op_line("rotate_back_aggregate", e * (4096 + 336 + 32 + 4) + n * 4096 + 8 * (n + 1),
+                   t, ctx["peak"], e,
+                   {"note": "rotate-back (84 coefficients per edge) + weighting + destination "
+                            "sum in one pass; inputs larger than L2"})
+
+
 def _op_small_step_graph(ctx):
     """A launch-bound step on the 192-atom C1 box, eager and as a CUDA-graph replay."""
     from bysj_b200 import _C
@@ -611,6 +643,7 @@ OPS = {
     "softmax_bwd": _op_softmax_bwd,
     "rmsnorm_bwd": _op_rmsnorm_bwd,
     "zonal_bwd": _op_zonal_bwd,
+    "rotate": _op_rotate,
 }
 
 

@@ -53,6 +53,7 @@ CU_SOURCES = [
     "force_assembly.cu",
     "rmsnorm.cu",
     "gie.cu",
+    "rotate_aggregate.cu",
 ]
 HEADERS = ["common.cuh", "launch.cuh"]
 

@@ -340,6 +340,50 @@ Tensor segment_attention_forward(Tensor logit, Tensor value, Tensor offsets, Opt
   return out;
 }
 
+// ---- rotate-back aggregation --------------------------------------------------
+
+Tensor rotate_back_aggregate_forward(Tensor x_local, Tensor rotation, OptTensor rescale,
+                                     Tensor alpha, Tensor offsets, OptTensor order,
+                                     int64_t lmax, int64_t heads) {
+  f32(x_local, "rotate-back x_local");
+  f32(rotation, "rotate-back rotation");
+  f32(alpha, "rotate-back attn_alpha");
+  i64(offsets, "rotate-back row_ptr");
+  TORCH_CHECK(x_local.dim() == 3, "rotate-back x_local must have shape (n_edges, S, channels)");
+  const int64_t edges = x_local.size(0), comps = x_local.size(1), channels = x_local.size(2);
+  TORCH_CHECK(lmax >= 0 && comps == (lmax + 1) * (lmax + 1),
+              "rotate-back x_local must have (lmax + 1)^2 components");
+  const int64_t packed = (lmax + 1) * (2 * lmax + 1) * (2 * lmax + 3) / 3;
+  TORCH_CHECK(rotation.dim() == 2 && rotation.size(0) == edges && rotation.size(1) == packed,
+              "rotate-back rotation must have shape (n_edges, sum_l (2l+1)^2)");
+  TORCH_CHECK(heads > 0 && channels % heads == 0, "rotate-back heads must divide the channels");
+  TORCH_CHECK(alpha.dim() == 2 && alpha.size(0) == edges && alpha.size(1) == heads,
+              "rotate-back attn_alpha must have shape (n_edges, heads)");
+  if (rescale) {
+    f32(*rescale, "rotate-back rotate_inv_rescale");
+    TORCH_CHECK(rescale->numel() == edges, "rotate-back rotate_inv_rescale must have n_edges");
+  }
+  if (order) i64(*order, "rotate-back order");
+  same_device(x_local, rotation, "rotation");
+  same_device(x_local, alpha, "attn_alpha");
+  same_device(x_local, offsets, "row_ptr");
+  same_device(x_local, rescale, "rotate_inv_rescale");
+  same_device(x_local, order, "order");
+  const int64_t nodes = offsets.size(0) - 1;
+  c10::cuda::CUDAGuard guard(x_local.device());
+  Tensor out = torch::empty({nodes, comps, channels}, x_local.options());
+  if (nodes == 0) return out;
+  Tensor ws = workspace(x_local, bysj_rotate_back_aggregate_workspace_size(edges, nodes, lmax,
+                                                                           heads, channels));
+  check(bysj_rotate_back_aggregate(
+            x_local.data_ptr<float>(), rotation.data_ptr<float>(), opt_ptr<float>(rescale),
+            alpha.data_ptr<float>(), offsets.data_ptr<int64_t>(), opt_ptr<int64_t>(order),
+            edges, nodes, lmax, heads, channels, out.data_ptr<float>(), ws.data_ptr(),
+            static_cast<size_t>(ws.numel()), stream_of(x_local)),
+        "rotate_back_aggregate_forward");
+  return out;
+}
+
 // ---- force_assembly ---------------------------------------------------------
 
 std::tuple<Tensor, Tensor> force_assembly(Tensor grad_edge, Tensor edge_vec, Tensor dst_offsets,
@@ -575,6 +619,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("segment_attention_forward", &segment_attention_forward, py::arg("logit"),
         py::arg("value"), py::arg("offsets"), py::arg("env") = py::none(),
         py::arg("null_logit") = py::none(), py::arg("order") = py::none());
+  m.def("rotate_back_aggregate_forward", &rotate_back_aggregate_forward, py::arg("x_local"),
+        py::arg("rotation"), py::arg("rotate_inv_rescale"), py::arg("attn_alpha"),
+        py::arg("row_ptr"), py::arg("order"), py::arg("lmax"), py::arg("heads"));
   m.def("force_assembly_src_partial", &force_assembly_src_partial, py::arg("grad_edge"),
         py::arg("edge_vec"), py::arg("src_offsets"), py::arg("src_order"));
   m.def("force_assembly_dst_add", &force_assembly_dst_add, py::arg("grad_edge"),

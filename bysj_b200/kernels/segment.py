@@ -39,6 +39,7 @@ _CHECK_GROUPING = os.environ.get("DPA4_CHECK_GROUPING", "0").strip().lower() in 
 }
 
 _FLAG_OUT_OF_RANGE = 1
+_FLAG_UNSORTED = 2
 
 
 def segment_offsets(dst: torch.Tensor, n_nodes: int) -> torch.Tensor:
@@ -63,6 +64,40 @@ def segment_offsets(dst: torch.Tensor, n_nodes: int) -> torch.Tensor:
     if flags & _FLAG_OUT_OF_RANGE:
         raise ValueError("destination values must be within the node range")
     return offsets
+
+
+def destination_csr(dst: torch.Tensor, n_nodes: int) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Destination CSR view ``(offsets, order)`` of an edge list in any order.
+
+    Replaces the seam's ``bincount`` + ``argsort`` (reference
+    ``python/model/fused_deepmd.py:111-124``) with device kernels: the
+    boundary kernel when ``dst`` is already non-decreasing (``order`` is then
+    ``None``: the edges are their own grouping, so the segmented operators
+    read them in place), otherwise the histogram for the offsets and the
+    stable device grouping for ``order`` (bit-identical to
+    ``torch.argsort(dst, stable=True)``).  One flag word is read back, as in
+    :func:`segment_offsets`.
+    """
+    if not isinstance(dst, torch.Tensor):
+        raise TypeError("destination CSR requires a tensor of destinations")
+    if dst.dtype != torch.int64:
+        raise TypeError("destination CSR requires int64 destinations")
+    if int(n_nodes) <= 0:
+        raise ValueError("destination CSR requires a positive node count")
+    if dst.ndim != 1:
+        raise ValueError("destination CSR requires a one-dimensional dst")
+    require_dcu(dst)
+    extension = _extension("segment_offsets")
+    dst = dst.contiguous()
+    offsets, flags = extension.segment_offsets(dst, int(n_nodes))
+    if flags & _FLAG_OUT_OF_RANGE:
+        raise ValueError("destination values must be within the node range")
+    if not flags & _FLAG_UNSORTED:
+        return offsets, None
+    order, _, flags = _extension("group_by_key").group_by_key(dst, int(n_nodes))
+    if flags & _FLAG_OUT_OF_RANGE:  # pragma: no cover - checked above
+        raise ValueError("destination values must be within the node range")
+    return offsets, order
 
 
 def group_by_source(src: torch.Tensor, n_nodes: int) -> tuple[torch.Tensor, torch.Tensor]:

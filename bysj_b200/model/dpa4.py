@@ -12,7 +12,10 @@ import os
 from pathlib import Path
 from typing import Any
 
-_FUSED_SEAMS = ("softmax", "envelope")
+_FUSED_SEAMS = ("softmax", "envelope", "force")
+# ``fused=True`` keeps the reference's meaning (its two seams); the force
+# seam, which the reference lists as not yet wired, is opt-in by name.
+_DEFAULT_SEAMS = ("softmax", "envelope")
 _REMOVED_SELECTORS = (
     ("tilelang_ops", "drop the argument; TileLang dispatch was removed from this project"),
     ("native_ops", 'drop the argument and use fused=("softmax", "envelope") instead'),
@@ -24,7 +27,7 @@ def _normalize_fused(fused: Any) -> dict[str, bool] | None:
     if not fused:
         return None
     if fused is True:
-        return dict.fromkeys(_FUSED_SEAMS, True)
+        return dict.fromkeys(_DEFAULT_SEAMS, True)
     if isinstance(fused, str):
         fused = (fused,)
     if isinstance(fused, (list, tuple, set, frozenset)):
@@ -44,7 +47,10 @@ def _normalize_fused(fused: Any) -> dict[str, bool] | None:
                 f"unknown fused seams: {', '.join(sorted(map(str, unknown)))}; "
                 f"choose from: {', '.join(_FUSED_SEAMS)}"
             )
-        return {name: bool(fused.get(name, False)) for name in _FUSED_SEAMS}
+        chosen = {name: bool(fused.get(name, False)) for name in _DEFAULT_SEAMS}
+        if "force" in fused:
+            chosen["force"] = bool(fused["force"])
+        return chosen
     raise TypeError("fused must be a bool, a seam name, a sequence of names or a mapping")
 
 
@@ -68,8 +74,9 @@ def _backend_name(deep_pot: Any) -> str:
 class DPA4Model:
     """``DeepPot`` facade that can bind the fused segmented operators.
 
-    ``fused``: ``True`` installs every seam; a seam name or a sequence of
-    names (``"softmax"``, ``"envelope"``) selects some; a mapping sets each;
+    ``fused``: ``True`` installs the softmax and envelope seams; a seam name
+    or a sequence of names (``"softmax"``, ``"envelope"``, ``"force"``)
+    selects some; a mapping sets each;
     ``None`` / ``False`` leaves DeepMD untouched.  Remaining keyword
     arguments go to ``deepmd.infer.DeepPot``.
     """

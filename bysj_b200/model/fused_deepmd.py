@@ -11,13 +11,19 @@ per-call fallback to DeepMD's own implementation.
 ``SO2Convolution.forward_envelope`` (per block instance)
     replaced by one ``ops.segment_sum`` with ``edge_scale = env * src_gate``
     and ``node_scale = inv_sqrt_deg``.
+``edge_force_virial`` (module attribute, opt-in with ``force=True``)
+    the per-atom force / virial scatter of DeepMD's post-processing, which the
+    reference lists as not yet wired (``docs/deepmd-fused-dispatch.md:126``):
+    ``(g, edge_vec, src, dst, n_ext) -> (force, atom_virial)`` replaced by
+    ``ops.force_assembly`` with fp64 sums.
 
 A call falls back -- counted in ``FusedStats`` and warned about once -- when a
 precondition fails (training mode, a source-weighted softmax, non-contiguous
 or non-fp32 or non-CUDA tensors, shape mismatch) or when the fused operator
 raises.  The destination CSR view (offsets, stable order) is built on the
-device with the operator bundle's ``segment_offsets`` and kept in a small LRU
-keyed by the ``dst`` storage.
+device (``destination_csr``: boundary kernel for sorted input, histogram and
+stable device grouping otherwise) and kept in a small LRU keyed by the ``dst``
+storage and version.
 """
 from __future__ import annotations
 
@@ -34,6 +40,7 @@ _CSR_CAPACITY = 4
 # on a real install this guard keeps CPU tensors away from the CUDA kernels.
 _ACCEPT_ANY_DEVICE = False
 _SOFTMAX_NAME = "segment_envelope_gated_softmax"
+_FORCE_NAME = "edge_force_virial"
 _BLOCK_PREFIX = "block:"
 
 
@@ -45,8 +52,11 @@ class FusedStats:
     softmax_fallbacks: int = 0
     envelope_hits: int = 0
     envelope_fallbacks: int = 0
+    force_hits: int = 0
+    force_fallbacks: int = 0
     bound_softmax: bool = False
     bound_envelope: bool = False
+    bound_force: bool = False
     blocks: int = 0
     last_error: str | None = None
 
@@ -56,8 +66,11 @@ class FusedStats:
             "softmax_fallbacks": self.softmax_fallbacks,
             "envelope_hits": self.envelope_hits,
             "envelope_fallbacks": self.envelope_fallbacks,
+            "force_hits": self.force_hits,
+            "force_fallbacks": self.force_fallbacks,
             "bound_softmax": self.bound_softmax,
             "bound_envelope": self.bound_envelope,
+            "bound_force": self.bound_force,
             "blocks": self.blocks,
             "last_error": self.last_error,
         }
@@ -82,13 +95,25 @@ def _load_ops() -> Any:
 
 
 class _CsrView:
-    """Destination CSR view ``(offsets, order)`` cached by the dst storage."""
+    """Destination CSR view ``(offsets, order)`` cached by the dst storage.
 
-    def __init__(self, builder=None, capacity: int = _CSR_CAPACITY) -> None:
+    With an operator bundle that has ``destination_csr`` (the B200 kernels)
+    the view is built on the device: the boundary kernel for a
+    destination-sorted list (``order`` is then ``None`` and the operators read
+    the edges in place), the histogram + stable device grouping otherwise.
+    Bundles without it fall back to their ``segment_offsets`` plus
+    ``torch.argsort(dst, stable=True)`` as the reference does
+    (``python/model/fused_deepmd.py:111-124``).  The cache key includes the
+    tensor's version counter, so an in-place change of ``dst`` is not served
+    a stale view.
+    """
+
+    def __init__(self, builder=None, capacity: int = _CSR_CAPACITY, csr=None) -> None:
         self._builder = builder
+        self._csr = csr
         self._capacity = capacity
-        self._cache: dict[tuple[int, int, int], tuple[torch.Tensor, torch.Tensor]] = {}
-        self._lru: list[tuple[int, int, int]] = []
+        self._cache: dict[tuple[int, ...], tuple[torch.Tensor, torch.Tensor | None]] = {}
+        self._lru: list[tuple[int, ...]] = []
 
     def _offsets(self, dst: torch.Tensor, n_nodes: int) -> torch.Tensor:
         builder = self._builder
@@ -96,17 +121,60 @@ class _CsrView:
             from ..kernels.segment import segment_offsets as builder
         return builder(dst, n_nodes)
 
-    def get(self, dst: torch.Tensor, n_nodes: int) -> tuple[torch.Tensor, torch.Tensor]:
-        key = (int(dst.data_ptr()), int(dst.numel()), int(n_nodes))
+    def _build(self, dst: torch.Tensor, n_nodes: int):
+        if self._csr is not None:
+            return self._csr(dst, n_nodes)
+        return self._offsets(dst, n_nodes), torch.argsort(dst, stable=True)
+
+    def get(self, dst: torch.Tensor, n_nodes: int) -> tuple[torch.Tensor, torch.Tensor | None]:
+        key = (int(dst.data_ptr()), int(dst.numel()), int(n_nodes), int(dst._version))
         hit = self._cache.get(key)
         if hit is not None:
             return hit
-        view = (self._offsets(dst, n_nodes), torch.argsort(dst, stable=True))
+        view = self._build(dst, n_nodes)
         self._cache[key] = view
         self._lru.append(key)
         while len(self._lru) > self._capacity:
             self._cache.pop(self._lru.pop(0), None)
         return view
+
+
+class _ForcePlan:
+    """Destination-sorted copies of the index columns and the source grouping
+    of one edge list, cached by the ``src`` / ``dst`` storages and versions.
+
+    ``force_assembly`` walks destination segments in place, so an edge list
+    that is not grouped by destination is permuted once (``dst_order``); the
+    per-edge gradients are permuted with the same order on every call.
+    """
+
+    def __init__(self, csr: _CsrView, grouper=None, capacity: int = _CSR_CAPACITY) -> None:
+        self._csr = csr
+        self._grouper = grouper
+        self._capacity = capacity
+        self._cache: dict[tuple[int, ...], tuple] = {}
+        self._lru: list[tuple[int, ...]] = []
+
+    def get(self, src: torch.Tensor, dst: torch.Tensor, n_nodes: int):
+        key = (int(src.data_ptr()), int(src._version), int(dst.data_ptr()), int(dst._version),
+               int(dst.numel()), int(n_nodes))
+        hit = self._cache.get(key)
+        if hit is not None:
+            return hit
+        offsets, order = self._csr.get(dst, n_nodes)
+        src_sorted = src if order is None else src.index_select(0, order)
+        dst_sorted = dst if order is None else dst.index_select(0, order)
+        grouper = self._grouper
+        if grouper is None:
+            from ..kernels.segment import group_by_source as grouper
+        src_order, src_offsets = grouper(src_sorted.contiguous(), n_nodes)
+        plan = (offsets, order, src_sorted.contiguous(), dst_sorted.contiguous(), src_offsets,
+                src_order)
+        self._cache[key] = plan
+        self._lru.append(key)
+        while len(self._lru) > self._capacity:
+            self._cache.pop(self._lru.pop(0), None)
+        return plan
 
 
 @dataclass
@@ -116,6 +184,7 @@ class _Session:
     reference_softmax: Any
     csr: _CsrView = field(default_factory=_CsrView)
     warned: bool = False
+    force_plan: _ForcePlan | None = None
 
     # -- softmax seam ---------------------------------------------------------
     def softmax(self, logits, edge_env, dst, n_nodes, z_bias_raw, eps, src_weight=None):
@@ -219,6 +288,56 @@ class _Session:
         stats.envelope_hits += 1
         return out.reshape(x.shape)
 
+    # -- force seam -----------------------------------------------------------
+    def force(self, original, g, edge_vec, src, dst, n_ext):
+        """``(force [n_ext, 3], atom_virial [n_ext, 9])`` of an edge list.
+
+        ``g`` is dE/d(edge_vec) per edge with ``edge_vec = r_src - r_dst``, so
+        ``F_k = sum_{dst=k} g - sum_{src=k} g`` and the per-atom virial is
+        ``-sum_{src=k} g (x) edge_vec`` (row-major), the four ``index_add_``
+        scatters of DeepMD's post-processing step
+        (``docs/fused-operators.md:111-140`` of the reference).  Ghost atoms
+        are rows like any other: folding them onto their local images stays
+        with DeepMD.
+        """
+        stats = self.stats
+
+        def stock():
+            stats.force_fallbacks += 1
+            return original(g, edge_vec, src, dst, n_ext)
+
+        ready = (
+            _usable_tensor(g)
+            and _usable_tensor(edge_vec)
+            and g.ndim == 2
+            and g.shape[1] == 3
+            and g.shape[0] > 0
+            and tuple(edge_vec.shape) == tuple(g.shape)
+            and _usable_tensor(src, dtype=torch.int64)
+            and _usable_tensor(dst, dtype=torch.int64)
+            and tuple(src.shape) == (g.shape[0],)
+            and tuple(dst.shape) == (g.shape[0],)
+            and int(n_ext) > 0
+            and not g.requires_grad
+        )
+        if not ready:
+            return stock()
+        try:
+            if self.force_plan is None:
+                self.force_plan = _ForcePlan(self.csr, getattr(self.ops, "group_by_source", None))
+            offsets, order, src_s, dst_s, src_offsets, src_order = self.force_plan.get(
+                src, dst, int(n_ext))
+            if order is not None:
+                g = g.index_select(0, order)
+                edge_vec = edge_vec.index_select(0, order)
+            force, virial = self.ops.force_assembly(g, edge_vec, src_s, dst_s, offsets,
+                                                    src_offsets, src_order)
+        except Exception as error:  # noqa: BLE001 - fall back, never break inference
+            self._record(error)
+            return stock()
+        stats.force_hits += 1
+        return force, virial
+
     def _record(self, error: Exception) -> None:
         self.stats.last_error = f"{type(error).__name__}: {error}"
         if not self.warned:
@@ -248,6 +367,15 @@ def _softmax_namespaces() -> list[Any]:
         return found
     found.append(package)
     return found
+
+
+def _force_namespaces() -> list[Any]:
+    """DeepMD modules whose ``edge_force_virial`` is rebound (none if absent)."""
+    try:
+        import deepmd.pt.model.model.transform_output as transform_output
+    except ImportError:
+        return []
+    return [transform_output]
 
 
 def _blocks(model: Any) -> list[Any]:
@@ -318,14 +446,18 @@ def _say(verbose: bool, text: str) -> None:
 
 def deepmd_patch(module: Any, *, ops: Any = None, softmax: bool = True, envelope: bool = True,
                  blocks: Iterable[Any] | None = None, namespaces: Iterable[Any] | None = None,
-                 verbose: bool = True) -> FusedStats:
+                 verbose: bool = True, force: bool = False,
+                 force_namespaces: Iterable[Any] | None = None) -> FusedStats:
     """Bind the fused operators on ``module`` (a ``DeepPot`` or an ``nn.Module``).
 
     ``ops`` is an operator bundle with ``segment_softmax`` and ``segment_sum``
-    (and optionally ``segment_offsets`` for the CSR view); it defaults to
-    :mod:`bysj_b200.kernels`, and the install is a logged no-op when the
-    extension cannot run on this host.  ``namespaces`` overrides the DeepMD
-    modules that carry the softmax name.  Installing twice keeps one patch.
+    (and optionally ``segment_offsets`` / ``destination_csr`` for the CSR
+    view, ``force_assembly`` and ``group_by_source`` for the force seam); it
+    defaults to :mod:`bysj_b200.kernels`, and the install is a logged no-op
+    when the extension cannot run on this host.  ``namespaces`` overrides the
+    DeepMD modules that carry the softmax name, ``force_namespaces`` those
+    that carry ``edge_force_virial`` (the third seam, off unless ``force``).
+    Installing twice keeps one patch.
     """
     global _SESSION
     stats = FusedStats()
@@ -358,7 +490,7 @@ def deepmd_patch(module: Any, *, ops: Any = None, softmax: bool = True, envelope
         reference = getattr(spaces[0], _SOFTMAX_NAME)
     builder = getattr(ops, "segment_offsets", None)
     _SESSION = _Session(ops=ops, stats=stats, reference_softmax=reference,
-                        csr=_CsrView(builder))
+                        csr=_CsrView(builder, csr=getattr(ops, "destination_csr", None)))
 
     if softmax:
         def bound_softmax(logits, edge_env, dst, n_nodes, z_bias_raw, eps, src_weight=None):
@@ -392,8 +524,29 @@ def deepmd_patch(module: Any, *, ops: Any = None, softmax: bool = True, envelope
         stats.bound_envelope = bool(targets)
         _say(verbose, f"replace SO2Convolution.forward_envelope on {len(targets)} block(s) -> "
                       "bysj_b200.model.fused_deepmd.patched")
+    if force:
+        force_spaces = (list(force_namespaces) if force_namespaces is not None
+                        else _force_namespaces())
+        for space in force_spaces:
+            if not hasattr(space, _FORCE_NAME):
+                _say(verbose, f"{getattr(space, '__name__', space)} has no {_FORCE_NAME}: "
+                              "force seam not bound there")
+                continue
+            stock_force = getattr(space, _FORCE_NAME)
+            _SAVED[f"{space.__name__}.{_FORCE_NAME}"] = (space, stock_force)
+
+            def bound_force(g, edge_vec, src, dst, n_ext, _stock=stock_force):
+                session = _SESSION
+                if session is None:
+                    return _stock(g, edge_vec, src, dst, n_ext)
+                return session.force(_stock, g, edge_vec, src, dst, n_ext)
+
+            setattr(space, _FORCE_NAME, bound_force)
+            stats.bound_force = True
+            _say(verbose, f"replace {space.__name__}.{_FORCE_NAME} -> "
+                          "bysj_b200.model.fused_deepmd.bound_force")
     _say(verbose, f"installed: softmax={stats.bound_softmax} envelope={stats.bound_envelope} "
-                  f"blocks={stats.blocks}")
+                  f"force={stats.bound_force} blocks={stats.blocks}")
     return stats
 
 

@@ -12,6 +12,7 @@ from .gie import gie_zonal_scatter_reference, zonal_scatter_reference
 from .rmsnorm import rmsnorm, rmsnorm_per_degree
 from .segment import (
     force_assembly_reference,
+    rotate_back_aggregate_reference,
     segment_attention_reference,
     segment_softmax_reference,
     segment_sum_reference,
@@ -22,6 +23,7 @@ __all__ = [
     "gie_zonal_scatter_reference",
     "rmsnorm",
     "rmsnorm_per_degree",
+    "rotate_back_aggregate_reference",
     "segment_attention_reference",
     "segment_softmax_reference",
     "segment_sum_reference",

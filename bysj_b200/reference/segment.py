@@ -162,8 +162,58 @@ def force_assembly_reference(grad_edge, edge_vec, src, dst, dst_offsets, src_off
     return force, virial
 
 
+def _rotation_offsets(lmax: int) -> list[int]:
+    offs, acc = [], 0
+    for l in range(lmax + 1):
+        offs.append(acc)
+        acc += (2 * l + 1) ** 2
+    return offs + [acc]
+
+
+def rotate_back_aggregate_reference(x_local, rotation, rotate_inv_rescale, attn_alpha, order,
+                                    row_ptr, dst, lmax, heads):
+    """Rotate-back + attention weighting + destination sum (the flash seam).
+
+    The argument list is the one the reference records for DeepMD's
+    ``SO2Convolution._flash_atten_fn`` (``docs/deepmd-fused-dispatch.md:127``):
+    ``x_local`` [E, (lmax+1)^2, C] edge messages in each edge's local frame,
+    ``rotation`` [E, sum_l (2l+1)^2] the block-diagonal rotation packed per
+    degree (block l row-major, ``x_local = D x_global``), ``rotate_inv_rescale``
+    [E] or None a per-edge factor applied with the inverse rotation,
+    ``attn_alpha`` [E, heads] the attention weights, ``order`` / ``row_ptr``
+    the destination CSR view (``order`` may be None), ``dst`` [E]:
+
+    ``out[n, l*l + b, c] = sum_{dst(e)=n} alpha[e, c // dh] * rescale[e] *
+    sum_a D_{e,l}[a, b] * x_local[e, l*l + a, c]``, ``dh = C / heads``.
+    """
+    if x_local.dtype != torch.float32 or x_local.ndim != 3:
+        raise ValueError("rotate-back x_local must be float32 (n_edges, (lmax+1)^2, channels)")
+    n_edges, comps, channels = x_local.shape
+    if comps != (lmax + 1) ** 2:
+        raise ValueError("rotate-back x_local must have (lmax+1)^2 components")
+    offs = _rotation_offsets(lmax)
+    if rotation.dtype != torch.float32 or tuple(rotation.shape) != (n_edges, offs[-1]):
+        raise ValueError("rotate-back rotation must be float32 (n_edges, sum_l (2l+1)^2)")
+    if heads <= 0 or channels % heads:
+        raise ValueError("rotate-back heads must divide the channels")
+    if attn_alpha.dtype != torch.float32 or tuple(attn_alpha.shape) != (n_edges, heads):
+        raise ValueError("rotate-back attn_alpha must be float32 (n_edges, heads)")
+    nodes = _n_segments(row_ptr)
+    _grouping(dst, row_ptr, n_edges, "rotate-back")
+    y = torch.empty_like(x_local)
+    for l in range(lmax + 1):
+        m = 2 * l + 1
+        blk = rotation[:, offs[l]:offs[l + 1]].reshape(n_edges, m, m)
+        y[:, l * l:(l + 1) ** 2, :] = torch.bmm(blk.transpose(1, 2), x_local[:, l * l:(l + 1) ** 2, :])
+    weight = attn_alpha.repeat_interleave(channels // heads, dim=1).unsqueeze(1)
+    if rotate_inv_rescale is not None:
+        weight = weight * rotate_inv_rescale.reshape(n_edges, 1, 1)
+    return _accumulate(nodes, dst, y * weight)
+
+
 __all__ = [
     "force_assembly_reference",
+    "rotate_back_aggregate_reference",
     "segment_attention_reference",
     "segment_softmax_reference",
     "segment_sum_reference",

@@ -226,6 +226,33 @@ BYSJ_API int bysj_segment_attention_forward_noalloc(
     int64_t channels, float* out, void* stream);
 
 /* ------------------------------------------------------------------------
+ * rotate-back aggregation (the flash aggregation seam of DeepMD's SO(2)
+ * block).  No single counterpart in the reference's kernels: the reference
+ * records the seam SO2Convolution._flash_atten_fn(x_local, rotation,
+ * rotate_inv_rescale, attn_alpha, order, row_ptr, dst, lmax, heads) as not yet
+ * wired (docs/deepmd-fused-dispatch.md:127-128); its eager form is a rotate,
+ * a weighting and an index_add_.  With the edges grouped by destination
+ * (offsets / order as above):
+ *   out[n, l*l + b, c] = sum_{e in n} alpha[e, c / dh] * rescale[e] *
+ *                        sum_a D_{e,l}[a, b] * x_local[e, l*l + a, c]
+ * x_local [n_edges, (lmax+1)^2, channels]; rotation [n_edges, sum_l (2l+1)^2]
+ * packs each edge's block-diagonal rotation per degree (block l row-major,
+ * x_local = D x_global, so this is the transpose); rescale [n_edges] may be
+ * NULL (1); alpha [n_edges, heads]; out float32 [n_nodes, (lmax+1)^2,
+ * channels]; dh = channels / heads; 0 <= lmax <= 3.  Deterministic.
+ * ------------------------------------------------------------------------ */
+BYSJ_API size_t bysj_rotate_back_aggregate_workspace_size(int64_t n_edges, int64_t n_nodes,
+                                                          int64_t lmax, int64_t heads,
+                                                          int64_t channels);
+BYSJ_API int bysj_rotate_back_aggregate(const float* x_local, const float* rotation,
+                                        const float* rescale, const float* alpha,
+                                        const int64_t* offsets, const int64_t* order,
+                                        int64_t n_edges, int64_t n_nodes, int64_t lmax,
+                                        int64_t heads, int64_t channels, float* out,
+                                        void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
+/* ------------------------------------------------------------------------
  * force_assembly
  * Replaces csrc/force_assembly.cpp:106-146.
  *   force[k]  = sum_{dst(e)=k} g_e - sum_{src(e)=k} g_e        (fp64 accumulate)

@@ -80,4 +80,26 @@ def zonal_scatter(zonal, radial, dst, radial_slot, inv):
     return out
 
 
-__all__ = ["force_assembly", "segment_softmax", "segment_sum", "zonal_scatter"]
+def rotate_back_aggregate(x_local, rotation, rescale, alpha, dst, nodes, lmax, heads):
+    """Loop form of the fused rotate-back aggregation (tiny inputs only)."""
+    comps = (lmax + 1) ** 2
+    channels = len(x_local[0][0]) if x_local else 0
+    dh = channels // heads
+    out = [[[0.0] * channels for _ in range(comps)] for _ in range(nodes)]
+    for e in range(len(x_local)):
+        off = 0
+        s = 1.0 if rescale is None else rescale[e]
+        for l in range(lmax + 1):
+            m = 2 * l + 1
+            for b in range(m):
+                for c in range(channels):
+                    acc = 0.0
+                    for a in range(m):
+                        acc += rotation[e][off + a * m + b] * x_local[e][l * l + a][c]
+                    out[dst[e]][l * l + b][c] += alpha[e][c // dh] * s * acc
+            off += m * m
+    return out
+
+
+__all__ = ["force_assembly", "rotate_back_aggregate", "segment_softmax", "segment_sum",
+           "zonal_scatter"]

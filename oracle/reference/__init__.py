@@ -17,6 +17,7 @@ from bysj_b200.reference import (
     gie_zonal_scatter_reference,
     rmsnorm,
     rmsnorm_per_degree,
+    rotate_back_aggregate_reference,
     segment_attention_reference,
     segment_softmax_reference,
     segment_sum_reference,
@@ -28,6 +29,7 @@ __all__ = [
     "gie_zonal_scatter_reference",
     "rmsnorm",
     "rmsnorm_per_degree",
+    "rotate_back_aggregate_reference",
     "segment_attention_reference",
     "segment_softmax_reference",
     "segment_sum_reference",

@@ -133,8 +133,43 @@ def zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg) -> np.ndarray:
     return out * inv[:, None, None]
 
 
+def rotation_block_offsets(lmax: int) -> list[int]:
+    """Start of each degree's block in a packed rotation row: sum_{l'<l} (2l'+1)^2."""
+    offs, acc = [], 0
+    for l in range(lmax + 1):
+        offs.append(acc)
+        acc += (2 * l + 1) ** 2
+    return offs + [acc]
+
+
+def rotate_back_aggregate(x_local, rotation, rescale, alpha, dst, n_nodes, lmax, heads):
+    """float64 truth of the fused rotate-back aggregation.
+
+    ``out[n, l*l + b, c] = sum_{dst(e)=n} alpha[e, c // dh] * rescale[e] *
+    sum_a D_{e,l}[a, b] * x_local[e, l*l + a, c]`` with ``D_{e,l}`` the
+    degree-l block of edge e's packed rotation (row-major, ``x_local = D
+    x_global`` per block, so the rotate-back is the transpose)."""
+    x = np.asarray(x_local, dtype=np.float64)
+    rot = np.asarray(rotation, dtype=np.float64)
+    a = np.asarray(alpha, dtype=np.float64)
+    e, comps, channels = x.shape
+    dh = channels // heads
+    offs = rotation_block_offsets(lmax)
+    y = np.zeros_like(x)
+    for l in range(lmax + 1):
+        m = 2 * l + 1
+        blk = rot[:, offs[l]:offs[l + 1]].reshape(e, m, m)
+        y[:, l * l:(l + 1) ** 2, :] = np.einsum("eab,eac->ebc", blk, x[:, l * l:(l + 1) ** 2, :])
+    w = np.repeat(a, dh, axis=1)[:, None, :]
+    if rescale is not None:
+        w = w * np.asarray(rescale, dtype=np.float64).reshape(e, 1, 1)
+    return _rows(n_nodes, np.asarray(dst), y * w)
+
+
 __all__ = [
     "dst_from_offsets",
+    "rotate_back_aggregate",
+    "rotation_block_offsets",
     "force_assembly",
     "gated_logit",
     "group_by_source",

@@ -36,6 +36,8 @@ def grouped(counts):
 def dst_from_csr(offsets, order):
     counts = (offsets[1:] - offsets[:-1]).tolist()
     grouped_ids = torch.repeat_interleave(torch.arange(offsets.numel() - 1), torch.tensor(counts))
+    if order is None:
+        return grouped_ids
     dst = torch.empty_like(grouped_ids)
     dst[order] = grouped_ids
     return dst
@@ -58,6 +60,29 @@ class FakeOps:
         self.calls.append(("sum", tuple(src.shape)))
         return segment_sum_reference(src, dst_from_csr(offsets, order), offsets, edge_scale,
                                      node_scale)
+
+    def group_by_source(self, src, n_nodes):
+        order, offsets = truth.group_by_source(src.numpy(), n_nodes)
+        return torch.from_numpy(order), torch.from_numpy(offsets)
+
+    def force_assembly(self, grad_edge, edge_vec, src, dst, dst_offsets, src_offsets=None,
+                       src_order=None):
+        self.calls.append(("force", tuple(grad_edge.shape)))
+        # the device kernel walks destination segments in place: dst must be grouped
+        assert torch.equal(dst_from_csr(dst_offsets, None), dst)
+        f, w = truth.force_assembly(grad_edge.numpy(), edge_vec.numpy(), src.numpy(),
+                                    dst.numpy(), dst_offsets.numel() - 1)
+        return torch.from_numpy(f).float(), torch.from_numpy(w).float()
+
+
+class DeviceCsrOps(FakeOps):
+    """A bundle with the device CSR view: ``order`` is None for sorted dst."""
+
+    def destination_csr(self, dst, n_nodes):
+        self.calls.append(("csr", int(dst.numel())))
+        offsets = self.segment_offsets(dst, n_nodes)
+        sorted_ = bool((dst[1:] >= dst[:-1]).all()) if dst.numel() > 1 else True
+        return offsets, None if sorted_ else torch.argsort(dst, stable=True)
 
 
 class FakeEdgeCache:
@@ -280,6 +305,9 @@ def test_module_dump_and_verbose_install():
 
 def test_fused_switch_parsing():
     assert _normalize_fused(True) == {"softmax": True, "envelope": True}
+    assert _normalize_fused("force") == {"force": True}
+    assert _normalize_fused({"force": True}) == {"softmax": False, "envelope": False,
+                                                 "force": True}
     assert _normalize_fused("softmax") == {"softmax": True}
     assert _normalize_fused(("envelope",)) == {"envelope": True}
     assert _normalize_fused({"softmax": True, "envelope": False}) == {"softmax": True,
@@ -291,3 +319,110 @@ def test_fused_switch_parsing():
         _normalize_fused(3)
     assert _normalize_fused(False) is None and _normalize_fused(None) is None
     assert _normalize_fused(()) is None
+
+
+# ---- force seam --------------------------------------------------------------------------
+
+def fake_transform_output(name="fake.transform_output"):
+    """Stand-in for DeepMD's post-processing namespace: ``edge_force_virial``
+    as four ``index_add_`` scatters in fp32, the stock path the seam replaces."""
+    module = types.ModuleType(name)
+
+    def edge_force_virial(g, edge_vec, src, dst, n_ext):
+        force = g.new_zeros(n_ext, 3)
+        force.index_add_(0, dst, g)
+        force.index_add_(0, src, -g)
+        virial = g.new_zeros(n_ext, 9)
+        virial.index_add_(0, src, -(g[:, :, None] * edge_vec[:, None, :]).reshape(-1, 9))
+        return force, virial
+
+    module.edge_force_virial = edge_force_virial
+    return module
+
+
+def toy_system(n=12, seed=0, shuffle=False):
+    """Random positions, all directed pairs within 2.5, and a pair energy
+    E = sum_e exp(-|v_e|^2) with v_e = r_src - r_dst."""
+    gen = torch.Generator().manual_seed(seed)
+    pos = (torch.rand(n, 3, generator=gen, dtype=torch.float64) * 4.0).requires_grad_(True)
+    d = (pos[None, :, :] - pos[:, None, :]).detach()
+    close = (d.norm(dim=-1) < 2.5) & ~torch.eye(n, dtype=torch.bool)
+    dst, src = close.nonzero(as_tuple=True)
+    if shuffle:
+        perm = torch.randperm(dst.numel(), generator=gen)
+        dst, src = dst[perm], src[perm]
+    vec = pos[src] - pos[dst]
+    energy = torch.exp(-(vec * vec).sum(-1)).sum()
+    g, = torch.autograd.grad(energy, vec, retain_graph=True)
+    forces, = torch.autograd.grad(energy, pos)
+    return (g.float().contiguous(), vec.detach().float().contiguous(), src.contiguous(),
+            dst.contiguous(), n, -forces)
+
+
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_force_seam_matches_stock_and_minus_the_energy_gradient(shuffle):
+    ns = fake_transform_output()
+    ops = DeviceCsrOps()
+    stats = fused_deepmd.deepmd_patch(FakeModel([]), ops=ops, softmax=False, envelope=False,
+                                      force=True, force_namespaces=[ns], verbose=False)
+    assert stats.bound_force
+    g, vec, src, dst, n, want_force = toy_system(shuffle=shuffle)
+    force, virial = ns.edge_force_virial(g, vec, src, dst, n)
+    assert stats.force_hits == 1 and ("force", tuple(g.shape)) in ops.calls
+    # sign: the assembled forces are minus the gradient of the energy
+    torch.testing.assert_close(force.double(), want_force, rtol=1e-5, atol=1e-6)
+    # momentum is conserved and the atom virials sum to -sum_e g (x) v
+    torch.testing.assert_close(force.double().sum(0), torch.zeros(3, dtype=torch.float64),
+                               rtol=0, atol=1e-5)
+    total = -(g.double()[:, :, None] * vec.double()[:, None, :]).reshape(-1, 9).sum(0)
+    torch.testing.assert_close(virial.double().sum(0), total, rtol=1e-5, atol=1e-6)
+    # same as the stock scatters and as the loop oracle
+    fused_deepmd.uninstall()
+    stock_force, stock_virial = ns.edge_force_virial(g, vec, src, dst, n)
+    torch.testing.assert_close(force, stock_force, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(virial, stock_virial, rtol=1e-5, atol=1e-6)
+    from oracle import loops
+
+    lf, lw = loops.force_assembly(g.tolist(), vec.tolist(), src.tolist(), dst.tolist(), n)
+    np.testing.assert_allclose(force.numpy(), np.asarray(lf), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(virial.numpy(), np.asarray(lw), rtol=1e-5, atol=1e-6)
+
+
+def test_force_seam_falls_back_and_restores():
+    ns = fake_transform_output()
+    stock = ns.edge_force_virial
+    stats = fused_deepmd.deepmd_patch(FakeModel([]), ops=DeviceCsrOps(), softmax=False,
+                                      envelope=False, force=True, force_namespaces=[ns],
+                                      verbose=False)
+    g, vec, src, dst, n, _ = toy_system(seed=3)
+    ns.edge_force_virial(g.double(), vec, src, dst, n)          # not fp32
+    ns.edge_force_virial(g.requires_grad_(True), vec, src, dst, n)  # in the autograd graph
+    assert stats.force_fallbacks == 2 and stats.force_hits == 0
+    fused_deepmd.uninstall()
+    assert ns.edge_force_virial is stock
+    # a namespace without the name binds nothing
+    stats = fused_deepmd.deepmd_patch(FakeModel([]), ops=DeviceCsrOps(), softmax=False,
+                                      envelope=False, force=True,
+                                      force_namespaces=[types.ModuleType("fake.empty")],
+                                      verbose=False)
+    assert not stats.bound_force
+
+
+def test_device_csr_view_keeps_sorted_edges_in_place():
+    ns = fake_namespace("fake.attention")
+    ops = DeviceCsrOps()
+    stats = fused_deepmd.deepmd_patch(FakeModel([]), ops=ops, namespaces=[ns], envelope=False,
+                                      verbose=False)
+    dst, _ = grouped([2, 0, 3])
+    logits, env, bias = torch.randn(5, 2, 3), torch.rand(5, 1) + 0.1, torch.randn(2, 3)
+    ns.segment_envelope_gated_softmax(logits, env, dst, 3, bias, 1e-6)
+    assert ("csr", 5) in ops.calls and stats.softmax_hits == 1
+    view = fused_deepmd._CsrView(csr=ops.destination_csr)
+    assert view.get(dst, 3)[1] is None
+    shuffled = dst[torch.tensor([4, 0, 3, 1, 2])]
+    offsets, order = view.get(shuffled, 3)
+    assert torch.equal(shuffled[order], dst)
+    # an in-place change of dst is not served the cached view
+    before = view.get(shuffled, 3)
+    shuffled[0] = 2
+    assert view.get(shuffled, 3) is not before
