@@ -103,17 +103,15 @@ class Dist:
 
     def setup(self, backend: str):
         if self.world > 1:
-            import datetime
-
-            import torch.distributed as dist
+            from bysj_b200 import sharding as S
 
             kwargs = {}
             if backend == "nccl":
                 device = torch.device("cuda", self.local)
                 torch.cuda.set_device(device)
                 kwargs["device_id"] = device
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kwargs)
-            self.pg = dist
+            # bounded: a rank that dies makes the others' next collective raise
+            self.pg = S.init_process_group(backend, timeout_s=120.0, **kwargs)
 
     def barrier(self):
         if self.pg is not None:

@@ -35,6 +35,29 @@ from typing import Callable
 import torch
 
 
+def init_process_group(backend: str = "nccl", *, timeout_s: float = 60.0, **kwargs):
+    """``torch.distributed.init_process_group`` with a bounded timeout.
+
+    Every collective of the partition (the force reduce-scatter) then ends
+    within ``timeout_s`` seconds: with a peer that died or left between steps
+    it raises on the host instead of waiting forever.  For NCCL the
+    asynchronous error handling is switched on (``TORCH_NCCL_ASYNC_ERROR_HANDLING=1``
+    unless the caller set it), so a timed-out or failed communicator aborts
+    and the waiting ``work.wait()`` raises.  No kernel of this library waits on
+    another rank: only NCCL's own kernels do, and their wait is bounded here.
+    """
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    if backend == "nccl":
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=float(timeout_s)),
+                            **kwargs)
+    return dist
+
+
 def frame_share(frames: int, rank: int, world: int) -> list[int]:
     """Frames handled by ``rank``: ``rank, rank + world, ...``."""
     if world <= 0 or not 0 <= rank < world:
@@ -245,6 +268,7 @@ __all__ = [
     "edge_balanced_bounds",
     "force_assembly_partitioned",
     "frame_share",
+    "init_process_group",
     "make_partition",
     "padded_offsets",
     "reduce_scatter_sum",

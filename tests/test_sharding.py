@@ -185,3 +185,48 @@ def test_single_partition_needs_no_process_group():
                                   g.dst.numpy(), g.n_atoms)
     np.testing.assert_allclose(f.numpy(), tf, rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(v.numpy(), tv, rtol=1e-5, atol=1e-5)
+
+
+def _leaving_worker(rank, world, port, out_dir, how):
+    # Both ranks run one partitioned step; rank 1 then leaves between steps
+    # (``exit``: its process ends, nothing of it in flight; ``stall``: it stays
+    # alive but never joins the next step) and rank 0 tries a second step,
+    # which must end with an error within the group's 5 s timeout.
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    S.init_process_group("gloo", timeout_s=5.0, rank=rank, world_size=world)
+    g = W.c1_box()
+    off = offsets_of(g.dst, g.n_atoms)
+    grad = torch.randn(g.n_edges, 3, generator=torch.Generator().manual_seed(2))
+    part = S.make_partition(off, g.src, rank, world, group_by_source=cpu_group_by_source)
+
+    def step():
+        return S.force_assembly_partitioned(part.edges(grad), part.edges(g.edge_vec), part,
+                                            src_partial=cpu_src_partial, dst_add=cpu_dst_add)
+
+    step()
+    if rank == 1:
+        if how == "stall":
+            time.sleep(12.0)
+        os._exit(0)  # leaves between steps without a goodbye
+    t0 = time.monotonic()
+    outcome = {"raised": False}
+    try:
+        step()
+    except Exception as error:  # noqa: BLE001 - the test records whatever surfaced
+        outcome = {"raised": True, "type": type(error).__name__, "message": str(error)[:200]}
+    outcome["seconds"] = time.monotonic() - t0
+    torch.save(outcome, os.path.join(out_dir, "rank0.pt"))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("how", ["exit", "stall"])
+def test_rank_leaving_between_steps_gives_a_clean_error(tmp_path, how):
+    mp.start_processes(_leaving_worker, args=(2, _free_port(), str(tmp_path), how), nprocs=2,
+                       join=True, start_method="spawn")
+    outcome = torch.load(tmp_path / "rank0.pt")
+    assert outcome["raised"], outcome
+    assert outcome["seconds"] < 11.0, outcome
+    print("rank 0 after its peer left:", outcome)
