@@ -578,6 +578,27 @@ def _op_rotate(ctx):
                             "sum in one pass; inputs larger than L2"})
 
 
+def _op_chain(ctx):
+    """One-pass edge-stream chain x + y * gate + residual over [E, 9, 64] fp32
+    (the gate [E, 1, 64] broadcast over the components) on the C3 edge
+    count, beside the same chain as eager torch passes."""
+    from bysj_b200 import kernels as K
+
+    e = ctx["g"].n_edges
+    device = ctx["device"]
+    gen = torch.Generator(device=device).manual_seed(95)
+    x, y, res = (torch.randn(e, 9, 64, device=device, generator=gen) for _ in range(3))
+    gate = torch.randn(e, 1, 64, device=device, generator=gen)
+    terms = [(1.0, x), (1.0, y, gate), (1.0, res)]
+    t = time_launches(lambda: K.edge_chain(terms, (e, 9, 64)), ctx["iters"])
+    t_eager = time_launches(lambda: x + y * gate + res, ctx["iters"])
+    row = 9 * 64 * 4
+    return op_line("edge_chain", e * (4 * row + 64 * 4), t, ctx["peak"], e,
+                   {"eager_us": t_eager * 1e6,
+                    "note": "3 terms (2 full streams + gated stream), 1 output, one pass; "
+                            "eager_us = torch x + y * gate + res (3 passes)"})
+
+
 def _op_small_step_graph(ctx):
     """A launch-bound step on the 192-atom C1 box, eager and as a CUDA-graph replay."""
     from bysj_b200 import _C
@@ -642,6 +663,7 @@ OPS = {
     "rmsnorm_bwd": _op_rmsnorm_bwd,
     "zonal_bwd": _op_zonal_bwd,
     "rotate": _op_rotate,
+    "chain": _op_chain,
 }
 
 

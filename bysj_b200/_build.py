@@ -54,6 +54,7 @@ CU_SOURCES = [
     "rmsnorm.cu",
     "gie.cu",
     "rotate_aggregate.cu",
+    "edge_chain.cu",
 ]
 HEADERS = ["common.cuh", "launch.cuh"]
 

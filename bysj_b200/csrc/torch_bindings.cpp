@@ -384,6 +384,50 @@ Tensor rotate_back_aggregate_forward(Tensor x_local, Tensor rotation, OptTensor 
   return out;
 }
 
+// ---- edge-stream elementwise chain ----------------------------------------------
+
+bysj_chain_operand chain_operand(const Tensor& t, int64_t e, int64_t s, int64_t c) {
+  // A broadcast view of the factor over [E, S, C]: stride 0 on broadcast axes.
+  Tensor v = t.expand({e, s, c});
+  bysj_chain_operand op{};
+  op.data = v.data_ptr<float>();
+  for (int i = 0; i < 3; ++i) op.stride[i] = v.size(i) == 1 ? 0 : v.stride(i);
+  return op;
+}
+
+Tensor edge_chain(std::vector<Tensor> first, std::vector<OptTensor> second,
+                  std::vector<double> coefs, int64_t n_edges, int64_t comps, int64_t channels,
+                  int64_t activation) {
+  const size_t n = first.size();
+  TORCH_CHECK(n >= 1 && n <= BYSJ_CHAIN_MAX_TERMS && second.size() == n && coefs.size() == n,
+              "edge chain: 1 to ", BYSJ_CHAIN_MAX_TERMS, " terms with matching lists");
+  // Factors are strided views (any strides, broadcasts included): float32
+  // on one CUDA device, no contiguity required.
+  auto factor = [&](const Tensor& f) {
+    TORCH_CHECK(f.is_cuda(), "edge chain factor must be a CUDA tensor");
+    TORCH_CHECK(f.scalar_type() == torch::kFloat32, "edge chain factor must be float32");
+    TORCH_CHECK(f.device() == first[0].device(), "edge chain factors must share a device");
+  };
+  for (size_t t = 0; t < n; ++t) {
+    factor(first[t]);
+    if (second[t]) factor(*second[t]);
+  }
+  c10::cuda::CUDAGuard guard(first[0].device());
+  Tensor out = torch::empty({n_edges, comps, channels}, first[0].options());
+  if (n_edges == 0) return out;
+  std::vector<bysj_chain_term> terms(n);
+  for (size_t t = 0; t < n; ++t) {
+    terms[t].coef = static_cast<float>(coefs[t]);
+    terms[t].a = chain_operand(first[t], n_edges, comps, channels);
+    if (second[t]) terms[t].b = chain_operand(*second[t], n_edges, comps, channels);
+  }
+  check(bysj_edge_chain(terms.data(), static_cast<int>(n), n_edges, comps, channels,
+                        static_cast<int>(activation), out.data_ptr<float>(),
+                        stream_of(first[0])),
+        "edge_chain");
+  return out;
+}
+
 // ---- force_assembly ---------------------------------------------------------
 
 std::tuple<Tensor, Tensor> force_assembly(Tensor grad_edge, Tensor edge_vec, Tensor dst_offsets,
@@ -619,6 +663,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("segment_attention_forward", &segment_attention_forward, py::arg("logit"),
         py::arg("value"), py::arg("offsets"), py::arg("env") = py::none(),
         py::arg("null_logit") = py::none(), py::arg("order") = py::none());
+  m.def("edge_chain", &edge_chain, py::arg("first"), py::arg("second"), py::arg("coefs"),
+        py::arg("n_edges"), py::arg("comps"), py::arg("channels"), py::arg("activation"));
   m.def("rotate_back_aggregate_forward", &rotate_back_aggregate_forward, py::arg("x_local"),
         py::arg("rotation"), py::arg("rotate_inv_rescale"), py::arg("attn_alpha"),
         py::arg("row_ptr"), py::arg("order"), py::arg("lmax"), py::arg("heads"));

@@ -1,12 +1,14 @@
 """B200 (sm_100a) native operators with the reference's ``kernels`` API.
 
 Same public names as the reference's ``python/kernels/__init__.py:14-26``,
-plus ``segment_attention`` (the fused softmax + weighted sum) and
+plus ``segment_attention`` (the fused softmax + weighted sum),
 ``rotate_back_aggregate`` (the fused rotate-back aggregation of the flash
-seam).
+seam) and ``edge_chain`` (an elementwise chain over the edge stream in one
+pass).
 """
 
 from .attention import segment_attention
+from .chain import edge_chain
 from .gie import gie_available, gie_zonal_scatter, zonal_scatter
 from .rmsnorm import rmsnorm, rmsnorm_available
 from .rotate import rotate_back_aggregate
@@ -21,6 +23,7 @@ from .segment import (
 )
 
 __all__ = [
+    "edge_chain",
     "force_assembly",
     "gie_available",
     "gie_zonal_scatter",

@@ -253,6 +253,36 @@ BYSJ_API int bysj_rotate_back_aggregate(const float* x_local, const float* rotat
                                         void* stream);
 
 /* ------------------------------------------------------------------------
+ * Edge-stream elementwise chain in one pass.  No counterpart in the
+ * reference's kernels: the reference plans it for the elementwise pool of its
+ * DeepMD profile (docs/task2-hip-fusion-plan.md:280-302: "a descriptor-driven
+ * kernel that reads k inputs once and sums a term table of pointer + strides
+ * + coefficient + broadcast axes into one output, with an optional
+ * activation"), where each term is a separate ATen pass today.
+ *   out[e, s, c] = act( sum_t coef_t * a_t[e, s, c] * b_t[e, s, c] )
+ * out is a contiguous float32 [n_edges, comps, channels]; each factor is a
+ * float32 strided view: element (e, s, c) is data[e*stride[0] + s*stride[1]
+ * + c*stride[2]], a stride of 0 broadcasts along that axis; b.data == NULL
+ * means the term has one factor.  Terms are summed in table order with fused
+ * multiply-adds (deterministic).  act: BYSJ_ACT_NONE, _SILU (z sigmoid(z)) or
+ * _SIGMOID.
+ * ------------------------------------------------------------------------ */
+#define BYSJ_CHAIN_MAX_TERMS 8
+enum { BYSJ_ACT_NONE = 0, BYSJ_ACT_SILU = 1, BYSJ_ACT_SIGMOID = 2 };
+typedef struct bysj_chain_operand {
+  const float* data;
+  int64_t stride[3];
+} bysj_chain_operand;
+typedef struct bysj_chain_term {
+  float coef;
+  bysj_chain_operand a;
+  bysj_chain_operand b;
+} bysj_chain_term;
+BYSJ_API int bysj_edge_chain(const bysj_chain_term* terms, int n_terms, int64_t n_edges,
+                             int64_t comps, int64_t channels, int activation, float* out,
+                             void* stream);
+
+/* ------------------------------------------------------------------------
  * force_assembly
  * Replaces csrc/force_assembly.cpp:106-146.
  *   force[k]  = sum_{dst(e)=k} g_e - sum_{src(e)=k} g_e        (fp64 accumulate)

@@ -166,8 +166,26 @@ def rotate_back_aggregate(x_local, rotation, rescale, alpha, dst, n_nodes, lmax,
     return _rows(n_nodes, np.asarray(dst), y * w)
 
 
+def edge_chain(terms, shape, activation=None) -> np.ndarray:
+    """float64 truth of the one-pass elementwise chain:
+    ``act(sum_t coef_t * a_t * b_t)`` with NumPy broadcasting to ``shape``."""
+    out = np.zeros(tuple(shape), dtype=np.float64)
+    for term in terms:
+        coef, a = term[0], np.asarray(term[1], dtype=np.float64)
+        value = coef * np.broadcast_to(a, shape)
+        if len(term) == 3:
+            value = value * np.broadcast_to(np.asarray(term[2], dtype=np.float64), shape)
+        out = out + value
+    if activation == "silu":
+        return out / (1.0 + np.exp(-out))
+    if activation == "sigmoid":
+        return 1.0 / (1.0 + np.exp(-out))
+    return out
+
+
 __all__ = [
     "dst_from_offsets",
+    "edge_chain",
     "rotate_back_aggregate",
     "rotation_block_offsets",
     "force_assembly",

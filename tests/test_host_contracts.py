@@ -57,7 +57,7 @@ def test_package_exports_reference_names_plus_fused_attention():
         "rmsnorm_available", "segment_available", "segment_offsets", "segment_softmax",
         "segment_sum", "zonal_scatter",
     ]
-    additive = {"segment_attention", "rotate_back_aggregate"}
+    additive = {"segment_attention", "rotate_back_aggregate", "edge_chain"}
     assert sorted(set(kernels.__all__) - additive) == reference_names
     assert kernels.__all__ == sorted(kernels.__all__)
     for name in kernels.__all__:

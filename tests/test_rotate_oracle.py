@@ -9,7 +9,8 @@ the fp32 ``reference.rotate_back_aggregate_reference``, the float64
 ``oracle.truth`` and the loop form ``oracle.loops`` -- are pinned to each
 other and to known answers: a hand-computed quarter turn, identity blocks
 (the operator must reduce to an alpha-weighted segment sum) and a round trip
-through random orthogonal blocks.
+through random orthogonal blocks.  The float64 truth of the one-pass edge
+chain (``oracle.truth.edge_chain``) is pinned to hand-computed values here too.
 """
 from __future__ import annotations
 
@@ -122,3 +123,22 @@ def test_reference_validation():
         rotate_back_aggregate_reference(x, rot, None, alpha, None, off, dst, 1, 3)  # heads
     with pytest.raises(ValueError):
         rotate_back_aggregate_reference(x, rot, None, alpha[:, :1], None, off, dst, 1, 2)
+
+
+def test_edge_chain_truth_known_answers():
+    # x + y * g with a [E, 1, C] gate, then the two activations
+    x = np.array([[[1.0, -2.0]], [[0.5, 0.0]]])            # [2, 1, 2]
+    y = np.array([[[3.0, 1.0]], [[-1.0, 2.0]]])
+    g = np.array([[[0.5, 2.0]], [[1.0, 1.0]]])             # gate, same shape here
+    z = truth.edge_chain([(1.0, x), (1.0, y, g)], (2, 1, 2))
+    np.testing.assert_array_equal(z, [[[2.5, 0.0]], [[-0.5, 2.0]]])
+    sig = truth.edge_chain([(1.0, x), (1.0, y, g)], (2, 1, 2), "sigmoid")
+    np.testing.assert_allclose(sig, 1.0 / (1.0 + np.exp(-z)))
+    silu = truth.edge_chain([(1.0, x), (1.0, y, g)], (2, 1, 2), "silu")
+    np.testing.assert_allclose(silu, z / (1.0 + np.exp(-z)))
+    # broadcasting: a per-channel vector and a per-edge scale
+    w = np.array([1.0, 10.0])
+    s = np.array([[[2.0]], [[3.0]]])
+    got = truth.edge_chain([(-1.0, w, s)], (2, 3, 2))
+    assert got.shape == (2, 3, 2)
+    np.testing.assert_array_equal(got[1, 2], [-3.0, -30.0])
