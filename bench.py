@@ -409,6 +409,28 @@ def _op_softmax(ctx):
                    {"note": "standalone alpha output, L2 flushed"})
 
 
+def _op_softmax_hub(ctx):
+    """Standalone softmax (H = 8) on the C3 segment sizes with one extra hub
+    segment of 100,000 edges in the middle of the frame; per-edge time is
+    compared with the uniform C3 line."""
+    from bysj_b200 import _C
+
+    g, n = ctx["g"], ctx["g"].n_atoms
+    device = ctx["device"]
+    sizes = (ctx["offsets"][1:] - ctx["offsets"][:-1]).clone()
+    sizes[n // 2] += 100_000
+    off = torch.zeros(n + 1, dtype=torch.int64, device=device)
+    off[1:] = torch.cumsum(sizes, 0)
+    e = int(off[-1])
+    gen = torch.Generator(device=device).manual_seed(94)
+    logit = torch.randn(e, 8, device=device, generator=gen) * 2 ** 0.5
+    env = torch.ones(e, device=device)
+    t = time_launches(lambda: _C.segment_softmax_forward(logit, env, off), ctx["iters"],
+                      ctx["flush"])
+    return op_line("segment_softmax_h8_hub", e * (32 + 4 + 32) + 8 * (n + 1), t, ctx["peak"], e,
+                   {"note": "C3 sizes plus one 100,000-edge segment; L2 flushed"})
+
+
 def _op_segment_sum(ctx):
     from bysj_b200 import _C
 
@@ -652,6 +674,7 @@ OPS = {
     "group": _op_group,
     "attention_bf16": _op_attention_bf16,
     "softmax": _op_softmax,
+    "softmax_hub": _op_softmax_hub,
     "segment_sum": _op_segment_sum,
     "force": _op_force,
     "force_random_order": lambda ctx: _op_force(ctx, shuffled=True),

@@ -41,6 +41,9 @@ struct SmxArgs {
   SplitSlots ss;         // partial statistics  [parts][2][2*cpad]
   float* final_stats;    // combined statistics [parts][2*cpad]
   int* big_split;        // set when a split segment is left to the second pass
+  int64_t* hub_slot;     // whole forward: per partition, the hub segment it left
+                         // to segment_softmax_hub_kernel, or -1 (NULL: no hubs)
+  int64_t hub_rows;      // segments longer than this are hubs
 };
 
 // Split segments up to this many edges are written by the piece that
@@ -822,18 +825,23 @@ __global__ void __launch_bounds__(kBlock, quad_pipelined<LP>() ? 2 : 3)
 
 // A whole segment longer than one chunk: running (max, sum) per channel over
 // chunks read from global memory, merged over the edge groups, then a second
-// read for the weights (as quad_segment's multi-chunk whole path).
+// read for the weights (as quad_segment's multi-chunk whole path).  The three
+// steps are separate so that a CTA can share one long segment among its warps
+// (segment_softmax_hub_kernel): pass 1 and pass 2 walk the chunks
+// lo + first, lo + first + step, ...
+
+// Pass 1: this warp's running (max, sum) per channel of its quad, merged over
+// the edge groups (every lane of quad q ends with the same values).
 template <int LP, bool kEnv>
-__device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
-                                         int g, int q) {
+__device__ __forceinline__ void lean_stats(const SmxArgs& a, int64_t lo, int64_t hi,
+                                           int64_t first, int64_t step, int g, int q,
+                                           float (&m)[4], float (&d)[4]) {
   using Q = QuadSmx<LP>;
-  constexpr int C = 4 * LP;
   float4 x[Q::T];
-  float m[4], d[4], inv[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
   #pragma unroll 1
-  for (int64_t base = lo; base < hi; base += Q::CHUNK) {
+  for (int64_t base = lo + first; base < hi; base += step) {
     quad_load<LP, kEnv>(a, base, hi, g, q, true, x);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -858,6 +866,15 @@ __device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo
       m[i] = mn;
     }
   }
+}
+
+// Folds in the null logit: m becomes the final shift, inv the reciprocal
+// denominator; the null weight is written when `write_null` (group 0).
+template <int LP>
+__device__ __forceinline__ void lean_norm(const SmxArgs& a, int64_t n, int g, int q,
+                                          bool write_null, float (&m)[4], const float (&d)[4],
+                                          float (&inv)[4]) {
+  constexpr int C = 4 * LP;
   float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   if (a.xn) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
@@ -872,14 +889,36 @@ __device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo
     inv[i] = total > 0.0f ? 1.0f / total : 0.0f;
     m[i] = mm;
   }
-  if (g == 0 && a.out_null)
+  if (write_null && g == 0 && a.out_null)
     reinterpret_cast<float4*>(a.out_null + n * C)[q] =
         make_float4(w0[0] * inv[0], w0[1] * inv[1], w0[2] * inv[2], w0[3] * inv[3]);
+}
+
+// Pass 2: the weights of this warp's chunks.
+template <int LP, bool kEnv>
+__device__ __forceinline__ void lean_emit(const SmxArgs& a, int64_t lo, int64_t hi,
+                                          int64_t first, int64_t step, int g, int q,
+                                          const float (&m)[4], const float (&inv)[4]) {
+  using Q = QuadSmx<LP>;
+  float4 x[Q::T];
+  float mm[4], ii[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { mm[i] = m[i]; ii[i] = inv[i]; }
   #pragma unroll 1
-  for (int64_t base = lo; base < hi; base += Q::CHUNK) {
+  for (int64_t base = lo + first; base < hi; base += step) {
     quad_load<LP, kEnv>(a, base, hi, g, q, true, x);
-    quad_write<LP>(a, base, hi, g, q, true, x, m, inv);
+    quad_write<LP>(a, base, hi, g, q, true, x, mm, ii);
   }
+}
+
+template <int LP, bool kEnv>
+__device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
+                                         int g, int q) {
+  using Q = QuadSmx<LP>;
+  float m[4], d[4], inv[4];
+  lean_stats<LP, kEnv>(a, lo, hi, 0, Q::CHUNK, g, q, m, d);
+  lean_norm<LP>(a, n, g, q, true, m, d, inv);
+  lean_emit<LP, kEnv>(a, lo, hi, 0, Q::CHUNK, g, q, m, inv);
 }
 
 // Rows per lane and CTA shape of the whole kernel: a 128-row chunk at every
@@ -922,6 +961,10 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
   const int q = lane % LP;
   const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
   const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
+  // Every partition records the hub segment it leaves to the hub kernel, or
+  // -1 (at most one: a hub is longer than a partition, so its start is the
+  // only segment start in the partition's range).
+  if (a.hub_slot && lane == 0) a.hub_slot[p] = -1;
   if (n0 >= n1) return;
   char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
   float4* bufs[2] = {reinterpret_cast<float4*>(mine), reinterpret_cast<float4*>(mine + S::kBytes)};
@@ -948,7 +991,11 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
     else if (hi - lo <= Q::CHUNK)
       lean_whole<LP, kEnv, TT>(a, n, lo, hi, g, q, bufs[b],
                            reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
-    else
+    else if (a.hub_slot != nullptr && hi - lo > a.hub_rows) {
+      // a CTA of the hub kernel takes it (the partition index is recomputed
+      // here rather than kept live through the loop)
+      if (lane == 0) a.hub_slot[global_warp()] = n;
+    } else
       lean_big<LP, kEnv>(a, n, lo, hi, g, q);
     __syncwarp();  // every lane is done with bufs[b] before it is refilled
     lo = hi;
@@ -957,6 +1004,98 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
     b ^= 1;
   }
   cp_async_wait<0>();
+  // This warp's slot is written: the dependent hub pass may be scheduled.
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// ---- forward, hub segments of the whole kernel -----------------------------
+// A segment longer than hub_rows (and than a partition) would keep one warp
+// of the whole kernel busy for all of its rows (a 100,000-edge hub: 8 ms).
+// The whole kernel leaves it here instead: one CTA of kHubWarps warps per hub
+// (hubs dealt round-robin over kHubCtas CTAs in partition order), warp w
+// walking chunks w, w + kHubWarps, ... for the statistics, which are merged
+// over the warps in warp order through shared memory (deterministic), then
+// for the weights.  Launched as a programmatic dependent of the whole kernel;
+// a frame without hubs reads the partitions' slots and returns.  (A version
+// that spread each hub over every SM with a grid barrier was 1.6-3.5x faster
+// on hubs but cost ~18 us per call without hubs, against ~3 us here.)
+constexpr int kHubWarps = 16;
+constexpr int kHubCtas = 8;
+constexpr int64_t kHubRows = 4096;
+
+template <int LP, bool kEnv>
+__global__ void __launch_bounds__(kHubWarps * kWarp, 1) segment_softmax_hub_kernel(SmxArgs a) {
+  using Q = QuadSmx<LP>;
+  constexpr int kThreads = kHubWarps * kWarp;
+  __shared__ float s_m[kHubWarps][LP][4];
+  __shared__ float s_d[kHubWarps][LP][4];
+  __shared__ int64_t s_list[kThreads];
+  __shared__ int s_warp_count[kHubWarps];
+  __shared__ int s_count;
+  const int lane = lane_id();
+  const int w = threadIdx.x >> 5;
+  const int g = lane / LP;
+  const int q = lane % LP;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the whole kernel is complete
+  {
+    bool any = false;
+    for (int64_t p = threadIdx.x; p < a.mp.parts; p += kThreads) any |= a.hub_slot[p] >= 0;
+    if (__syncthreads_count(any) == 0) return;
+  }
+  int seen = 0;  // hubs found in earlier sweeps (the same in every thread)
+  for (int64_t base = 0; base < a.mp.parts; base += kThreads) {
+    const int64_t p = base + threadIdx.x;
+    const int64_t hub = p < a.mp.parts ? a.hub_slot[p] : -1;
+    const unsigned ballot = __ballot_sync(kFull, hub >= 0);
+    if (lane == 0) s_warp_count[w] = __popc(ballot);
+    if (threadIdx.x == 0) s_count = 0;
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int k = 0; k < kHubWarps; ++k) {
+      if (k < w) before += s_warp_count[k];
+      total += s_warp_count[k];
+    }
+    // The k-th hub in partition order goes to CTA k mod gridDim.
+    const int rank = seen + before + __popc(ballot & ((1u << lane) - 1u));
+    if (hub >= 0 && rank % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x))
+      s_list[atomicAdd(&s_count, 1)] = hub;  // list order does not matter: each
+                                             // hub is computed on its own
+    __syncthreads();
+    const int mine = s_count;
+    for (int k = 0; k < mine; ++k) {
+      const int64_t n = s_list[k];
+      const int64_t lo = __ldg(a.mp.offsets + n), hi = __ldg(a.mp.offsets + n + 1);
+      float m[4], d[4], inv[4];
+      lean_stats<LP, kEnv>(a, lo, hi, static_cast<int64_t>(w) * Q::CHUNK,
+                           static_cast<int64_t>(kHubWarps) * Q::CHUNK, g, q, m, d);
+      if (g == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          s_m[w][q][i] = m[i];
+          s_d[w][q][i] = d[i];
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float mm = -INFINITY, dd = 0.0f;
+        for (int k2 = 0; k2 < kHubWarps; ++k2) {  // warp order: deterministic
+          const float mo = s_m[k2][q][i], dk = s_d[k2][q][i];
+          const float mn = fmaxf(mm, mo);
+          dd = dd * shifted_exp(mm, mn) + dk * shifted_exp(mo, mn);
+          mm = mn;
+        }
+        m[i] = mm;
+        d[i] = dd;
+      }
+      lean_norm<LP>(a, n, g, q, w == 0, m, d, inv);
+      lean_emit<LP, kEnv>(a, lo, hi, static_cast<int64_t>(w) * Q::CHUNK,
+                          static_cast<int64_t>(kHubWarps) * Q::CHUNK, g, q, m, inv);
+      __syncthreads();  // s_m / s_d are reused by the next hub
+    }
+    seen += total;
+    __syncthreads();  // s_warp_count / s_count / s_list are reused by the next sweep
+  }
 }
 
 // ---- forward, whole segments in a permuted storage order (C = 4 or 8) -----
@@ -1726,6 +1865,7 @@ __global__ void __launch_bounds__(kBlock)
 using SmxKernel = void (*)(SmxArgs);
 struct SmxConfig {
   SmxKernel main = nullptr, split = nullptr;
+  SmxKernel hub = nullptr;  // whole forward: the CTA-wide pass over hub segments
   int64_t tc = 0, tiles = 1;
   size_t main_smem = 0;  // dynamic shared memory of the main launch
   int block = kBlock;    // threads per CTA of the main launch
@@ -1747,6 +1887,7 @@ SmxConfig quad_make_env() {
   if constexpr (kLean) {
     c.main = segment_softmax_whole_kernel<LP, kEnv>;
     c.split = nullptr;  // no segment is split
+    c.hub = segment_softmax_hub_kernel<LP, kEnv>;
     c.block = WholeShape<LP>::kThreads;
   } else {
     c.main = segment_softmax_quad_kernel<LP, false, kEnv>;
@@ -1879,6 +2020,7 @@ struct SmxLayout {
   size_t bytes = 0;
   SplitSlots ss{};
   float* final_stats = nullptr;
+  int64_t* hub_slot = nullptr;
   int smem_status = BYSJ_OK;
 };
 
@@ -1903,6 +2045,7 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
   float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * 2 * L.cpad);
   int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts) * L.cfg.tiles + 1);
   L.final_stats = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * L.cpad);
+  if (L.cfg.hub != nullptr) L.hub_slot = carve.take<int64_t>(static_cast<size_t>(L.plan.parts));
   L.bytes = carve.need;
   L.ss = SplitSlots{slots, tickets, 2 * L.cpad, static_cast<int>(L.cfg.tiles)};
   return L;
@@ -1923,10 +2066,34 @@ int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
   a.final_stats = L.final_stats;
   a.big_split = L.ss.tickets + L.plan.parts * L.cfg.tiles;
   a.cpad = L.cpad;
+  a.hub_slot = L.hub_slot;
+  // A hub is longer than a partition (so a partition owns at most one) and
+  // than kHubRows rows (so short-segment frames never use the hub pass).
+  a.hub_rows = L.plan.ipc > kHubRows ? L.plan.ipc : kHubRows;
   if (L.smem_status != BYSJ_OK) return L.smem_status;
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
   L.cfg.main<<<grid, L.cfg.block, L.cfg.main_smem, s>>>(a);
   st = launch_check(name);
+  if (st) return st;
+  if (L.cfg.hub != nullptr && n_edges > kHubRows) {  // no hub fits a smaller frame
+    // A programmatic dependent launch: the hub kernel's launch is processed
+    // while the whole kernel drains, and its griddepcontrol.wait orders it
+    // after the whole kernel (the usual frame has no hub, so this launch is
+    // all it costs).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kHubCtas);
+    cfg.blockDim = dim3(kHubWarps * kWarp);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    st = cuda_check(cudaLaunchKernelEx(&cfg, L.cfg.hub, a), "segment softmax: hub pass");
+    if (st) return st;
+    st = launch_check(name);
+  }
   if (st || L.cfg.split == nullptr) return st;
   L.cfg.split<<<grid, kBlock, 0, s>>>(a);
   return launch_check(name);

@@ -392,3 +392,30 @@ def test_segment_softmax_all_masked_segment_is_zero(cuda):
     a = K.segment_softmax(logit, env, off)
     assert a[:3].count_nonzero() == 0
     torch.testing.assert_close(a[3:].sum(0), torch.ones(4, device="cuda"))
+
+
+@pytest.mark.parametrize("heads", [8, 4, 16])
+def test_segment_softmax_hub_segments(cuda, heads):
+    # Hubs (100k and 20k edges) among 3000 short segments: the whole-segment
+    # kernel leaves them to the CTA-wide hub pass; every weight, with env and
+    # null logit, against the fp32 oracle; repeats bit-identical.
+    gen = torch.Generator().manual_seed(heads)
+    sizes = torch.randint(20, 120, (3000,), generator=gen)
+    sizes[1234], sizes[2999], sizes[0] = 100_000, 20_000, 5000
+    dst, off = graph(sizes)
+    e = dst.numel()
+    logit = torch.randn(e, heads, generator=gen) * 2
+    env = torch.where(torch.rand(e, generator=gen) < 0.1, torch.tensor(0.0),
+                      torch.rand(e, generator=gen) + 0.05)
+    null = torch.randn(sizes.numel(), heads, generator=gen)
+    a, n0 = K.segment_softmax(logit.cuda(), env.cuda(), off, null.cuda())
+    wa, wn = segment_softmax_reference(logit, env, dst.cpu(), off.cpu(), null)
+    torch.testing.assert_close(a.cpu(), wa, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(n0.cpu(), wn, rtol=1e-5, atol=1e-6)
+    a2, n2 = K.segment_softmax(logit.cuda(), env.cuda(), off, null.cuda())
+    assert torch.equal(a, a2) and torch.equal(n0, n2)
+    # plain (no null, all-ones env) takes the same path
+    ones = torch.ones(e)
+    got = K.segment_softmax(logit.cuda(), ones.cuda(), off)
+    want, _ = segment_softmax_reference(logit, ones, dst.cpu(), off.cpu())
+    torch.testing.assert_close(got.cpu(), want, rtol=1e-5, atol=1e-6)
