@@ -372,7 +372,7 @@ def _op_offsets(ctx):
     t = time_launches(lambda: _C.segment_offsets_device(g.dst, n, flags), ctx["iters"],
                       ctx["flush"])
     return op_line("segment_offsets", 8 * e + 8 * (n + 1), t, ctx["peak"], e,
-                   {"note": "2 launches (check + boundary), L2 flushed"})
+                   {"note": "one fused check + boundary launch, L2 flushed"})
 
 
 def _op_group(ctx):

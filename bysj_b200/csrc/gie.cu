@@ -31,6 +31,7 @@ struct GieArgs {
   int64_t rows, n_radial, channels;
   int64_t lv;            // R*C/VEC
   int64_t skip_degrees;  // generic kernels: > 0 = return if slot[] is the degree table of that L
+  const uint32_t* gate;  // non-NULL: every kernel returns at once if *gate != 0
   MergePath mp;
   SplitSlots ss;
 };
@@ -116,6 +117,7 @@ __device__ __forceinline__ void gie_accumulate(const GieArgs& a, const LaneMap<V
 
 template <int VEC, int NV>
 __global__ void __launch_bounds__(kBlock, 2) gie_fwd_kernel(GieArgs a) {
+  if (a.gate != nullptr && *a.gate != 0) return;  // the CSR view was not built
   constexpr int TV = kWarp * NV;
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
@@ -197,6 +199,7 @@ constexpr int kZonalChunk = 32;  // edges whose zonal rows a warp stages at once
 template <int LPE, int L>
 __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
     gie_fwd_degree_kernel(GieArgs a, int64_t slot_base) {
+  if (a.gate != nullptr && *a.gate != 0) return;  // the CSR view was not built
   constexpr int R = (L + 1) * (L + 1) - 1;
   constexpr int EG = kWarp / LPE;
   __shared__ float zstage[kWarpsPerBlock][kZonalChunk * R];
@@ -369,6 +372,7 @@ struct GieBwdSmem {
 template <int LPE, int L>
 __global__ void __launch_bounds__(kBlock, 2)
     gie_bwd_degree_kernel(GieArgs a, int64_t slot_base) {
+  if (a.gate != nullptr && *a.gate != 0) return;  // the CSR view was not built
   using M = GieBwdSmem<LPE, L>;
   constexpr int R = M::R;
   constexpr int EG = kWarp / LPE;
@@ -533,6 +537,7 @@ __global__ void __launch_bounds__(kBlock, 2)
 // resolved before the upstream weight is applied.
 template <int VEC, int NV>
 __global__ void __launch_bounds__(kBlock, 2) gie_bwd_kernel(GieArgs a) {
+  if (a.gate != nullptr && *a.gate != 0) return;  // the CSR view was not built
   constexpr int TV = kWarp * NV;
   extern __shared__ float s_dot[];  // [warps][TV]
   const int64_t p = global_warp();
@@ -768,9 +773,11 @@ GieDegreeLayout gie_degree_layout(int64_t n_edges, int64_t n_nodes, int64_t degr
                            kWarpsPerBlock;
   L.plan = plan_partitions(n_edges, n_nodes, resident, 16);
   const int64_t stride = (rows * channels + 7) / 8 * 8;
+  // Tickets first: they then follow the generic layout's tickets (which end
+  // that layout) across at most 255 bytes of padding, so one memset clears both.
   Carver carve(ws);
-  float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * stride);
   int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts));
+  float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * stride);
   L.bytes = carve.need;
   L.ss = SplitSlots{slots, tickets, stride, 1};
   return L;
@@ -823,15 +830,16 @@ size_t bysj_gie_zonal_scatter_workspace_size(int64_t n_edges, int64_t n_nodes,
          gie_degree_layout(n_edges, n_nodes, degrees, channels, nullptr).bytes;
 }
 
-int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
-                                   const int64_t* offsets,
-                                   const int64_t* order,
-                                   const int64_t* radial_slot,
-                                   const float* inv_sqrt_deg, int64_t n_edges,
-                                   int64_t n_nodes, int64_t n_rows,
-                                   int64_t n_radial, int64_t channels,
-                                   float* out, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int gie_forward_impl(const float* zonal, const float* radial, const int64_t* offsets,
+                     const int64_t* order, const int64_t* radial_slot,
+                     const float* inv_sqrt_deg, int64_t n_edges, int64_t n_nodes,
+                     int64_t n_rows, int64_t n_radial, int64_t channels, float* out,
+                     void* workspace, size_t workspace_bytes, void* stream,
+                     const uint32_t* gate) {
   clear_error();
   int st = gie_check(n_edges, n_nodes, n_rows, n_radial, channels);
   if (st) return st;
@@ -860,11 +868,17 @@ int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
     return fail(BYSJ_ERR_WORKSPACE,
                 "zonal scatter: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
-  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0,
-                                  sizeof(int) * L.plan.parts * L.cfg.tiles, s),
+  // One memset for both kernels' tickets (the degree layout's tickets follow
+  // the generic layout's, across the alignment padding).
+  const size_t ticket_bytes =
+      degrees > 0 ? static_cast<size_t>(reinterpret_cast<char*>(D.ss.tickets + D.plan.parts) -
+                                        reinterpret_cast<char*>(L.ss.tickets))
+                  : sizeof(int) * L.plan.parts * L.cfg.tiles;
+  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, ticket_bytes, s),
                   "zonal scatter: ticket reset");
   if (st) return st;
   GieArgs a{};
+  a.gate = gate;
   a.zonal = zonal;
   a.radial = radial;
   a.order = order;
@@ -878,9 +892,6 @@ int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
   if (degrees > 0) {
-    st = cuda_check(cudaMemsetAsync(D.ss.tickets, 0, sizeof(int) * D.plan.parts, s),
-                    "zonal scatter: ticket reset (degree rows)");
-    if (st) return st;
     GieArgs d = a;
     d.lv = 0;
     d.mp = MergePath{offsets, n_nodes, n_edges, D.plan.ipc, D.plan.parts};
@@ -893,6 +904,33 @@ int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
   dim3 grid(L.plan.blocks, static_cast<unsigned>(L.cfg.tiles));
   L.cfg.kernel<<<grid, kBlock, 0, s>>>(a);
   return launch_check("gie_fwd_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int bysj_gie_zonal_scatter_forward(const float* zonal, const float* radial,
+                                   const int64_t* offsets, const int64_t* order,
+                                   const int64_t* radial_slot, const float* inv_sqrt_deg,
+                                   int64_t n_edges, int64_t n_nodes, int64_t n_rows,
+                                   int64_t n_radial, int64_t channels, float* out,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  return gie_forward_impl(zonal, radial, offsets, order, radial_slot, inv_sqrt_deg, n_edges,
+                          n_nodes, n_rows, n_radial, channels, out, workspace, workspace_bytes,
+                          stream, nullptr);
+}
+
+int bysj_gie_zonal_scatter_forward_gated(const float* zonal, const float* radial,
+                                         const int64_t* offsets, const int64_t* order,
+                                         const int64_t* radial_slot, const float* inv_sqrt_deg,
+                                         int64_t n_edges, int64_t n_nodes, int64_t n_rows,
+                                         int64_t n_radial, int64_t channels, float* out,
+                                         void* workspace, size_t workspace_bytes, void* stream,
+                                         const uint32_t* gate) {
+  return gie_forward_impl(zonal, radial, offsets, order, radial_slot, inv_sqrt_deg, n_edges,
+                          n_nodes, n_rows, n_radial, channels, out, workspace, workspace_bytes,
+                          stream, gate);
 }
 
 size_t bysj_gie_zonal_scatter_degree_workspace_size(int64_t n_edges, int64_t n_nodes,
@@ -964,13 +1002,16 @@ size_t bysj_gie_zonal_scatter_backward_workspace_size(int64_t n_edges,
          gie_degree_layout(n_edges, n_nodes, degrees, channels, nullptr, true).bytes;
 }
 
-int bysj_gie_zonal_scatter_backward(
-    const float* grad_out, const float* zonal, const float* radial,
-    const int64_t* dst, const int64_t* offsets, const int64_t* order,
-    const int64_t* radial_slot, const float* inv_sqrt_deg, int64_t n_edges,
-    int64_t n_nodes, int64_t n_rows, int64_t n_radial, int64_t channels,
-    float* grad_zonal, float* grad_radial, float* grad_inv, void* workspace,
-    size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int gie_backward_impl(const float* grad_out, const float* zonal, const float* radial,
+                      const int64_t* dst, const int64_t* offsets, const int64_t* order,
+                      const int64_t* radial_slot, const float* inv_sqrt_deg, int64_t n_edges,
+                      int64_t n_nodes, int64_t n_rows, int64_t n_radial, int64_t channels,
+                      float* grad_zonal, float* grad_radial, float* grad_inv, void* workspace,
+                      size_t workspace_bytes, void* stream, const uint32_t* gate) {
   clear_error();
   (void)dst;
   int st = gie_check(n_edges, n_nodes, n_rows, n_radial, channels);
@@ -1017,10 +1058,15 @@ int bysj_gie_zonal_scatter_backward(
     return fail(BYSJ_ERR_WORKSPACE,
                 "zonal scatter backward: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
-  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, sizeof(int) * L.plan.parts, s),
+  const size_t ticket_bytes =
+      degrees > 0 ? static_cast<size_t>(reinterpret_cast<char*>(D.ss.tickets + D.plan.parts) -
+                                        reinterpret_cast<char*>(L.ss.tickets))
+                  : sizeof(int) * L.plan.parts;
+  st = cuda_check(cudaMemsetAsync(L.ss.tickets, 0, ticket_bytes, s),
                   "zonal scatter backward: ticket reset");
   if (st) return st;
   GieArgs a{};
+  a.gate = gate;
   a.zonal = zonal;
   a.radial = radial;
   a.order = order;
@@ -1037,9 +1083,6 @@ int bysj_gie_zonal_scatter_backward(
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
   if (degrees > 0) {
-    st = cuda_check(cudaMemsetAsync(D.ss.tickets, 0, sizeof(int) * D.plan.parts, s),
-                    "zonal scatter backward: ticket reset (degree rows)");
-    if (st) return st;
     GieArgs d = a;
     d.lv = 0;
     d.mp = MergePath{offsets, n_nodes, n_edges, D.plan.ipc, D.plan.parts};
@@ -1052,6 +1095,35 @@ int bysj_gie_zonal_scatter_backward(
   const size_t smem = sizeof(float) * kBlock * L.cfg.nv;
   L.cfg.kernel<<<L.plan.blocks, kBlock, smem, s>>>(a);
   return launch_check("gie_bwd_kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int bysj_gie_zonal_scatter_backward(
+    const float* grad_out, const float* zonal, const float* radial, const int64_t* dst,
+    const int64_t* offsets, const int64_t* order, const int64_t* radial_slot,
+    const float* inv_sqrt_deg, int64_t n_edges, int64_t n_nodes, int64_t n_rows,
+    int64_t n_radial, int64_t channels, float* grad_zonal, float* grad_radial,
+    float* grad_inv, void* workspace, size_t workspace_bytes, void* stream) {
+  return gie_backward_impl(grad_out, zonal, radial, dst, offsets, order, radial_slot,
+                           inv_sqrt_deg, n_edges, n_nodes, n_rows, n_radial, channels,
+                           grad_zonal, grad_radial, grad_inv, workspace, workspace_bytes,
+                           stream, nullptr);
+}
+
+int bysj_gie_zonal_scatter_backward_gated(
+    const float* grad_out, const float* zonal, const float* radial, const int64_t* dst,
+    const int64_t* offsets, const int64_t* order, const int64_t* radial_slot,
+    const float* inv_sqrt_deg, int64_t n_edges, int64_t n_nodes, int64_t n_rows,
+    int64_t n_radial, int64_t channels, float* grad_zonal, float* grad_radial,
+    float* grad_inv, void* workspace, size_t workspace_bytes, void* stream,
+    const uint32_t* gate) {
+  return gie_backward_impl(grad_out, zonal, radial, dst, offsets, order, radial_slot,
+                           inv_sqrt_deg, n_edges, n_nodes, n_rows, n_radial, channels,
+                           grad_zonal, grad_radial, grad_inv, workspace, workspace_bytes,
+                           stream, gate);
 }
 
 size_t bysj_gie_zonal_scatter_backward_degree_workspace_size(int64_t n_edges, int64_t n_nodes,

@@ -5,9 +5,10 @@
 // paths replace it:
 //
 //  * sorted: for a destination-sorted edge list the offsets are the segment
-//    boundaries, offsets[n] = first e with dst[e] >= n.  A validation pass
-//    flags unsorted or out-of-range input; only if the flags are clear does
-//    the boundary pass write, so an unsorted list cannot make it loop.
+//    boundaries, offsets[n] = first e with dst[e] >= n.  One pass validates
+//    dst (flags for unsorted or out-of-range input) and writes the
+//    boundaries from clamped values, so an unsorted list cannot make it loop
+//    or write out of bounds (its offsets are then meaningless).
 //  * histogram: any order.  Warp-aggregated integer atomics count the edges
 //    per node (lanes holding the same destination are merged with
 //    __match_any_sync first), then a three-phase exclusive scan.  Integer
@@ -29,52 +30,27 @@ __device__ __forceinline__ longlong2 ld_pair(const int64_t* dst, int64_t i) {
   return __ldg(reinterpret_cast<const longlong2*>(dst) + i);
 }
 
-__global__ void __launch_bounds__(kBlock)
-    offsets_check_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
-                         int64_t n_nodes, uint32_t* flags) {
-  uint32_t local = 0;
-  const int64_t pairs = n_edges / 2;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < pairs;
-       i0 += stride * kPairsPerStep) {
-    longlong2 v[kPairsPerStep];
-    int64_t before[kPairsPerStep];
-#pragma unroll
-    for (int k = 0; k < kPairsPerStep; ++k) {
-      const int64_t i = i0 + k * stride;
-      v[k] = i < pairs ? ld_pair(dst, i) : make_longlong2(0, 0);
-      before[k] = (i < pairs && i > 0) ? __ldg(dst + 2 * i - 1) : INT64_MIN;
-    }
-#pragma unroll
-    for (int k = 0; k < kPairsPerStep; ++k) {
-      if (i0 + k * stride >= pairs) continue;
-      const int64_t x = v[k].x, y = v[k].y;
-      if (x < 0 || x >= n_nodes || y < 0 || y >= n_nodes) local |= BYSJ_FLAG_OUT_OF_RANGE;
-      if (before[k] > x || x > y) local |= BYSJ_FLAG_UNSORTED;
-    }
-  }
-  // An odd element count leaves the last element to one thread.
-  if ((n_edges & 1) && blockIdx.x == 0 && threadIdx.x == 0) {
-    const int64_t e = n_edges - 1;
-    const int64_t d = __ldg(dst + e);
-    if (d < 0 || d >= n_nodes) local |= BYSJ_FLAG_OUT_OF_RANGE;
-    if (e > 0 && __ldg(dst + e - 1) > d) local |= BYSJ_FLAG_UNSORTED;
-  }
-  local = __reduce_or_sync(kFull, local);
-  if (local && lane_id() == 0) atomicOr(flags, local);
-}
-
 // offsets[n] for the nodes in (dst[e-1], dst[e]] is e.
 __device__ __forceinline__ void write_boundary(int64_t prev, int64_t cur, int64_t e,
                                                int64_t* __restrict__ offsets) {
   for (int64_t n = prev + 1; n <= cur; ++n) offsets[n] = e;
 }
 
+// One pass for a sorted list: validates dst and writes the boundaries in the
+// same read of each pair.  Values are clamped to [-1, n_nodes] before a
+// boundary is written, so an unsorted or out-of-range list (flagged, its
+// offsets meaningless) still writes only offsets[0..n_nodes] and no loop runs
+// longer than n_nodes + 1 steps.  For a valid list every offset is written
+// exactly once, as by the two-pass form.
+__device__ __forceinline__ int64_t clamp_node(int64_t v, int64_t n_nodes) {
+  return v < -1 ? -1 : (v > n_nodes ? n_nodes : v);
+}
+
 __global__ void __launch_bounds__(kBlock)
-    offsets_boundary_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
-                            int64_t n_nodes, int64_t* __restrict__ offsets,
-                            const uint32_t* flags) {
-  if (*flags != 0) return;
+    offsets_sorted_fused_kernel(const int64_t* __restrict__ dst, int64_t n_edges,
+                                int64_t n_nodes, int64_t* __restrict__ offsets,
+                                uint32_t* flags) {
+  uint32_t local = 0;
   const int64_t pairs = n_edges / 2;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < pairs;
@@ -91,8 +67,12 @@ __global__ void __launch_bounds__(kBlock)
     for (int k = 0; k < kPairsPerStep; ++k) {
       const int64_t i = i0 + k * stride;
       if (i >= pairs) continue;
-      write_boundary(before[k], v[k].x, 2 * i, offsets);
-      write_boundary(v[k].x, v[k].y, 2 * i + 1, offsets);
+      const int64_t x = v[k].x, y = v[k].y;
+      if (x < 0 || x >= n_nodes || y < 0 || y >= n_nodes) local |= BYSJ_FLAG_OUT_OF_RANGE;
+      if (before[k] > x || x > y) local |= BYSJ_FLAG_UNSORTED;
+      const int64_t xc = clamp_node(x, n_nodes), yc = clamp_node(y, n_nodes);
+      write_boundary(clamp_node(before[k], n_nodes), xc, 2 * i, offsets);
+      write_boundary(xc, yc, 2 * i + 1, offsets);
     }
   }
   // The odd last element and the end marker: nodes in (dst[E-1], N] start at E.
@@ -100,11 +80,16 @@ __global__ void __launch_bounds__(kBlock)
     int64_t prev = n_edges >= 2 ? __ldg(dst + 2 * pairs - 1) : -1;
     if (n_edges & 1) {
       const int64_t last = __ldg(dst + n_edges - 1);
-      write_boundary(prev, last, n_edges - 1, offsets);
+      if (last < 0 || last >= n_nodes) local |= BYSJ_FLAG_OUT_OF_RANGE;
+      if (n_edges > 1 && prev > last) local |= BYSJ_FLAG_UNSORTED;
+      write_boundary(clamp_node(prev, n_nodes), clamp_node(last, n_nodes), n_edges - 1,
+                     offsets);
       prev = last;
     }
-    write_boundary(prev, n_nodes, n_edges, offsets);
+    write_boundary(clamp_node(prev, n_nodes), n_nodes, n_edges, offsets);
   }
+  local = __reduce_or_sync(kFull, local);
+  if (local && lane_id() == 0) atomicOr(flags, local);
 }
 
 // Scalar forms for a dst that is not 16-byte aligned.
@@ -276,11 +261,9 @@ int bysj_segment_offsets_sorted(const int64_t* dst, int64_t n_edges,
                       "segment offsets: zero fill");
   if (aligned16(dst)) {
     const unsigned blocks = stream_blocks((n_edges / 2 + kPairsPerStep - 1) / kPairsPerStep);
-    offsets_check_kernel<<<blocks, kBlock, 0, s>>>(dst, n_edges, n_nodes, flags);
-    int st = launch_check("offsets_check_kernel");
-    if (st) return st;
-    offsets_boundary_kernel<<<blocks, kBlock, 0, s>>>(dst, n_edges, n_nodes, offsets, flags);
-    return launch_check("offsets_boundary_kernel");
+    offsets_sorted_fused_kernel<<<blocks, kBlock, 0, s>>>(dst, n_edges, n_nodes, offsets,
+                                                          flags);
+    return launch_check("offsets_sorted_fused_kernel");
   }
   offsets_check_scalar_kernel<<<stream_blocks(n_edges), kBlock, 0, s>>>(dst, n_edges, n_nodes,
                                                                         flags);

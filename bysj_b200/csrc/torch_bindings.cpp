@@ -149,6 +149,20 @@ std::tuple<Tensor, OptTensor> csr_view(const Tensor& dst, int64_t n_nodes) {
   return {offsets, order};
 }
 
+// Launch-only CSR view for a destination-sorted dst: the boundary offsets and
+// the device flags word, not read back (the GIE entry points take the word as
+// their gate and read it once their kernels are queued).
+std::tuple<Tensor, Tensor> csr_view_launch(const Tensor& dst, int64_t n_nodes) {
+  Tensor offsets = torch::empty({n_nodes + 1}, dst.options());
+  Tensor flags = torch::zeros({1}, dst.options().dtype(torch::kInt32));
+  check(bysj_segment_offsets_sorted(dst.data_ptr<int64_t>(), dst.numel(), n_nodes,
+                                    offsets.data_ptr<int64_t>(),
+                                    reinterpret_cast<uint32_t*>(flags.data_ptr<int32_t>()),
+                                    stream_of(dst)),
+        "segment_offsets");
+  return {offsets, flags};
+}
+
 // ---- segment_sum ------------------------------------------------------------
 
 Tensor segment_sum_forward(Tensor src, Tensor offsets, OptTensor edge_scale,
@@ -589,14 +603,30 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
   // The slot table stays on the device: for the degree-grouped shape the
   // library launches the degree kernel and the generic one, and each checks
   // the table itself (no read back here).
-  auto [offsets, order] = csr_view(dst, nodes);
+  // The sorted-path CSR and the operator are queued together, the operator
+  // gated on the CSR flags; the flags are read once both are in flight.  An
+  // unsorted dst (flag set, operator skipped) is then grouped on the device
+  // and the operator runs again; a destination out of range is an error.
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_workspace_size(edges, nodes, rows, channels));
-  check(bysj_gie_zonal_scatter_forward(
+  auto [offsets, flags] = csr_view_launch(dst, nodes);
+  check(bysj_gie_zonal_scatter_forward_gated(
             zonal.data_ptr<float>(), radial.data_ptr<float>(), offsets.data_ptr<int64_t>(),
-            opt_ptr<int64_t>(order), radial_slot.data_ptr<int64_t>(),
-            inv_sqrt_deg.data_ptr<float>(), edges, nodes, rows, n_radial, channels,
-            out.data_ptr<float>(), ws.data_ptr(), static_cast<size_t>(ws.numel()),
-            stream_of(zonal)),
+            nullptr, radial_slot.data_ptr<int64_t>(), inv_sqrt_deg.data_ptr<float>(), edges,
+            nodes, rows, n_radial, channels, out.data_ptr<float>(), ws.data_ptr(),
+            static_cast<size_t>(ws.numel()), stream_of(zonal),
+            reinterpret_cast<const uint32_t*>(flags.data_ptr<int32_t>())),
+        "gie_zonal_scatter_forward");
+  const int64_t word = flags.item<int32_t>();
+  if (word == 0) return out;
+  TORCH_CHECK(!(word & BYSJ_FLAG_OUT_OF_RANGE),
+              "destination values must be within the node range");
+  auto [grouped_offsets, order] = csr_view(dst, nodes);
+  check(bysj_gie_zonal_scatter_forward(
+            zonal.data_ptr<float>(), radial.data_ptr<float>(),
+            grouped_offsets.data_ptr<int64_t>(), opt_ptr<int64_t>(order),
+            radial_slot.data_ptr<int64_t>(), inv_sqrt_deg.data_ptr<float>(), edges, nodes, rows,
+            n_radial, channels, out.data_ptr<float>(), ws.data_ptr(),
+            static_cast<size_t>(ws.numel()), stream_of(zonal)),
         "gie_zonal_scatter_forward");
   return out;
 }
@@ -618,16 +648,30 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
   Tensor gr = torch::empty_like(radial);
   Tensor gi = torch::empty_like(inv_sqrt_deg);
   if (nodes == 0) return {gz, gr, gi};
-  auto [offsets, order] = csr_view(dst, nodes);
+  // As the forward: gated on the sorted-path flags, read once queued.
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_workspace_size(edges, nodes, rows,
                                                                               channels));
-  check(bysj_gie_zonal_scatter_backward(
+  auto [offsets, flags] = csr_view_launch(dst, nodes);
+  check(bysj_gie_zonal_scatter_backward_gated(
             grad_output.data_ptr<float>(), zonal.data_ptr<float>(), radial.data_ptr<float>(),
-            dst.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(), opt_ptr<int64_t>(order),
+            dst.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(), nullptr,
             radial_slot.data_ptr<int64_t>(), inv_sqrt_deg.data_ptr<float>(), edges, nodes, rows,
             n_radial, channels, gz.data_ptr<float>(), gr.data_ptr<float>(),
             gi.data_ptr<float>(), ws.data_ptr(), static_cast<size_t>(ws.numel()),
-            stream_of(zonal)),
+            stream_of(zonal), reinterpret_cast<const uint32_t*>(flags.data_ptr<int32_t>())),
+        "gie_zonal_scatter_backward");
+  const int64_t word = flags.item<int32_t>();
+  if (word == 0) return {gz, gr, gi};
+  TORCH_CHECK(!(word & BYSJ_FLAG_OUT_OF_RANGE),
+              "destination values must be within the node range");
+  auto [grouped_offsets, order] = csr_view(dst, nodes);
+  check(bysj_gie_zonal_scatter_backward(
+            grad_output.data_ptr<float>(), zonal.data_ptr<float>(), radial.data_ptr<float>(),
+            dst.data_ptr<int64_t>(), grouped_offsets.data_ptr<int64_t>(),
+            opt_ptr<int64_t>(order), radial_slot.data_ptr<int64_t>(),
+            inv_sqrt_deg.data_ptr<float>(), edges, nodes, rows, n_radial, channels,
+            gz.data_ptr<float>(), gr.data_ptr<float>(), gi.data_ptr<float>(), ws.data_ptr(),
+            static_cast<size_t>(ws.numel()), stream_of(zonal)),
         "gie_zonal_scatter_backward");
   return {gz, gr, gi};
 }

@@ -368,6 +368,22 @@ BYSJ_API int bysj_gie_zonal_scatter_forward(const float* zonal, const float* rad
                                    float* out, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/* The same operator with a device gate: when *gate != 0 at kernel time every
+ * kernel returns at once (outputs untouched).  A caller that derives the
+ * destination CSR on the device (bysj_segment_offsets_sorted, whose flags word
+ * is the gate) can launch both without reading the flags back first, and read
+ * them afterwards to recompute through the unsorted path or report a range
+ * error.  No reference counterpart: the pipelining form of
+ * csrc/gie.cpp:148-228's entry. */
+BYSJ_API int bysj_gie_zonal_scatter_forward_gated(const float* zonal, const float* radial,
+                                         const int64_t* offsets, const int64_t* order,
+                                         const int64_t* radial_slot,
+                                         const float* inv_sqrt_deg, int64_t n_edges,
+                                         int64_t n_nodes, int64_t n_rows, int64_t n_radial,
+                                         int64_t channels, float* out, void* workspace,
+                                         size_t workspace_bytes, void* stream,
+                                         const uint32_t* gate);
+
 /* Same operator for the degree-grouped row layout the DPA4 GIE uses: rows
  * r = 0 .. (degrees+1)^2 - 2, row r has degree l = floor(sqrt(r + 1)) and
  * reads radial slot l + slot_base (slot_base = 0 for slots 1..L, -1 for
@@ -416,6 +432,15 @@ BYSJ_API int bysj_gie_zonal_scatter_backward(
     int64_t n_nodes, int64_t n_rows, int64_t n_radial, int64_t channels,
     float* grad_zonal, float* grad_radial, float* grad_inv, void* workspace,
     size_t workspace_bytes, void* stream);
+
+/* Backward with the same device gate as bysj_gie_zonal_scatter_forward_gated. */
+BYSJ_API int bysj_gie_zonal_scatter_backward_gated(
+    const float* grad_out, const float* zonal, const float* radial,
+    const int64_t* dst, const int64_t* offsets, const int64_t* order,
+    const int64_t* radial_slot, const float* inv_sqrt_deg, int64_t n_edges,
+    int64_t n_nodes, int64_t n_rows, int64_t n_radial, int64_t channels,
+    float* grad_zonal, float* grad_radial, float* grad_inv, void* workspace,
+    size_t workspace_bytes, void* stream, const uint32_t* gate);
 
 #ifdef __cplusplus
 } /* extern "C" */
