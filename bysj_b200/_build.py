@@ -55,6 +55,7 @@ CU_SOURCES = [
     "gie.cu",
     "rotate_aggregate.cu",
     "edge_chain.cu",
+    "checks.cu",
 ]
 HEADERS = ["common.cuh", "launch.cuh"]
 

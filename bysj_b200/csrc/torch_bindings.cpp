@@ -163,6 +163,37 @@ std::tuple<Tensor, Tensor> csr_view_launch(const Tensor& dst, int64_t n_nodes) {
   return {offsets, flags};
 }
 
+// Index guard: the BYSJ_INDEX_* word (read back).
+int64_t check_indices(OptTensor offsets, int64_t n_edges, OptTensor order, OptTensor values,
+                      int64_t value_limit) {
+  const Tensor& ref = offsets ? *offsets : (order ? *order : *values);
+  TORCH_CHECK(offsets || order || values, "check_indices needs something to check");
+  TORCH_CHECK(n_edges >= 0, "check_indices: n_edges must be non-negative");
+  if (offsets) {
+    i64(*offsets, "offsets");
+    TORCH_CHECK(offsets->dim() == 1 && offsets->numel() >= 1,
+                "check_indices: offsets must be one-dimensional with at least one entry");
+  }
+  if (order) {
+    i64(*order, "order");
+    TORCH_CHECK(order->numel() == n_edges, "check_indices: order must have n_edges entries");
+  }
+  if (values) i64(*values, "values");
+  same_device(ref, offsets, "offsets");
+  same_device(ref, order, "order");
+  same_device(ref, values, "values");
+  c10::cuda::CUDAGuard guard(ref.device());
+  Tensor error = torch::zeros({1}, ref.options().dtype(torch::kInt32));
+  Tensor ws = workspace(ref, bysj_check_indices_workspace_size(order ? n_edges : 0));
+  const int64_t nodes = offsets ? offsets->numel() - 1 : 0;
+  check(bysj_check_indices(opt_ptr<int64_t>(offsets), nodes, n_edges, opt_ptr<int64_t>(order),
+                           opt_ptr<int64_t>(values), values ? values->numel() : 0, value_limit,
+                           reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>()), ws.data_ptr(),
+                           static_cast<size_t>(ws.numel()), stream_of(ref)),
+        "check_indices");
+  return error.item<int32_t>();
+}
+
 // ---- segment_sum ------------------------------------------------------------
 
 Tensor segment_sum_forward(Tensor src, Tensor offsets, OptTensor edge_scale,
@@ -707,6 +738,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("segment_attention_forward", &segment_attention_forward, py::arg("logit"),
         py::arg("value"), py::arg("offsets"), py::arg("env") = py::none(),
         py::arg("null_logit") = py::none(), py::arg("order") = py::none());
+  m.def("check_indices", &check_indices, py::arg("offsets"), py::arg("n_edges"),
+        py::arg("order") = py::none(), py::arg("values") = py::none(),
+        py::arg("value_limit") = 0);
   m.def("edge_chain", &edge_chain, py::arg("first"), py::arg("second"), py::arg("coefs"),
         py::arg("n_edges"), py::arg("comps"), py::arg("channels"), py::arg("activation"));
   m.def("rotate_back_aggregate_forward", &rotate_back_aggregate_forward, py::arg("x_local"),

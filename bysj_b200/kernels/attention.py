@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import torch
 
+from . import segment as _segment
 from .native import _extension, require_dcu
 from .segment import _validate_order
 
@@ -66,6 +67,8 @@ def segment_attention(logit, value, offsets, env=None, null_logit=None, *, order
     """
     _validate(logit, value, offsets, env, null_logit, order)
     require_dcu(logit, value, offsets, env, null_logit, order)
+    if _segment._should_check(None):
+        _segment.check_indices(offsets, logit.shape[0], order=order, name="segment attention")
     return _extension("segment_attention_forward").segment_attention_forward(
         logit, value, offsets, env, null_logit, order
     )

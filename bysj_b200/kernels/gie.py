@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from . import segment as _segment
 from .native import _extension, require_dcu
 
 
@@ -89,6 +90,10 @@ def zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg):
     """
     _validate(zonal, radial, dst, radial_slot, inv_sqrt_deg)
     require_dcu(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+    if _segment._should_check(None):
+        _segment.check_indices(values=radial_slot, value_limit=radial.shape[1],
+                               name="GIE radial_slot")
+        _segment.check_indices(values=dst, value_limit=inv_sqrt_deg.shape[0], name="GIE dst")
     return _GIEZonalScatterFunction.apply(zonal, radial, dst, radial_slot, inv_sqrt_deg)
 
 

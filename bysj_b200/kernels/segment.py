@@ -233,6 +233,30 @@ def _should_check(explicit):
     return _CHECK_GROUPING if explicit is None else bool(explicit)
 
 
+_INDEX_MESSAGES = (
+    (1, "offsets must be an exclusive prefix sum from 0 to n_edges"),
+    (2, "order must be a permutation of the edge indices"),
+    (4, "index values must be within range"),
+)
+
+
+def check_indices(offsets=None, n_edges=0, *, order=None, values=None, value_limit=0,
+                  name="segment operator") -> None:
+    """Device index guard: raises ``ValueError`` naming every violated invariant.
+
+    The kernels trust their indices; this checks what they trust -- offsets a
+    CSR prefix sum ending at ``n_edges``, ``order`` a permutation of the edges,
+    ``values`` inside ``[0, value_limit)`` -- in one device pass and one flag
+    read back.  Run by the operators when grouping validation is asked for
+    (``check_grouping=True`` or ``DPA4_CHECK_GROUPING=1``).
+    """
+    word = _extension("check_indices").check_indices(offsets, int(n_edges), order, values,
+                                                     int(value_limit))
+    if word:
+        broken = "; ".join(text for bit, text in _INDEX_MESSAGES if word & bit)
+        raise ValueError(f"{name}: {broken}")
+
+
 def _check_csr(dst: torch.Tensor, offsets: torch.Tensor, n_nodes: int, name: str) -> None:
     expected = segment_offsets(dst, n_nodes)
     if not torch.equal(expected, offsets):
@@ -325,9 +349,11 @@ def segment_sum(src, dst, offsets, edge_scale=None, node_scale=None, *, order=No
     the indices; ``edge_scale`` has none (as in the reference).
     """
     n_nodes = _validate_segment_sum(src, dst, offsets, edge_scale, node_scale, order)
-    if _should_check(check_grouping):
-        _check_csr(dst, offsets, n_nodes, "segment sum")
     require_dcu(src, dst, offsets, edge_scale, node_scale, order)
+    if _should_check(check_grouping):
+        check_indices(offsets, src.shape[0], order=order, name="segment sum")
+        if order is None:
+            _check_csr(dst, offsets, n_nodes, "segment sum")
     return _SegmentSumFunction.apply(src, dst, offsets, edge_scale, node_scale, order)
 
 
@@ -336,11 +362,14 @@ def segment_softmax(logit, env, offsets, null_logit=None, *, order=None, check_g
 
     Returns ``alpha`` ``(n_edges, channels)``; with ``null_logit`` also the
     per-channel null mass ``(n_nodes, channels)``.  Edges with a non-positive
-    envelope carry no mass.  ``check_grouping`` is accepted for signature
-    compatibility; the softmax receives no ``dst`` to check against.
+    envelope carry no mass.  With ``check_grouping`` (or
+    ``DPA4_CHECK_GROUPING=1``) the offsets and ``order`` are checked on the
+    device first (the softmax receives no ``dst`` to compare the grouping to).
     """
     _validate_segment_softmax(logit, env, offsets, null_logit, order)
     require_dcu(logit, env, offsets, null_logit, order)
+    if _should_check(check_grouping):
+        check_indices(offsets, logit.shape[0], order=order, name="segment softmax")
     if null_logit is None:
         return _SegmentSoftmaxFunction.apply(logit, env, offsets, order)
     return _SegmentSoftmaxNullFunction.apply(logit, env, offsets, null_logit, order)
@@ -361,6 +390,10 @@ def force_assembly(grad_edge, edge_vec, src, dst, dst_offsets, src_offsets=None,
         src_offsets = offsets if src_offsets is None else src_offsets
     _validate_force_assembly(grad_edge, edge_vec, dst_offsets, src_offsets, src_order)
     require_dcu(grad_edge, edge_vec, dst_offsets, src_offsets, src_order)
+    if _CHECK_GROUPING:
+        check_indices(dst_offsets, grad_edge.shape[0], name="force assembly destination")
+        check_indices(src_offsets, grad_edge.shape[0], order=src_order,
+                      name="force assembly source")
     return _extension("force_assembly").force_assembly(
         grad_edge, edge_vec, dst_offsets, src_offsets, src_order
     )

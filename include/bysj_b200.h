@@ -68,6 +68,29 @@ BYSJ_API const char* bysj_status_string(int status);
 BYSJ_API const char* bysj_last_error(void);
 
 /* ------------------------------------------------------------------------
+ * Index guard (opt-in).  The operators trust their index inputs, as the
+ * reference's native paths do (python/kernels/gie.py:80-81); this pass checks
+ * what they trust and ORs one bit per violated invariant into *error (a device
+ * word the caller zeroes and reads back):
+ *   BYSJ_INDEX_OFFSETS  offsets[0] != 0, offsets[n_nodes] != n_edges, or a
+ *                       decreasing / out-of-range entry   (offsets may be NULL)
+ *   BYSJ_INDEX_ORDER    order[] not a permutation of [0, n_edges)  (NULL: skip)
+ *   BYSJ_INDEX_VALUES   values[0..n_values) outside [0, value_limit) (NULL: skip)
+ * The order check needs bysj_check_indices_workspace_size(n_edges) bytes of
+ * workspace.  No reference counterpart: the stand-in for a bounds-checked
+ * debug build (the reference's opt-in check is the grouping comparison of
+ * python/kernels/segment.py:38-43,182-193).
+ * ------------------------------------------------------------------------ */
+#define BYSJ_INDEX_OFFSETS 1u
+#define BYSJ_INDEX_ORDER 2u
+#define BYSJ_INDEX_VALUES 4u
+BYSJ_API size_t bysj_check_indices_workspace_size(int64_t n_edges);
+BYSJ_API int bysj_check_indices(const int64_t* offsets, int64_t n_nodes, int64_t n_edges,
+                                const int64_t* order, const int64_t* values, int64_t n_values,
+                                int64_t value_limit, uint32_t* error, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * segment_offsets
  * Replaces python/kernels/segment.py:46-57 (bincount + cumsum over dst).
  * ------------------------------------------------------------------------ */
