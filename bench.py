@@ -485,7 +485,8 @@ def _op_zonal(ctx):
     t = time_launches(lambda: _C.gie_zonal_scatter_forward(zonal, radial, g.dst, slot, inv),
                       ctx["iters"])
     return op_line("zonal_scatter", e * (60 + 8 + 256 * 3) + n * (4096 + 4), t, ctx["peak"], e,
-                   {"note": "includes device CSR view of dst (sync for the range flag)"})
+                   {"note": "includes the device CSR view of dst; its flags word is read as soon "
+                            "as the CSR kernel is done, while the operator runs"})
 
 
 def _op_rmsnorm(ctx, dtype):

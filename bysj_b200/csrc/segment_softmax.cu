@@ -19,6 +19,8 @@
 // for C = 4, 8 or 16 with rows in storage order (the attention widths)
 // instead gives each warp whole segments (segment_softmax_whole_kernel): no
 // split, no second pass.
+#include <atomic>
+
 #include "launch.cuh"
 
 namespace bysj {
@@ -44,6 +46,10 @@ struct SmxArgs {
   int64_t* hub_slot;     // whole forward: per partition, the hub segment it left
                          // to segment_softmax_hub_kernel, or -1 (NULL: no hubs)
   int64_t hub_rows;      // segments longer than this are hubs
+  float* hub_stats;      // [parts][2][2*cpad]: (max, sum) of a partition's slice of
+                         // the hub it starts (kind 0) and of the one it continues (1)
+  unsigned long long* hub_flag;  // == epoch when this call met a hub
+  unsigned long long epoch;      // unique per call
 };
 
 // Split segments up to this many edges are written by the piece that
@@ -940,6 +946,99 @@ struct WholeShape {
   static_assert(kBytes % 16 == 0, "stage buffers must stay 16-byte aligned");
 };
 
+// Running (max, sum) per channel of this lane's quad over one staged chunk
+// [lo, hi) (rows and envelopes as lean_stage leaves them).
+template <int LP, bool kEnv, int TT>
+__device__ __forceinline__ void staged_stats(const float4* buf, const float* envs, int64_t lo,
+                                             int64_t hi, int g, int q, float (&m)[4],
+                                             float (&d)[4]) {
+  constexpr int G = WholeShape<LP>::G;
+  const int rows = quad_rows_n<LP, TT>(lo, hi, g);
+  const int lane = g * LP + q;
+  const uint32_t rows_s = smem_addr(buf) + 16u * lane;
+  const uint32_t env_s = smem_addr(envs) + 4u * g;
+  float4 x[TT];
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+    float shift = 0.0f;
+    bool keep = t < rows;
+    if constexpr (kEnv) {
+      const float e = keep ? lds_f32(env_s + 4u * t * G) : 0.0f;
+      keep = keep && e > 0.0f;
+      shift = keep ? 2.0f * __logf(e) : 0.0f;
+    }
+    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (keep) {
+      const float4 raw = lds_f4(rows_s + 16u * t * kWarp);
+      v = make_float4(raw.x + shift, raw.y + shift, raw.z + shift, raw.w + shift);
+    }
+    x[t] = v;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float cm = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) cm = fmaxf(cm, quad_get(x[t], i));
+    const float mn = fmaxf(m[i], cm);
+    float acc = d[i] * shifted_exp(m[i], mn);
+#pragma unroll
+    for (int t = 0; t < TT; ++t) acc += shifted_exp_fast(quad_get(x[t], i), mn);
+    d[i] = acc;
+    m[i] = mn;
+  }
+}
+
+// (max, sum) per channel of rows [lo, hi) of a hub segment, stored as
+// max[C] | sum[C] (C = 4 LP) at `slot` by the lanes of edge group 0.  The
+// rows go through the warp's two stage buffers (cp.async, the next chunk in
+// flight while this one is reduced), as the whole kernel's segments do.
+template <int LP, bool kEnv>
+__device__ __forceinline__ void hub_slice(const SmxArgs& a, int64_t lo, int64_t hi, int g, int q,
+                                          float4* smem, float* slot) {
+  using S = WholeShape<LP>;
+  constexpr int TT = S::T;
+  constexpr int64_t kChunk = S::CHUNK;
+  char* mine = reinterpret_cast<char*>(smem) + (threadIdx.x >> 5) * S::kWarpBytes;
+  float4* const bufs[2] = {reinterpret_cast<float4*>(mine),
+                           reinterpret_cast<float4*>(mine + S::kBytes)};
+  float m[4], d[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
+  lean_stage<LP, kEnv, TT>(a, lo, lo + kChunk < hi ? lo + kChunk : hi, g, q, bufs[0],
+                           reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+  cp_async_commit();
+  int b = 0;
+  #pragma unroll 1
+  for (int64_t base = lo; base < hi; base += kChunk) {
+    const int64_t next = base + kChunk;
+    if (next < hi)
+      lean_stage<LP, kEnv, TT>(a, next, next + kChunk < hi ? next + kChunk : hi, g, q,
+                               bufs[b ^ 1], reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    staged_stats<LP, kEnv, TT>(bufs[b], reinterpret_cast<const float*>(bufs[b] + S::kRowsF4),
+                               base, next < hi ? next : hi, g, q, m, d);
+    __syncwarp();  // every lane is done with bufs[b] before it is refilled
+    b ^= 1;
+  }
+  cp_async_wait<0>();
+  for (int st = LP; st < kWarp; st <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float mo = __shfl_xor_sync(kFull, m[i], st);
+      const float dd = __shfl_xor_sync(kFull, d[i], st);
+      const float mn = fmaxf(m[i], mo);
+      d[i] = d[i] * shifted_exp(m[i], mn) + dd * shifted_exp(mo, mn);
+      m[i] = mn;
+    }
+  }
+  if (g == 0) {
+    reinterpret_cast<float4*>(slot)[q] = make_float4(m[0], m[1], m[2], m[3]);
+    reinterpret_cast<float4*>(slot + 4 * LP)[q] = make_float4(d[0], d[1], d[2], d[3]);
+  }
+}
+
 template <int LP, bool kEnv>
 __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMinBlocks)
     segment_softmax_whole_kernel(SmxArgs a) {
@@ -961,10 +1060,23 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
   const int q = lane % LP;
   const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
   const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
-  // Every partition records the hub segment it leaves to the hub kernel, or
-  // -1 (at most one: a hub is longer than a partition, so its start is the
-  // only segment start in the partition's range).
-  if (a.hub_slot && lane == 0) a.hub_slot[p] = -1;
+  // Every partition records the hub segment it starts, or -1 (at most one: a
+  // hub is longer than a partition, so its start is the only segment start in
+  // the partition's range).  A partition whose range begins inside a hub's
+  // edges computes the (max, sum) of that slice for the hub pass: the
+  // partitions a hub spans share its statistics, as a split segment's
+  // pieces do, and nothing is idle while the hub pass waits.
+  if (a.hub_slot != nullptr) {
+    if (lane == 0) a.hub_slot[p] = -1;
+    if (n0 >= 1) {
+      const int64_t c = n0 - 1;
+      const int64_t clo = __ldg(a.mp.offsets + c), chi = __ldg(a.mp.offsets + c + 1);
+      const int64_t e0 = p * a.mp.ipc - c;  // edge at this partition's first position
+      if (chi - clo > a.hub_rows && e0 < chi)
+        hub_slice<LP, kEnv>(a, e0, e0 + a.mp.ipc < chi ? e0 + a.mp.ipc : chi, g, q, quad_smem,
+                            a.hub_stats + (2 * p + 1) * 2 * a.cpad);
+    }
+  }
   if (n0 >= n1) return;
   char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
   float4* bufs[2] = {reinterpret_cast<float4*>(mine), reinterpret_cast<float4*>(mine + S::kBytes)};
@@ -977,6 +1089,7 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
     lean_stage<LP, kEnv, TT>(a, lo, hi, g, q, bufs[0], reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
   cp_async_commit();
   int b = 0;
+  bool owns_hub = false;
   for (int64_t n = n0; n < n1; ++n) {
     const int64_t nnhi = n + 2 < n1 ? __ldg(off + n + 3) : nhi;
     if (n + 1 < n1 && nhi - hi <= Q::CHUNK)
@@ -992,9 +1105,14 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
       lean_whole<LP, kEnv, TT>(a, n, lo, hi, g, q, bufs[b],
                            reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
     else if (a.hub_slot != nullptr && hi - lo > a.hub_rows) {
-      // a CTA of the hub kernel takes it (the partition index is recomputed
-      // here rather than kept live through the loop)
-      if (lane == 0) a.hub_slot[global_warp()] = n;
+      // the hub pass writes its weights; this partition's slice statistics
+      // are computed after the loop (the partition index is recomputed
+      // rather than kept live through the loop)
+      if (lane == 0) {
+        a.hub_slot[global_warp()] = n;
+        *reinterpret_cast<volatile unsigned long long*>(a.hub_flag) = a.epoch;
+      }
+      owns_hub = true;
     } else
       lean_big<LP, kEnv>(a, n, lo, hi, g, q);
     __syncwarp();  // every lane is done with bufs[b] before it is refilled
@@ -1004,97 +1122,126 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
     b ^= 1;
   }
   cp_async_wait<0>();
-  // This warp's slot is written: the dependent hub pass may be scheduled.
+  if (owns_hub) {  // the slice of the hub from its first row to this partition's end
+    __syncwarp();
+    const int64_t pp = global_warp();
+    const int64_t n = *reinterpret_cast<volatile int64_t*>(a.hub_slot + pp);
+    const int64_t hlo = __ldg(off + n), hhi = __ldg(off + n + 1);
+    const int64_t end = (pp + 1) * a.mp.ipc - n;
+    hub_slice<LP, kEnv>(a, hlo, end < hhi ? end : hhi, g, q, quad_smem,
+                        a.hub_stats + 2 * pp * 2 * a.cpad);
+  }
+  // This warp's slots are written: the dependent hub pass may be scheduled.
   asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // ---- forward, hub segments of the whole kernel -----------------------------
 // A segment longer than hub_rows (and than a partition) would keep one warp
 // of the whole kernel busy for all of its rows (a 100,000-edge hub: 8 ms).
-// The whole kernel leaves it here instead: one CTA of kHubWarps warps per hub
-// (hubs dealt round-robin over kHubCtas CTAs in partition order), warp w
-// walking chunks w, w + kHubWarps, ... for the statistics, which are merged
-// over the warps in warp order through shared memory (deterministic), then
-// for the weights.  Launched as a programmatic dependent of the whole kernel;
-// a frame without hubs reads the partitions' slots and returns.  (A version
-// that spread each hub over every SM with a grid barrier was 1.6-3.5x faster
-// on hubs but cost ~18 us per call without hubs, against ~3 us here.)
+// Instead every partition the hub spans computes the (max, sum) of its slice
+// inside the whole kernel (hub_slice), and this pass -- launched as a
+// programmatic dependent of the whole kernel, one CTA per SM -- merges the
+// slices in partition order (deterministic: the same slices, the same order,
+// every call) and writes the weights, the hub's chunks dealt over every warp
+// of the grid.  Every CTA merges the statistics itself, so no CTA waits on
+// another.  A call without hubs reads one word (the flag the whole kernel sets
+// to this call's epoch when it meets a hub) and returns.
 constexpr int kHubWarps = 16;
-constexpr int kHubCtas = 8;
 constexpr int64_t kHubRows = 4096;
 
 template <int LP, bool kEnv>
 __global__ void __launch_bounds__(kHubWarps * kWarp, 1) segment_softmax_hub_kernel(SmxArgs a) {
   using Q = QuadSmx<LP>;
+  constexpr int C = 4 * LP;
   constexpr int kThreads = kHubWarps * kWarp;
-  __shared__ float s_m[kHubWarps][LP][4];
-  __shared__ float s_d[kHubWarps][LP][4];
-  __shared__ int64_t s_list[kThreads];
-  __shared__ int s_warp_count[kHubWarps];
+  __shared__ float s_m[kHubWarps][C];
+  __shared__ float s_d[kHubWarps][C];
+  __shared__ float s_fm[C], s_fd[C];
+  constexpr int kScan = 8;  // hub slots read per thread per sweep, all in flight
+  __shared__ int64_t s_list[kThreads * kScan];
   __shared__ int s_count;
   const int lane = lane_id();
   const int w = threadIdx.x >> 5;
   const int g = lane / LP;
   const int q = lane % LP;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the whole kernel is complete
-  {
-    bool any = false;
-    for (int64_t p = threadIdx.x; p < a.mp.parts; p += kThreads) any |= a.hub_slot[p] >= 0;
-    if (__syncthreads_count(any) == 0) return;
-  }
-  int seen = 0;  // hubs found in earlier sweeps (the same in every thread)
-  for (int64_t base = 0; base < a.mp.parts; base += kThreads) {
-    const int64_t p = base + threadIdx.x;
-    const int64_t hub = p < a.mp.parts ? a.hub_slot[p] : -1;
-    const unsigned ballot = __ballot_sync(kFull, hub >= 0);
-    if (lane == 0) s_warp_count[w] = __popc(ballot);
+  if (*reinterpret_cast<volatile unsigned long long*>(a.hub_flag) != a.epoch) return;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kHubWarps;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kHubWarps + w;
+  const int64_t stride = 2 * a.cpad;
+  for (int64_t base = 0; base < a.mp.parts; base += kThreads * kScan) {
+    int64_t found[kScan];
+#pragma unroll
+    for (int k = 0; k < kScan; ++k) {
+      const int64_t p = base + k * kThreads + threadIdx.x;
+      found[k] = p < a.mp.parts ? __ldcg(a.hub_slot + p) : -1;
+    }
     if (threadIdx.x == 0) s_count = 0;
     __syncthreads();
-    int before = 0, total = 0;
-    for (int k = 0; k < kHubWarps; ++k) {
-      if (k < w) before += s_warp_count[k];
-      total += s_warp_count[k];
-    }
-    // The k-th hub in partition order goes to CTA k mod gridDim.
-    const int rank = seen + before + __popc(ballot & ((1u << lane) - 1u));
-    if (hub >= 0 && rank % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x))
-      s_list[atomicAdd(&s_count, 1)] = hub;  // list order does not matter: each
-                                             // hub is computed on its own
+#pragma unroll
+    for (int k = 0; k < kScan; ++k)  // each hub is computed on its own: any order
+      if (found[k] >= 0) s_list[atomicAdd(&s_count, 1)] = found[k];
     __syncthreads();
-    const int mine = s_count;
-    for (int k = 0; k < mine; ++k) {
+    const int hubs = s_count;
+    for (int k = 0; k < hubs; ++k) {
       const int64_t n = s_list[k];
       const int64_t lo = __ldg(a.mp.offsets + n), hi = __ldg(a.mp.offsets + n + 1);
-      float m[4], d[4], inv[4];
-      lean_stats<LP, kEnv>(a, lo, hi, static_cast<int64_t>(w) * Q::CHUNK,
-                           static_cast<int64_t>(kHubWarps) * Q::CHUNK, g, q, m, d);
-      if (g == 0) {
+      const int64_t pa = (lo + n) / a.mp.ipc, pb = (hi - 1 + n) / a.mp.ipc;
+      // Slices pa (kind 0), pa+1 .. pb (kind 1): warp w takes the run
+      // [w*per, (w+1)*per) of them, its lanes as R = 32 / C rows of C
+      // channels, row r merging slices r, r + R, ...; the rows are then
+      // merged by a butterfly, whose row 0 is kept, and the warps' results in
+      // warp order.  A fixed pattern for a given slice count: the same bits
+      // every call.
+      constexpr int R = kWarp / C;
+      const int ch = lane % C, r = lane / C;
+      const int64_t count = pb - pa + 1;
+      const int64_t per = (count + kHubWarps - 1) / kHubWarps;
+      const int64_t j1 = (w + 1) * per < count ? (w + 1) * per : count;
+      float mm = -INFINITY, dd = 0.0f;
+#pragma unroll 4
+      for (int64_t j = w * per + r; j < j1; j += R) {
+        const float* slot = a.hub_stats + (2 * (pa + j) + (j == 0 ? 0 : 1)) * stride;
+        const float mo = __ldcg(slot + ch), dk = __ldcg(slot + C + ch);
+        const float mn = fmaxf(mm, mo);
+        dd = dd * shifted_exp(mm, mn) + dk * shifted_exp(mo, mn);
+        mm = mn;
+      }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          s_m[w][q][i] = m[i];
-          s_d[w][q][i] = d[i];
-        }
+      for (int st = C; st < kWarp; st <<= 1) {
+        const float mo = __shfl_xor_sync(kFull, mm, st), dk = __shfl_xor_sync(kFull, dd, st);
+        const float mn = fmaxf(mm, mo);
+        dd = dd * shifted_exp(mm, mn) + dk * shifted_exp(mo, mn);
+        mm = mn;
+      }
+      if (r == 0) {
+        s_m[w][ch] = mm;
+        s_d[w][ch] = dd;
       }
       __syncthreads();
+      if (w == 0 && lane < C) {  // the warps' results, in warp order
+        float fm = -INFINITY, fd = 0.0f;
+        for (int k2 = 0; k2 < kHubWarps; ++k2) {
+          const float mo = s_m[k2][lane], dk = s_d[k2][lane];
+          const float mn = fmaxf(fm, mo);
+          fd = fd * shifted_exp(fm, mn) + dk * shifted_exp(mo, mn);
+          fm = mn;
+        }
+        s_fm[lane] = fm;
+        s_fd[lane] = fd;
+      }
+      __syncthreads();
+      float m[4], d[4], inv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float mm = -INFINITY, dd = 0.0f;
-        for (int k2 = 0; k2 < kHubWarps; ++k2) {  // warp order: deterministic
-          const float mo = s_m[k2][q][i], dk = s_d[k2][q][i];
-          const float mn = fmaxf(mm, mo);
-          dd = dd * shifted_exp(mm, mn) + dk * shifted_exp(mo, mn);
-          mm = mn;
-        }
-        m[i] = mm;
-        d[i] = dd;
+        m[i] = s_fm[4 * q + i];
+        d[i] = s_fd[4 * q + i];
       }
-      lean_norm<LP>(a, n, g, q, w == 0, m, d, inv);
-      lean_emit<LP, kEnv>(a, lo, hi, static_cast<int64_t>(w) * Q::CHUNK,
-                          static_cast<int64_t>(kHubWarps) * Q::CHUNK, g, q, m, inv);
+      lean_norm<LP>(a, n, g, q, gw == 0, m, d, inv);
+      lean_emit<LP, kEnv>(a, lo, hi, gw * Q::CHUNK, warps * Q::CHUNK, g, q, m, inv);
       __syncthreads();  // s_m / s_d are reused by the next hub
     }
-    seen += total;
-    __syncthreads();  // s_warp_count / s_count / s_list are reused by the next sweep
+    __syncthreads();  // s_count / s_list are reused by the next sweep
   }
 }
 
@@ -1573,7 +1720,6 @@ __device__ __forceinline__ void bwd_segment_global(const SmxArgs& a, int64_t n, 
                                                    int64_t hi, int g, int q, bool qok) {
   using Q = QuadSmx<LP>;
   constexpr int64_t kChunk = static_cast<int64_t>(Q::G) * TT;
-  const int64_t C = a.channels;
   float4 al[TT], gr[TT];
   float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
@@ -1675,7 +1821,6 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
                                                    int64_t hi, int g, int q, const char* buf,
                                                    const int64_t* idx = nullptr) {
   using B = BwdStage<LP>;
-  constexpr int C = 4 * LP;
   const int rows = quad_rows_n<LP, TT>(lo, hi, g);
   const int lane = g * LP + q;
   const uint32_t al_s = smem_addr(buf) + 16u * lane;
@@ -2021,6 +2166,8 @@ struct SmxLayout {
   SplitSlots ss{};
   float* final_stats = nullptr;
   int64_t* hub_slot = nullptr;
+  float* hub_stats = nullptr;
+  unsigned long long* hub_flag = nullptr;
   int smem_status = BYSJ_OK;
 };
 
@@ -2045,10 +2192,22 @@ SmxLayout smx_layout(int64_t n_edges, int64_t n_nodes, int64_t channels,
   float* slots = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * 2 * L.cpad);
   int* tickets = carve.take<int>(static_cast<size_t>(L.plan.parts) * L.cfg.tiles + 1);
   L.final_stats = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * L.cpad);
-  if (L.cfg.hub != nullptr) L.hub_slot = carve.take<int64_t>(static_cast<size_t>(L.plan.parts));
+  if (L.cfg.hub != nullptr) {
+    L.hub_slot = carve.take<int64_t>(static_cast<size_t>(L.plan.parts));
+    L.hub_stats = carve.take<float>(static_cast<size_t>(L.plan.parts) * 2 * 2 * L.cpad);
+    L.hub_flag = carve.take<unsigned long long>(1);
+  }
   L.bytes = carve.need;
   L.ss = SplitSlots{slots, tickets, 2 * L.cpad, static_cast<int>(L.cfg.tiles)};
   return L;
+}
+
+// A value per call that the hub flag (left in the workspace by earlier use)
+// is unlikely to hold already; if it does, the hub pass only scans the
+// partitions' hub slots, which the whole kernel always rewrites.
+unsigned long long next_hub_epoch() {
+  static std::atomic<unsigned long long> counter{0x9e3779b97f4a7c15ull};
+  return counter.fetch_add(0x9e3779b97f4a7c15ull, std::memory_order_relaxed);
 }
 
 int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
@@ -2067,6 +2226,9 @@ int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
   a.big_split = L.ss.tickets + L.plan.parts * L.cfg.tiles;
   a.cpad = L.cpad;
   a.hub_slot = L.hub_slot;
+  a.hub_stats = L.hub_stats;
+  a.hub_flag = L.hub_flag;
+  a.epoch = next_hub_epoch();
   // A hub is longer than a partition (so a partition owns at most one) and
   // than kHubRows rows (so short-segment frames never use the hub pass).
   a.hub_rows = L.plan.ipc > kHubRows ? L.plan.ipc : kHubRows;
@@ -2081,7 +2243,7 @@ int smx_run(SmxArgs& a, const SmxLayout& L, int64_t n_edges, int64_t n_nodes,
     // after the whole kernel (the usual frame has no hub, so this launch is
     // all it costs).
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kHubCtas);
+    cfg.gridDim = dim3(static_cast<unsigned>(current_device_info().sm_count));
     cfg.blockDim = dim3(kHubWarps * kWarp);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = s;

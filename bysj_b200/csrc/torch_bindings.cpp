@@ -5,6 +5,7 @@
 // launches on the current torch stream of the inputs' device.  No arithmetic
 // happens here.
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CUDAEvent.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
@@ -162,6 +163,44 @@ std::tuple<Tensor, Tensor> csr_view_launch(const Tensor& dst, int64_t n_nodes) {
         "segment_offsets");
   return {offsets, flags};
 }
+
+// An early read of a device flags word: the 4-byte copy into pinned memory
+// runs on a side stream, ordered after the work queued so far on the current
+// stream (the kernel that writes the word) but not after what is queued next.
+// A caller that launches its gated operator between start() and word() keeps
+// the GPU busy while the host waits only for the small kernel.
+class EarlyFlags {
+ public:
+  explicit EarlyFlags(const Tensor& flags)
+      : flags_(flags),
+        host_(at::empty({1}, flags.options().device(at::kCPU).pinned_memory(true))) {
+    const auto dev = flags.device().index();
+    at::cuda::CUDAStream main = at::cuda::getCurrentCUDAStream(dev);
+    at::cuda::CUDAStream side = at::cuda::getStreamFromPool(false, dev);
+    ready_.record(main);
+    ready_.block(side);
+    C10_CUDA_CHECK(cudaMemcpyAsync(host_.data_ptr(), flags_.data_ptr(), sizeof(int32_t),
+                                   cudaMemcpyDeviceToHost, side.stream()));
+    done_.record(side);
+  }
+  EarlyFlags(const EarlyFlags&) = delete;
+  EarlyFlags& operator=(const EarlyFlags&) = delete;
+  // An exception between start and word() must not free the buffers under
+  // the pending copy.
+  ~EarlyFlags() {
+    if (!read_ && done_.isCreated()) (void)cudaEventSynchronize(done_.event());
+  }
+  int64_t word() {
+    done_.synchronize();
+    read_ = true;
+    return host_.data_ptr<int32_t>()[0];
+  }
+
+ private:
+  Tensor flags_, host_;
+  at::cuda::CUDAEvent ready_, done_;
+  bool read_ = false;
+};
 
 // Index guard: the BYSJ_INDEX_* word (read back).
 int64_t check_indices(OptTensor offsets, int64_t n_edges, OptTensor order, OptTensor values,
@@ -635,11 +674,13 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
   // library launches the degree kernel and the generic one, and each checks
   // the table itself (no read back here).
   // The sorted-path CSR and the operator are queued together, the operator
-  // gated on the CSR flags; the flags are read once both are in flight.  An
+  // gated on the CSR flags; the flags are read as soon as the CSR kernel is
+  // done, while the operator runs (the host does not wait for it).  An
   // unsorted dst (flag set, operator skipped) is then grouped on the device
   // and the operator runs again; a destination out of range is an error.
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_workspace_size(edges, nodes, rows, channels));
   auto [offsets, flags] = csr_view_launch(dst, nodes);
+  EarlyFlags early(flags);
   check(bysj_gie_zonal_scatter_forward_gated(
             zonal.data_ptr<float>(), radial.data_ptr<float>(), offsets.data_ptr<int64_t>(),
             nullptr, radial_slot.data_ptr<int64_t>(), inv_sqrt_deg.data_ptr<float>(), edges,
@@ -647,7 +688,7 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
             static_cast<size_t>(ws.numel()), stream_of(zonal),
             reinterpret_cast<const uint32_t*>(flags.data_ptr<int32_t>())),
         "gie_zonal_scatter_forward");
-  const int64_t word = flags.item<int32_t>();
+  const int64_t word = early.word();
   if (word == 0) return out;
   TORCH_CHECK(!(word & BYSJ_FLAG_OUT_OF_RANGE),
               "destination values must be within the node range");
@@ -679,10 +720,11 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
   Tensor gr = torch::empty_like(radial);
   Tensor gi = torch::empty_like(inv_sqrt_deg);
   if (nodes == 0) return {gz, gr, gi};
-  // As the forward: gated on the sorted-path flags, read once queued.
+  // As the forward: gated on the sorted-path flags, read early.
   Tensor ws = workspace(zonal, bysj_gie_zonal_scatter_backward_workspace_size(edges, nodes, rows,
                                                                               channels));
   auto [offsets, flags] = csr_view_launch(dst, nodes);
+  EarlyFlags early(flags);
   check(bysj_gie_zonal_scatter_backward_gated(
             grad_output.data_ptr<float>(), zonal.data_ptr<float>(), radial.data_ptr<float>(),
             dst.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(), nullptr,
@@ -691,7 +733,7 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
             gi.data_ptr<float>(), ws.data_ptr(), static_cast<size_t>(ws.numel()),
             stream_of(zonal), reinterpret_cast<const uint32_t*>(flags.data_ptr<int32_t>())),
         "gie_zonal_scatter_backward");
-  const int64_t word = flags.item<int32_t>();
+  const int64_t word = early.word();
   if (word == 0) return {gz, gr, gi};
   TORCH_CHECK(!(word & BYSJ_FLAG_OUT_OF_RANGE),
               "destination values must be within the node range");
