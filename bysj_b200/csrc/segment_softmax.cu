@@ -2010,7 +2010,7 @@ __global__ void __launch_bounds__(kBlock)
 using SmxKernel = void (*)(SmxArgs);
 struct SmxConfig {
   SmxKernel main = nullptr, split = nullptr;
-  SmxKernel hub = nullptr;  // whole forward: the CTA-wide pass over hub segments
+  SmxKernel hub = nullptr;  // whole forward: the dependent pass over hub segments
   int64_t tc = 0, tiles = 1;
   size_t main_smem = 0;  // dynamic shared memory of the main launch
   int block = kBlock;    // threads per CTA of the main launch
