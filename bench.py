@@ -904,7 +904,7 @@ def run_ours(args, dist):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clock_info,
-            "gpu_launches": 3 * args.steps * dist.world,
+            "gpu_launches": 2 * args.steps * dist.world,
         }
         if check is not None:
             line["check"] = check
