@@ -5,9 +5,9 @@
 // The reference (python/kernels/segment.py:60-71) runs a stable argsort of
 // the int64 keys plus bincount/cumsum.  Here, all on the device:
 //
-//  1. count: warp-aggregated integer atomics count the edges per key, and
-//     each edge keeps the count its increment found (its slot in the group:
-//     lanes of one warp instruction keep their order, warps do not);
+//  1. count: each tile of edges is counted in a shared-memory hash table of
+//     its keys, then one global atomic per distinct key reserves the tile's
+//     slots; each edge keeps a distinct slot in its group (arrival order);
 //     a three-phase scan turns the counts into offsets;
 //  2. place: order[offsets[key] + slot] = edge, with no atomics;
 //  3. sort each group by edge index, which restores the stable order
@@ -26,42 +26,83 @@ namespace {
 constexpr int kWarpBucket = 256;   // largest group sorted by one warp
 constexpr int kBlockBucket = 4096; // largest group sorted by one CTA in shared memory
 
-__device__ __forceinline__ unsigned lanemask_lt() {
-  return (1u << lane_id()) - 1u;
-}
+// Pass 1: counts[k] = number of edges with key k, and rank[e] = a distinct
+// slot of edge e in its group (arrival order; pass 3 sorts the groups).  A
+// CTA takes tiles of kHashTile consecutive edges and counts each tile in a
+// shared-memory hash table of its keys first: a tile of a dst-sorted
+// neighbour list holds a few hundred distinct sources in ~4096 edges (their
+// key range is wide -- Morton order wraps around a periodic box -- so a
+// window would not do), and the table turns one returning global atomic per
+// edge into one per distinct key per tile.  An edge whose key finds no free
+// slot within kHashProbes probes takes its slot from the global counter
+// directly.  Out-of-range keys are skipped and flagged.
+constexpr int kHashTile = 4096;                 // edges per tile
+constexpr int kHashPer = kHashTile / kBlock;    // edges per thread per tile
+constexpr int kHashSlots = 2048;                // table size (a power of two)
+constexpr int kHashProbes = 32;
+constexpr uint32_t kHashEmpty = 0xffffffffu;    // no key: keys are < 2^31 - 1
+constexpr int kSlotDirect = -1, kSlotSkip = -2;
 
-// Pass 1: counts[k] = number of edges with key k, and rank[e] = the count
-// edge e's increment found (its arrival slot in its group; lanes of one warp
-// instruction that share a key are merged by __match_any_sync and keep lane
-// order).  Out-of-range keys are skipped and flagged.
 __global__ void __launch_bounds__(kBlock)
     group_count_kernel(const int64_t* __restrict__ keys, int64_t n_edges, int64_t n_keys,
                        unsigned* __restrict__ counts, unsigned* __restrict__ rank,
                        uint32_t* flags) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t warp_begin =
-      static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x - lane_id();
+  __shared__ uint32_t s_key[kHashSlots];
+  __shared__ unsigned s_cnt[kHashSlots];
   uint32_t bad = 0;
-  for (int64_t base = warp_begin; base < n_edges; base += stride) {  // warp-uniform
-    const int64_t e = base + lane_id();
-    int64_t k = -1;
-    if (e < n_edges) {
-      k = __ldg(keys + e);
+  for (int64_t tile = static_cast<int64_t>(blockIdx.x) * kHashTile; tile < n_edges;
+       tile += static_cast<int64_t>(gridDim.x) * kHashTile) {
+    for (int i = threadIdx.x; i < kHashSlots; i += kBlock) {
+      s_key[i] = kHashEmpty;
+      s_cnt[i] = 0;
+    }
+    __syncthreads();
+    int slot[kHashPer];
+    unsigned local[kHashPer];
+#pragma unroll
+    for (int j = 0; j < kHashPer; ++j) {
+      const int64_t e = tile + j * kBlock + threadIdx.x;
+      slot[j] = kSlotSkip;
+      local[j] = 0;
+      if (e >= n_edges) continue;
+      const int64_t k = __ldg(keys + e);
       if (k < 0 || k >= n_keys) {
         bad = BYSJ_FLAG_OUT_OF_RANGE;
-        k = -1;
+        continue;
       }
+      const uint32_t key = static_cast<uint32_t>(k);
+      uint32_t h = (key * 0x9e3779b1u) >> (32 - 11);  // 11 bits: kHashSlots
+      slot[j] = kSlotDirect;
+      for (int probe = 0; probe < kHashProbes; ++probe) {
+        const uint32_t old = atomicCAS(s_key + h, kHashEmpty, key);
+        if (old == kHashEmpty || old == key) {
+          slot[j] = static_cast<int>(h);
+          break;
+        }
+        h = (h + 1) & (kHashSlots - 1);
+      }
+      local[j] = slot[j] >= 0 ? atomicAdd(s_cnt + slot[j], 1u) : atomicAdd(counts + k, 1u);
     }
-    const unsigned peers = __match_any_sync(kFull, static_cast<unsigned long long>(k));
-    const int leader = __ffs(peers) - 1;
-    unsigned slot = 0;
-    if (k >= 0 && lane_id() == leader) slot = atomicAdd(counts + k, __popc(peers));
-    slot = __shfl_sync(kFull, slot, leader);
-    if (e < n_edges) rank[e] = slot + __popc(peers & lanemask_lt());
+    __syncthreads();
+    // One global atomic per distinct key of the tile: the tile's base slot.
+    for (int i = threadIdx.x; i < kHashSlots; i += kBlock) {
+      const uint32_t key = s_key[i];
+      if (key != kHashEmpty) s_cnt[i] = atomicAdd(counts + key, s_cnt[i]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kHashPer; ++j) {
+      const int64_t e = tile + j * kBlock + threadIdx.x;
+      if (slot[j] == kSlotSkip) continue;
+      rank[e] = slot[j] >= 0 ? s_cnt[slot[j]] + local[j] : local[j];
+    }
+    __syncthreads();  // the table is reset for the next tile
   }
   bad = __reduce_or_sync(kFull, bad);
   if (bad && lane_id() == 0) atomicOr(flags, bad);
 }
+static_assert(kHashSlots == 1 << 11, "the hash takes the top 11 bits");
+static_assert(kHashTile % kBlock == 0, "whole edges per thread");
 
 // Pass 2 (no atomics): order[offsets[k] + rank[e]] = e.
 template <typename V>
@@ -384,8 +425,8 @@ int bysj_group_by_key(const int64_t* keys, int64_t n_edges, int64_t n_keys, int6
                   "group by key: zero list counts");
   if (st) return st;
   if (n_edges > 0) {
-    group_count_kernel<<<grid_for(n_edges, kBlock, 8), kBlock, 0, s>>>(keys, n_edges, n_keys,
-                                                                      L.counts, L.rank, flags);
+    group_count_kernel<<<grid_for(n_edges, kHashTile, 8), kBlock, 0, s>>>(
+        keys, n_edges, n_keys, L.counts, L.rank, flags);
     st = launch_check("group_count_kernel");
     if (st) return st;
   }

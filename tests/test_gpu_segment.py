@@ -87,12 +87,17 @@ def test_offsets_golden(cuda):
     np.testing.assert_array_equal(off.cpu().numpy(), g["src_offsets"])
 
 
-@pytest.mark.parametrize("case", ["small", "block", "scan", "mixed"])
+@pytest.mark.parametrize("case", ["small", "block", "scan", "mixed", "dense_tiles",
+                                  "many_keys"])
 def test_group_by_source_every_sort_regime(cuda, case):
-    # groups of <= 256 edges (warp sort), 257..4096 (CTA sort), > 4096 (scan)
+    # groups of <= 256 edges (warp sort), 257..4096 (CTA sort), > 4096 (scan);
+    # 65536 and 300000 random keys put more distinct keys in a 4096-edge tile
+    # than the counting pass's shared-memory table holds (its direct-atomic path)
     gen = torch.Generator().manual_seed(len(case))
-    n = {"small": 3000, "block": 40, "scan": 6, "mixed": 500}[case]
-    e = {"small": 200000, "block": 60000, "scan": 60000, "mixed": 120000}[case]
+    n = {"small": 3000, "block": 40, "scan": 6, "mixed": 500, "dense_tiles": 65536,
+         "many_keys": 300000}[case]
+    e = {"small": 200000, "block": 60000, "scan": 60000, "mixed": 120000,
+         "dense_tiles": 500000, "many_keys": 400000}[case]
     src = torch.randint(0, n, (e,), generator=gen)
     if case == "mixed":  # one giant, a few medium, many small and some empty keys
         src[: e // 3] = 7
