@@ -1827,15 +1827,18 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
   const uint32_t gr_s = al_s + 16u * B::kRowsF4;
   const uint32_t env_s = smem_addr(buf) + 32u * B::kRowsF4 + 4u * g;
   float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float4 ah[TT], gh[TT];  // the rows, held for the second pass
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
+    ah[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    gh[t] = ah[t];
     if (t < rows) {
-      const float4 al = lds_f4(al_s + 16u * t * kWarp);
-      const float4 gr = lds_f4(gr_s + 16u * t * kWarp);
-      S[0] = fmaf(al.x, gr.x, S[0]);
-      S[1] = fmaf(al.y, gr.y, S[1]);
-      S[2] = fmaf(al.z, gr.z, S[2]);
-      S[3] = fmaf(al.w, gr.w, S[3]);
+      ah[t] = lds_f4(al_s + 16u * t * kWarp);
+      gh[t] = lds_f4(gr_s + 16u * t * kWarp);
+      S[0] = fmaf(ah[t].x, gh[t].x, S[0]);
+      S[1] = fmaf(ah[t].y, gh[t].y, S[1]);
+      S[2] = fmaf(ah[t].z, gh[t].z, S[2]);
+      S[3] = fmaf(ah[t].w, gh[t].w, S[3]);
     }
   }
 #pragma unroll
@@ -1846,11 +1849,7 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     const bool live = t < rows;
-    float4 al = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gr = al;
-    if (live) {
-      al = lds_f4(al_s + 16u * t * kWarp);
-      gr = lds_f4(gr_s + 16u * t * kWarp);
-    }
+    const float4 al = ah[t], gr = gh[t];
     const float4 gl = make_float4(al.x * (gr.x - S[0]), al.y * (gr.y - S[1]),
                                   al.z * (gr.z - S[2]), al.w * (gr.w - S[3]));
     const int64_t slot = lo + g + static_cast<int64_t>(t) * B::G;
