@@ -1779,6 +1779,7 @@ __global__ void __launch_bounds__(kBlock, 4) segment_softmax_whole_bwd_kernel(Sm
 // than a chunk take the register form.  Four-warp CTAs, 17 KB of buffers per
 // warp at LP = 2 (the width it is used for).
 constexpr int kStagedBwdBlock = 128;
+constexpr int kStagedBwdMinBlocks = 4;
 
 template <int LP>
 struct BwdStage {
@@ -1816,10 +1817,18 @@ __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t 
 
 // TT row slots per lane (<= BwdStage<LP>::T): a segment that fits fewer
 // slots skips the empty ones (they add nothing, so the bits are the same).
-template <int LP, int TT = BwdStage<LP>::T>
+struct NoRefill {
+  __device__ __forceinline__ void operator()() const {}
+};
+
+// The rows (and envelopes) go to registers in the first pass; `refill` runs
+// once the stage buffer has been read (a single-buffer caller stages the next
+// segment into it there, while this one's second pass runs).
+template <int LP, int TT = BwdStage<LP>::T, typename Refill = NoRefill>
 __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, int64_t lo,
                                                    int64_t hi, int g, int q, const char* buf,
-                                                   const int64_t* idx = nullptr) {
+                                                   const int64_t* idx = nullptr,
+                                                   Refill refill = Refill{}) {
   using B = BwdStage<LP>;
   const int rows = quad_rows_n<LP, TT>(lo, hi, g);
   const int lane = g * LP + q;
@@ -1828,19 +1837,26 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
   const uint32_t env_s = smem_addr(buf) + 32u * B::kRowsF4 + 4u * g;
   float S[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   float4 ah[TT], gh[TT];  // the rows, held for the second pass
+  float eh[TT];
+  int64_t ih[TT];
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
     ah[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     gh[t] = ah[t];
+    eh[t] = 1.0f;
+    ih[t] = 0;
     if (t < rows) {
       ah[t] = lds_f4(al_s + 16u * t * kWarp);
       gh[t] = lds_f4(gr_s + 16u * t * kWarp);
+      if (a.env && a.out_env && q == 0) eh[t] = lds_f32(env_s + 4u * t * B::G);
+      if (idx) ih[t] = lds_i64(smem_addr(idx) + 8u * (g + t * B::G));
       S[0] = fmaf(ah[t].x, gh[t].x, S[0]);
       S[1] = fmaf(ah[t].y, gh[t].y, S[1]);
       S[2] = fmaf(ah[t].z, gh[t].z, S[2]);
       S[3] = fmaf(ah[t].w, gh[t].w, S[3]);
     }
   }
+  refill();
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -1853,23 +1869,26 @@ __device__ __forceinline__ void bwd_segment_staged(const SmxArgs& a, int64_t n, 
     const float4 gl = make_float4(al.x * (gr.x - S[0]), al.y * (gr.y - S[1]),
                                   al.z * (gr.z - S[2]), al.w * (gr.w - S[3]));
     const int64_t slot = lo + g + static_cast<int64_t>(t) * B::G;
-    const int64_t e = !live ? 0
-                      : idx ? lds_i64(smem_addr(idx) + 8u * (g + t * B::G))
-                      : a.order ? __ldg(a.order + slot) : slot;
+    const int64_t e = !live ? 0 : idx ? ih[t] : a.order ? __ldg(a.order + slot) : slot;
     if (live) reinterpret_cast<float4*>(a.out)[e * LP + q] = gl;
     if (a.out_env) {
       float rowsum = (gl.x + gl.y) + (gl.z + gl.w);
       if constexpr (LP > 1) rowsum = group_sum(rowsum, LP);
       if (live && q == 0) {
-        const float env = a.env ? lds_f32(env_s + 4u * t * B::G) : 1.0f;
+        const float env = eh[t];
         a.out_env[e] = env > 0.0f ? rowsum * 2.0f / env : 0.0f;
       }
     }
   }
 }
 
+// One stage buffer per warp: segment n's rows are read into registers, the
+// buffer is refilled with segment n+1 at once, and segment n's second pass
+// runs while those copies are in flight.  Half the shared memory of a double
+// buffer, so four CTAs per SM (register-bound) instead of three.
 template <int LP>
-__global__ void __launch_bounds__(kStagedBwdBlock) segment_softmax_staged_bwd_kernel(SmxArgs a) {
+__global__ void __launch_bounds__(kStagedBwdBlock, kStagedBwdMinBlocks)
+    segment_softmax_staged_bwd_kernel(SmxArgs a) {
   using B = BwdStage<LP>;
   extern __shared__ float4 quad_smem[];
   const int64_t p = global_warp();
@@ -1880,34 +1899,35 @@ __global__ void __launch_bounds__(kStagedBwdBlock) segment_softmax_staged_bwd_ke
   const int64_t n0 = a.mp.starts_before(p * a.mp.ipc);
   const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
   if (n0 >= n1) return;
-  char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * B::kWarpBytes;
-  char* bufs[2] = {mine, mine + B::kBytes};
+  char* buf = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * B::kBytes;
   const int64_t* off = a.mp.offsets;
   // Segment n is [lo, hi); the next one ends at nhi.
   int64_t lo = __ldg(off + n0), hi = __ldg(off + n0 + 1);
   int64_t nhi = n0 + 1 < n1 ? __ldg(off + n0 + 2) : hi;
-  if (hi - lo <= B::CHUNK) bwd_stage<LP>(a, lo, hi, g, q, bufs[0]);
+  if (hi - lo <= B::CHUNK) bwd_stage<LP>(a, lo, hi, g, q, buf);
   cp_async_commit();
-  int b = 0;
   for (int64_t n = n0; n < n1; ++n) {
     const int64_t nnhi = n + 2 < n1 ? __ldg(off + n + 3) : nhi;
-    if (n + 1 < n1 && nhi - hi <= B::CHUNK) bwd_stage<LP>(a, hi, nhi, g, q, bufs[b ^ 1]);
-    cp_async_commit();
-    cp_async_wait<1>();  // this segment's copies have landed
+    cp_async_wait<0>();  // this segment's copies have landed
     __syncwarp();
+    const auto refill = [&] {
+      __syncwarp();  // every lane has read the buffer
+      if (n + 1 < n1 && nhi - hi <= B::CHUNK) bwd_stage<LP>(a, hi, nhi, g, q, buf);
+      cp_async_commit();
+    };
     // Segments that fit 3/4 of the chunk take 6 row slots per lane instead
-    // of 8 (C3, H = 8: 63.6 -> 60.7 us, same bits).
-    if (hi - lo <= kBwdShort * B::G)
-      bwd_segment_staged<LP, kBwdShort>(a, n, lo, hi, g, q, bufs[b]);
-    else if (hi - lo <= B::CHUNK)
-      bwd_segment_staged<LP>(a, n, lo, hi, g, q, bufs[b]);
-    else
+    // of 8 (same bits).
+    if (hi - lo <= kBwdShort * B::G) {
+      bwd_segment_staged<LP, kBwdShort>(a, n, lo, hi, g, q, buf, nullptr, refill);
+    } else if (hi - lo <= B::CHUNK) {
+      bwd_segment_staged<LP>(a, n, lo, hi, g, q, buf, nullptr, refill);
+    } else {
+      refill();
       bwd_segment_global<LP, kBwdT>(a, n, lo, hi, g, q, true);
-    __syncwarp();  // every lane is done with bufs[b] before it is refilled
+    }
     lo = hi;
     hi = nhi;
     nhi = nnhi;
-    b ^= 1;
   }
   cp_async_wait<0>();
 }
@@ -2083,7 +2103,7 @@ SmxConfig staged_bwd_make() {
   c.tc = 4 * LP;
   c.tiles = 1;
   c.block = kStagedBwdBlock;
-  c.main_smem = (kStagedBwdBlock / kWarp) * BwdStage<LP>::kWarpBytes;
+  c.main_smem = (kStagedBwdBlock / kWarp) * BwdStage<LP>::kBytes;
   return c;
 }
 
