@@ -653,10 +653,18 @@ __device__ __forceinline__ void lean_stage(const SmxArgs& a, int64_t lo, int64_t
   }
 }
 
-template <int LP, bool kEnv, int TT = QuadSmx<LP>::T>
+// A no-op for the refill hook of the staged segment passes: a caller with a
+// single stage buffer passes a functor that stages the next segment once the
+// buffer has been read into registers.
+struct NoRefill {
+  __device__ __forceinline__ void operator()() const {}
+};
+
+template <int LP, bool kEnv, int TT = QuadSmx<LP>::T, typename Refill = NoRefill>
 __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t lo, int64_t hi,
                                            int g, int q, const float4* buf, const float* envs,
-                                           const int64_t* idx = nullptr) {
+                                           const int64_t* idx = nullptr,
+                                           Refill refill = Refill{}) {
   using Q = QuadSmx<LP>;
   constexpr int C = 4 * LP;
   const int rows = quad_rows_n<LP, TT>(lo, hi, g);
@@ -683,6 +691,7 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
       x[t][1] = add2(pk2(raw.z, raw.w), sh);
     }
   }
+  refill();  // the rows are in registers (an idx buffer is read below: no refill then)
   float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   if (a.xn) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
@@ -929,10 +938,13 @@ __device__ __forceinline__ void lean_big(const SmxArgs& a, int64_t n, int64_t lo
 
 // Rows per lane and CTA shape of the whole kernel: a 128-row chunk at every
 // width (4, 8 or 16 rows per lane at LP = 1, 2, 4), so that a typical segment
-// (~90 edges) fits one chunk without lanes idling over most of it.  LP <= 2:
-// eight-warp CTAs, three per SM (80 registers); LP = 4: 17 KB of buffers per
-// warp, four-warp CTAs.  (At LP = 1, 4 rows per lane measured 1.3x faster
-// than 8.)
+// (~90 edges) fits one chunk without lanes idling over most of it.  One
+// stage buffer per warp (the next segment is staged once this one is in
+// registers), four-warp CTAs; LP <= 2: five per SM (102 registers; C3, H = 8:
+// 37.9 us with a double buffer and three eight-warp CTAs at 80 registers,
+// 35.9 us single-buffered at the same shape, 33.8 us at this one; two or six
+// CTAs per SM measured 37.0 / 35.9 us); LP = 4: three per SM.  (At LP = 1, 4
+// rows per lane measured 1.3x faster than 8.)
 template <int LP>
 struct WholeShape {
   static constexpr int T = LP >= 4 ? 16 : LP == 2 ? 8 : 4;
@@ -940,18 +952,18 @@ struct WholeShape {
   static constexpr int CHUNK = G * T;
   static constexpr int kRowsF4 = T * kWarp;
   static constexpr size_t kBytes = sizeof(float4) * kRowsF4 + sizeof(float) * CHUNK;
-  static constexpr size_t kWarpBytes = 2 * kBytes;
-  static constexpr int kThreads = LP >= 4 ? 128 : kBlock;
-  static constexpr int kMinBlocks = 3;
+  static constexpr size_t kWarpBytes = kBytes;  // one stage buffer per warp
+  static constexpr int kThreads = 128;
+  static constexpr int kMinBlocks = LP >= 4 ? 3 : 5;
   static_assert(kBytes % 16 == 0, "stage buffers must stay 16-byte aligned");
 };
 
 // Running (max, sum) per channel of this lane's quad over one staged chunk
 // [lo, hi) (rows and envelopes as lean_stage leaves them).
-template <int LP, bool kEnv, int TT>
+template <int LP, bool kEnv, int TT, typename Refill = NoRefill>
 __device__ __forceinline__ void staged_stats(const float4* buf, const float* envs, int64_t lo,
                                              int64_t hi, int g, int q, float (&m)[4],
-                                             float (&d)[4]) {
+                                             float (&d)[4], Refill refill = Refill{}) {
   constexpr int G = WholeShape<LP>::G;
   const int rows = quad_rows_n<LP, TT>(lo, hi, g);
   const int lane = g * LP + q;
@@ -974,6 +986,7 @@ __device__ __forceinline__ void staged_stats(const float4* buf, const float* env
     }
     x[t] = v;
   }
+  refill();
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     float cm = -INFINITY;
@@ -990,37 +1003,35 @@ __device__ __forceinline__ void staged_stats(const float4* buf, const float* env
 
 // (max, sum) per channel of rows [lo, hi) of a hub segment, stored as
 // max[C] | sum[C] (C = 4 LP) at `slot` by the lanes of edge group 0.  The
-// rows go through the warp's two stage buffers (cp.async, the next chunk in
-// flight while this one is reduced), as the whole kernel's segments do.
+// rows go through the warp's stage buffer (cp.async; the next chunk is staged
+// as soon as this one is in registers), as the whole kernel's segments do.
 template <int LP, bool kEnv>
 __device__ __forceinline__ void hub_slice(const SmxArgs& a, int64_t lo, int64_t hi, int g, int q,
                                           float4* smem, float* slot) {
   using S = WholeShape<LP>;
   constexpr int TT = S::T;
   constexpr int64_t kChunk = S::CHUNK;
-  char* mine = reinterpret_cast<char*>(smem) + (threadIdx.x >> 5) * S::kWarpBytes;
-  float4* const bufs[2] = {reinterpret_cast<float4*>(mine),
-                           reinterpret_cast<float4*>(mine + S::kBytes)};
+  float4* const buf =
+      reinterpret_cast<float4*>(reinterpret_cast<char*>(smem) + (threadIdx.x >> 5) * S::kWarpBytes);
+  float* const envs = reinterpret_cast<float*>(buf + S::kRowsF4);
   float m[4], d[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) { m[i] = -INFINITY; d[i] = 0.0f; }
-  lean_stage<LP, kEnv, TT>(a, lo, lo + kChunk < hi ? lo + kChunk : hi, g, q, bufs[0],
-                           reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+  lean_stage<LP, kEnv, TT>(a, lo, lo + kChunk < hi ? lo + kChunk : hi, g, q, buf, envs);
   cp_async_commit();
-  int b = 0;
   #pragma unroll 1
   for (int64_t base = lo; base < hi; base += kChunk) {
     const int64_t next = base + kChunk;
-    if (next < hi)
-      lean_stage<LP, kEnv, TT>(a, next, next + kChunk < hi ? next + kChunk : hi, g, q,
-                               bufs[b ^ 1], reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
-    cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<0>();
     __syncwarp();
-    staged_stats<LP, kEnv, TT>(bufs[b], reinterpret_cast<const float*>(bufs[b] + S::kRowsF4),
-                               base, next < hi ? next : hi, g, q, m, d);
-    __syncwarp();  // every lane is done with bufs[b] before it is refilled
-    b ^= 1;
+    const auto refill = [&] {
+      __syncwarp();  // every lane has read the buffer
+      if (next < hi)
+        lean_stage<LP, kEnv, TT>(a, next, next + kChunk < hi ? next + kChunk : hi, g, q, buf,
+                                 envs);
+      cp_async_commit();
+    };
+    staged_stats<LP, kEnv, TT>(buf, envs, base, next < hi ? next : hi, g, q, m, d, refill);
   }
   cp_async_wait<0>();
   for (int st = LP; st < kWarp; st <<= 1) {
@@ -1078,48 +1089,48 @@ __global__ void __launch_bounds__(WholeShape<LP>::kThreads, WholeShape<LP>::kMin
     }
   }
   if (n0 >= n1) return;
-  char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
-  float4* bufs[2] = {reinterpret_cast<float4*>(mine), reinterpret_cast<float4*>(mine + S::kBytes)};
+  float4* const buf = reinterpret_cast<float4*>(reinterpret_cast<char*>(quad_smem) +
+                                                (threadIdx.x >> 5) * S::kWarpBytes);
+  float* const envs = reinterpret_cast<float*>(buf + S::kRowsF4);
   const int64_t* off = a.mp.offsets;
-  // Segment n is [lo, hi); the next one ends at nhi.  Its rows are copied
-  // into the other buffer while this one is computed.
+  // Segment n is [lo, hi); the next one ends at nhi.  One stage buffer per
+  // warp: once segment n's rows are in registers the buffer takes segment
+  // n+1's copies, which land while segment n is computed.
   int64_t lo = __ldg(off + n0), hi = __ldg(off + n0 + 1);
   int64_t nhi = n0 + 1 < n1 ? __ldg(off + n0 + 2) : hi;
-  if (hi - lo <= Q::CHUNK)
-    lean_stage<LP, kEnv, TT>(a, lo, hi, g, q, bufs[0], reinterpret_cast<float*>(bufs[0] + S::kRowsF4));
+  if (hi - lo <= Q::CHUNK) lean_stage<LP, kEnv, TT>(a, lo, hi, g, q, buf, envs);
   cp_async_commit();
-  int b = 0;
   bool owns_hub = false;
   for (int64_t n = n0; n < n1; ++n) {
     const int64_t nnhi = n + 2 < n1 ? __ldg(off + n + 3) : nhi;
-    if (n + 1 < n1 && nhi - hi <= Q::CHUNK)
-      lean_stage<LP, kEnv, TT>(a, hi, nhi, g, q, bufs[b ^ 1],
-                           reinterpret_cast<float*>(bufs[b ^ 1] + S::kRowsF4));
-    cp_async_commit();
-    cp_async_wait<1>();  // this segment's copies have landed
+    cp_async_wait<0>();  // this segment's copies have landed
     __syncwarp();
-    if (hi - lo <= TS * S::G)
-      lean_whole<LP, kEnv, TS>(a, n, lo, hi, g, q, bufs[b],
-                           reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
-    else if (hi - lo <= Q::CHUNK)
-      lean_whole<LP, kEnv, TT>(a, n, lo, hi, g, q, bufs[b],
-                           reinterpret_cast<float*>(bufs[b] + S::kRowsF4));
-    else if (a.hub_slot != nullptr && hi - lo > a.hub_rows) {
+    const auto refill = [&] {
+      __syncwarp();  // every lane has read the buffer
+      if (n + 1 < n1 && nhi - hi <= Q::CHUNK) lean_stage<LP, kEnv, TT>(a, hi, nhi, g, q, buf, envs);
+      cp_async_commit();
+    };
+    if (hi - lo <= TS * S::G) {
+      lean_whole<LP, kEnv, TS>(a, n, lo, hi, g, q, buf, envs, nullptr, refill);
+    } else if (hi - lo <= Q::CHUNK) {
+      lean_whole<LP, kEnv, TT>(a, n, lo, hi, g, q, buf, envs, nullptr, refill);
+    } else if (a.hub_slot != nullptr && hi - lo > a.hub_rows) {
       // the hub pass writes its weights; this partition's slice statistics
       // are computed after the loop (the partition index is recomputed
       // rather than kept live through the loop)
+      refill();
       if (lane == 0) {
         a.hub_slot[global_warp()] = n;
         *reinterpret_cast<volatile unsigned long long*>(a.hub_flag) = a.epoch;
       }
       owns_hub = true;
-    } else
+    } else {
+      refill();
       lean_big<LP, kEnv>(a, n, lo, hi, g, q);
-    __syncwarp();  // every lane is done with bufs[b] before it is refilled
+    }
     lo = hi;
     hi = nhi;
     nhi = nnhi;
-    b ^= 1;
   }
   cp_async_wait<0>();
   if (owns_hub) {  // the slice of the hub from its first row to this partition's end
@@ -1817,10 +1828,6 @@ __device__ __forceinline__ void bwd_stage(const SmxArgs& a, int64_t lo, int64_t 
 
 // TT row slots per lane (<= BwdStage<LP>::T): a segment that fits fewer
 // slots skips the empty ones (they add nothing, so the bits are the same).
-struct NoRefill {
-  __device__ __forceinline__ void operator()() const {}
-};
-
 // The rows (and envelopes) go to registers in the first pass; `refill` runs
 // once the stage buffer has been read (a single-buffer caller stages the next
 // segment into it there, while this one's second pass runs).
