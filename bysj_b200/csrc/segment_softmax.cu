@@ -691,7 +691,7 @@ __device__ __forceinline__ void lean_whole(const SmxArgs& a, int64_t n, int64_t 
       x[t][1] = add2(pk2(raw.z, raw.w), sh);
     }
   }
-  refill();  // the rows are in registers (an idx buffer is read below: no refill then)
+  refill();  // the rows are in registers (the index buffer is read below)
   float nl[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   if (a.xn) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(a.xn + n * C) + q);
@@ -1266,6 +1266,7 @@ __global__ void __launch_bounds__(kHubWarps * kWarp, 1) segment_softmax_hub_kern
 // buffer.  Outputs go to the staged storage rows.  Arithmetic as the whole
 // kernel; segments longer than a chunk take lean_big (global, through order).
 constexpr int kGatherBlock = 128;  // four-warp CTAs
+constexpr int kGatherMinBlocks = 5;
 
 template <int LP>
 struct GatherStage {
@@ -1273,12 +1274,13 @@ struct GatherStage {
   static constexpr size_t kRows = sizeof(float4) * Q::T * kWarp;
   static constexpr size_t kEnv = sizeof(float) * Q::CHUNK;
   static constexpr size_t kIdx = sizeof(int64_t) * Q::CHUNK;
-  static constexpr size_t kWarpBytes = 2 * (kRows + kEnv) + 3 * kIdx;
+  static constexpr size_t kWarpBytes = (kRows + kEnv) + 3 * kIdx;  // one row buffer
   static_assert((kRows + kEnv) % 16 == 0 && kIdx % 16 == 0, "16-byte aligned buffers");
 };
 
 template <int LP, bool kEnv>
-__global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(SmxArgs a) {
+__global__ void __launch_bounds__(kGatherBlock, kGatherMinBlocks)
+    segment_softmax_gather_kernel(SmxArgs a) {
   using Q = QuadSmx<LP>;
   using S = GatherStage<LP>;
   // Row slots per lane for a segment within 7/8 (C = 8) or 3/8 (C = 4) of
@@ -1295,12 +1297,10 @@ __global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(Sm
   const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
   if (n0 >= n1) return;
   char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
-  auto rows_buf = [&](int b) { return reinterpret_cast<float4*>(mine + b * (S::kRows + S::kEnv)); };
-  auto env_buf = [&](int b) {
-    return reinterpret_cast<float*>(mine + b * (S::kRows + S::kEnv) + S::kRows);
-  };
+  float4* const rbuf = reinterpret_cast<float4*>(mine);
+  float* const ebuf = reinterpret_cast<float*>(mine + S::kRows);
   auto idx_buf = [&](int k) {
-    return reinterpret_cast<int64_t*>(mine + 2 * (S::kRows + S::kEnv) + k * S::kIdx);
+    return reinterpret_cast<int64_t*>(mine + (S::kRows + S::kEnv) + k * S::kIdx);
   };
   // order[lo..hi) -> index buffer k (if the segment fits a chunk).
   auto stage_idx = [&](int64_t lo, int64_t hi, int k) {
@@ -1309,11 +1309,11 @@ __global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(Sm
     for (int64_t i = lane; i < hi - lo; i += kWarp) cp_async8(dst + i, a.order + lo + i);
   };
   // Rows (and envelopes) of a staged segment, gathered by its staged indices.
-  auto stage_rows = [&](int64_t lo, int64_t hi, int b, int k) {
+  auto stage_rows = [&](int64_t lo, int64_t hi, int k) {
     if (hi - lo > Q::CHUNK) return;
     const int rows = quad_rows<LP>(lo, hi, g);
     const int64_t* idx = idx_buf(k);
-    float4* rb = rows_buf(b);
+    float4* rb = rbuf;
 #pragma unroll
     for (int t = 0; t < Q::T; ++t)
       if (t < rows) {
@@ -1321,7 +1321,7 @@ __global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(Sm
         cp_async16(rb + t * kWarp + lane, a.x + e * (4 * LP) + 4 * q);
       }
     if constexpr (kEnv) {
-      float* eb = env_buf(b);
+      float* eb = ebuf;
 #pragma unroll
       for (int j = 0; j < Q::T / LP; ++j) {
         const int t = q + j * LP;
@@ -1339,10 +1339,9 @@ __global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(Sm
   cp_async_wait<0>();
   __syncwarp();
   if (n0 + 1 < n1) stage_idx(o1, o2, 1);
-  stage_rows(o0, o1, 0, 0);
+  stage_rows(o0, o1, 0);
   cp_async_commit();
-  int kb = 0;  // index buffer of segment n; rows buffer is (n - n0) & 1
-  int rb = 0;
+  int kb = 0;  // index buffer of segment n
   for (int64_t n = n0; n < n1; ++n) {
     cp_async_wait<0>();  // segment n's rows, segment n+1's indices
     __syncwarp();
@@ -1350,22 +1349,28 @@ __global__ void __launch_bounds__(kGatherBlock) segment_softmax_gather_kernel(Sm
     const int k1 = kb == 2 ? 0 : kb + 1;
     const int k2 = k1 == 2 ? 0 : k1 + 1;
     if (n + 2 < n1) stage_idx(o2, o3, k2);
-    if (n + 1 < n1) stage_rows(o1, o2, rb ^ 1, k1);
     cp_async_commit();
-    if (o1 - o0 <= kGatherShort * Q::G)
-      lean_whole<LP, kEnv, kGatherShort>(a, n, o0, o1, g, q, rows_buf(rb), env_buf(rb),
-                                         idx_buf(kb));
-    else if (o1 - o0 <= Q::CHUNK)
-      lean_whole<LP, kEnv>(a, n, o0, o1, g, q, rows_buf(rb), env_buf(rb), idx_buf(kb));
-    else
+    // One row buffer: segment n+1's rows are gathered into it as soon as
+    // segment n's are in registers.
+    const auto refill = [&] {
+      __syncwarp();  // every lane has read the row buffer
+      if (n + 1 < n1) stage_rows(o1, o2, k1);
+      cp_async_commit();
+    };
+    if (o1 - o0 <= kGatherShort * Q::G) {
+      lean_whole<LP, kEnv, kGatherShort>(a, n, o0, o1, g, q, rbuf, ebuf, idx_buf(kb), refill);
+    } else if (o1 - o0 <= Q::CHUNK) {
+      lean_whole<LP, kEnv>(a, n, o0, o1, g, q, rbuf, ebuf, idx_buf(kb), refill);
+    } else {
+      refill();
       lean_big<LP, kEnv>(a, n, o0, o1, g, q);
-    __syncwarp();  // buffers of segment n are free for segment n+2 / n+3
+    }
+    __syncwarp();  // segment n's index buffer is free for segment n+3
     o0 = o1;
     o1 = o2;
     o2 = o3;
     o3 = o4;
     kb = k1;
-    rb ^= 1;
   }
   cp_async_wait<0>();
 }
@@ -1947,11 +1952,11 @@ template <int LP>
 struct GatherBwdStage {
   using B = BwdStage<LP>;
   static constexpr size_t kIdx = sizeof(int64_t) * B::CHUNK;
-  static constexpr size_t kWarpBytes = B::kWarpBytes + 3 * kIdx;
+  static constexpr size_t kWarpBytes = B::kBytes + 3 * kIdx;  // one row buffer
 };
 
 template <int LP>
-__global__ void __launch_bounds__(kStagedBwdBlock)
+__global__ void __launch_bounds__(kStagedBwdBlock, 3)
     segment_softmax_gather_bwd_kernel(SmxArgs a) {
   using B = BwdStage<LP>;
   using S = GatherBwdStage<LP>;
@@ -1965,9 +1970,9 @@ __global__ void __launch_bounds__(kStagedBwdBlock)
   const int64_t n1 = a.mp.starts_before((p + 1) * a.mp.ipc);
   if (n0 >= n1) return;
   char* mine = reinterpret_cast<char*>(quad_smem) + (threadIdx.x >> 5) * S::kWarpBytes;
-  char* bufs[2] = {mine, mine + B::kBytes};
+  char* const buf = mine;
   auto idx_buf = [&](int k) {
-    return reinterpret_cast<int64_t*>(mine + B::kWarpBytes + k * S::kIdx);
+    return reinterpret_cast<int64_t*>(mine + B::kBytes + k * S::kIdx);
   };
   auto stage_idx = [&](int64_t lo, int64_t hi, int k) {
     if (hi - lo > B::CHUNK) return;
@@ -1983,9 +1988,9 @@ __global__ void __launch_bounds__(kStagedBwdBlock)
   cp_async_wait<0>();
   __syncwarp();
   if (n0 + 1 < n1) stage_idx(o1, o2, 1);
-  if (o1 - o0 <= B::CHUNK) bwd_stage<LP>(a, o0, o1, g, q, bufs[0], idx_buf(0));
+  if (o1 - o0 <= B::CHUNK) bwd_stage<LP>(a, o0, o1, g, q, buf, idx_buf(0));
   cp_async_commit();
-  int kb = 0, rb = 0;
+  int kb = 0;
   for (int64_t n = n0; n < n1; ++n) {
     cp_async_wait<0>();  // segment n's rows, segment n+1's indices
     __syncwarp();
@@ -1993,21 +1998,28 @@ __global__ void __launch_bounds__(kStagedBwdBlock)
     const int k1 = kb == 2 ? 0 : kb + 1;
     const int k2 = k1 == 2 ? 0 : k1 + 1;
     if (n + 2 < n1) stage_idx(o2, o3, k2);
-    if (n + 1 < n1 && o2 - o1 <= B::CHUNK) bwd_stage<LP>(a, o1, o2, g, q, bufs[rb ^ 1], idx_buf(k1));
     cp_async_commit();
-    if (o1 - o0 <= kBwdShort * B::G)
-      bwd_segment_staged<LP, kBwdShort>(a, n, o0, o1, g, q, bufs[rb], idx_buf(kb));
-    else if (o1 - o0 <= B::CHUNK)
-      bwd_segment_staged<LP>(a, n, o0, o1, g, q, bufs[rb], idx_buf(kb));
-    else
+    // One row buffer: segment n+1's rows are gathered into it as soon as
+    // segment n's are in registers.
+    const auto refill = [&] {
+      __syncwarp();  // every lane has read the row buffer
+      if (n + 1 < n1 && o2 - o1 <= B::CHUNK) bwd_stage<LP>(a, o1, o2, g, q, buf, idx_buf(k1));
+      cp_async_commit();
+    };
+    if (o1 - o0 <= kBwdShort * B::G) {
+      bwd_segment_staged<LP, kBwdShort>(a, n, o0, o1, g, q, buf, idx_buf(kb), refill);
+    } else if (o1 - o0 <= B::CHUNK) {
+      bwd_segment_staged<LP>(a, n, o0, o1, g, q, buf, idx_buf(kb), refill);
+    } else {
+      refill();
       bwd_segment_global<LP, kBwdT>(a, n, o0, o1, g, q, true);
-    __syncwarp();  // buffers of segment n are free for segments n+2 / n+3
+    }
+    __syncwarp();  // segment n's index buffer is free for segment n+3
     o0 = o1;
     o1 = o2;
     o2 = o3;
     o3 = o4;
     kb = k1;
-    rb ^= 1;
   }
   cp_async_wait<0>();
 }
