@@ -388,6 +388,18 @@ def test_segment_softmax_row_slot_boundaries(cuda, heads):
     ap, np0 = K.segment_softmax(lp.cuda(), ep.cuda(), off, null.cuda(), order=perm.cuda())
     torch.testing.assert_close(ap[perm.cuda()].cpu(), wa, rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(np0.cpu(), wn, rtol=1e-5, atol=1e-6)
+    # and the backward in that order (the gather kernel at H = 8) against the
+    # storage-order backward of the same rows
+    ext = __import__("bysj_b200._C", fromlist=["_C"])
+    a, n0 = a.detach(), n0.detach()
+    plain = ext.segment_softmax_backward(a, ua, ev.detach(), off, n0, un)
+    pa, pu, pe = (torch.empty_like(t) for t in (a, ua, ev))
+    pa[perm.cuda()], pu[perm.cuda()], pe[perm.cuda()] = a, ua, ev.detach()
+    gl_p, gnl_p, genv_p = ext.segment_softmax_backward(pa, pu, pe, off, n0, un,
+                                                       order=perm.cuda())
+    torch.testing.assert_close(gl_p[perm.cuda()], plain[0], rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(gnl_p, plain[1], rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(genv_p[perm.cuda()], plain[2], rtol=1e-5, atol=1e-5)
 
 
 def test_segment_softmax_all_masked_segment_is_zero(cuda):
