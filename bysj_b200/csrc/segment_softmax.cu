@@ -1259,12 +1259,15 @@ __global__ void __launch_bounds__(kHubWarps * kWarp, 1) segment_softmax_hub_kern
 // ---- forward, whole segments in a permuted storage order (C = 4 or 8) -----
 // The rows of segment n sit at storage rows order[lo..hi): a gather.  A lane
 // that had to load order[slot] before issuing its row copy would wait a full
-// memory round trip; so the warp runs three stages: while it computes segment
-// n from shared memory, segment n+1's rows and envelopes are gathered into
-// its other row buffer (cp.async, indices read from shared memory), and
-// segment n+2's contiguous order[lo..hi) slice is copied into the third index
-// buffer.  Outputs go to the staged storage rows.  Arithmetic as the whole
-// kernel; segments longer than a chunk take lean_big (global, through order).
+// memory round trip; so the warp runs three stages: segment n+2's contiguous
+// order[lo..hi) slice is copied into one of three index buffers, and as soon
+// as segment n's rows are in registers, segment n+1's rows and envelopes are
+// gathered into the warp's one row buffer (cp.async, indices read from
+// shared memory) while segment n is computed.  Outputs go to the staged
+// storage rows.  Arithmetic as the whole kernel; segments longer than a
+// chunk take lean_big (global, through order).  One row buffer per warp:
+// five four-warp CTAs per SM (C3 permuted, H = 8: 78.0 -> 75.1 us against
+// two row buffers).
 constexpr int kGatherBlock = 128;  // four-warp CTAs
 constexpr int kGatherMinBlocks = 5;
 
@@ -1787,13 +1790,14 @@ __global__ void __launch_bounds__(kBlock, 4) segment_softmax_whole_bwd_kernel(Sm
 }
 
 // Backward for C = 4 LP exactly (LP <= 2) with shared-memory staging, as the
-// forward whole kernel: while a warp computes one segment from shared memory
-// (S from one pass over the staged alpha and grad_alpha rows, grad_logit and
-// grad_env from a second), the next segment's rows and envelopes are copied
-// into its other buffer (cp.async).  The rows of a lane are summed in the same
-// order as in the register form, so both give the same bits.  Segments longer
-// than a chunk take the register form.  Four-warp CTAs, 17 KB of buffers per
-// warp at LP = 2 (the width it is used for).
+// forward whole kernel: a segment's alpha, grad_alpha and envelope rows are
+// staged (cp.async), the first pass reads them into registers (S), the warp's
+// one stage buffer is refilled with the next segment at once, and the second
+// pass (grad_logit, grad_env) runs from registers while those copies land.
+// The rows of a lane are summed in the same order as in the register form,
+// so both give the same bits.  Segments longer than a chunk take the
+// register form.  Four-warp CTAs, 8.7 KB of buffer per warp at LP = 2 (the
+// width it is used for), four CTAs per SM.
 constexpr int kStagedBwdBlock = 128;
 constexpr int kStagedBwdMinBlocks = 4;
 
@@ -1946,8 +1950,9 @@ __global__ void __launch_bounds__(kStagedBwdBlock, kStagedBwdMinBlocks)
 
 // Staged backward with a permuted storage order (C = 8): the three-stage
 // pipeline of the forward gather kernel (order slice two segments ahead,
-// gathered alpha / grad_alpha / envelope rows one segment ahead, outputs
-// scattered through the staged indices).
+// gathered alpha / grad_alpha / envelope rows one segment ahead in the
+// warp's one row buffer, refilled once the first pass has the rows in
+// registers; outputs scattered through the staged indices).
 template <int LP>
 struct GatherBwdStage {
   using B = BwdStage<LP>;
