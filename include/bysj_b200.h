@@ -236,7 +236,7 @@ BYSJ_API int bysj_segment_attention_forward(const float* logit, const void* valu
  * capped so the split-segment slots fit; a value row (components * channels)
  * too wide for even one partition is rejected with BYSJ_ERR_TOO_LARGE.
  * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.  All calls
+ * device current) and keeps it for the device's CUDA context.  All calls
  * on a device share the array and it keeps the last call's contents (each
  * call zeroes, on its own stream, the counters that must start at zero):
  * calls that overlap on the GPU, e.g. on two streams at once, race and must
