@@ -52,13 +52,13 @@ struct AttnShape {
                            : (NV * VEC >= 16) ? 2
                            : (8 / NV < 1 ? 1 : 8 / NV);
   static constexpr int kMinBlocks = (NV * VEC >= 32) ? 2 : 3;
-  // bf16 rows with 16-byte vectors: the rows of the edges `kAhead` slots
-  // ahead (the next loop step) are prefetched into L2 by one bulk request
-  // each, so that two steps of row loads are in flight without more
-  // registers (C3 bf16: 856 -> 799 us).  fp32 rows already keep enough
-  // bytes in flight (twice the bytes per edge); prefetching them only
-  // competes for L2 there.
-  static constexpr int kAhead = (sizeof(T) == 2 && VEC * sizeof(T) == 16) ? 2 : 0;
+  // 2 KB rows with 16-byte vectors (bf16 [16, 64], fp32 [16, 32]): the rows
+  // of the edges `kAhead` slots ahead (the next loop step) are prefetched
+  // into L2 by one bulk request each, so that two steps of row loads are in
+  // flight without more registers (C3 bf16: 856 -> 799 us; fp32 at C = 32:
+  // 801 -> 769 us).  4 KB fp32 rows already keep enough bytes in flight;
+  // prefetching them only competes for L2 there.
+  static constexpr int kAhead = (VEC * sizeof(T) == 16 && kWarp * NV * VEC * sizeof(T) == 2048) ? 2 : 0;
 };
 
 // Per-head maximum and denominator over slots [lo, hi).  Whole segments
