@@ -32,6 +32,8 @@ segment sum) producing [N, 8, 16, 8].  The metric is edges/s.
 * ``--mode chain``: 64 independent frames of the full chain (offsets ->
   RMSNorm -> fused attention -> zonal scatter -> source grouping -> force
   assembly, fp32, C = 32) sharded over the ranks; frames/s ("strong").
+  Each rank alternates its frames over two CUDA streams and interleaves
+  their stages (``--chain-streams 1`` runs them one after another).
 * ``--mode partition``: one 500k-atom box split by destination ranges over
   the ranks (strong scaling; force partials reduce-scattered over NCCL).
 
@@ -85,6 +87,8 @@ def parse_args():
                         "box split by destination-atom ranges, force partials reduce-scattered")
     p.add_argument("--chain-frames", type=int, default=64,
                    help="frames of the job in --mode chain")
+    p.add_argument("--chain-streams", type=int, default=2,
+                   help="CUDA streams per rank that --mode chain alternates frames over")
     p.add_argument("--partition-atoms", type=int, default=500_000,
                    help="atoms of the box used by --mode partition")
     return p.parse_args()
@@ -956,6 +960,65 @@ def chain_frame(f):
     return h, agg, z, force, virial
 
 
+# The same calls in stages, for the two-stream pipeline of run_chain: the
+# read-backs of the public API (the offsets flags, the GIE CSR view's flags,
+# the grouping range flag) wait on their own stream only, so a frame's wait
+# overlaps the other stream's kernels.
+def chain_offsets(f, st):
+    from bysj_b200 import kernels as K
+
+    st["offsets"] = K.segment_offsets(f["g"].dst, f["n"])
+
+
+def chain_node_ops(f, st):
+    from bysj_b200 import kernels as K
+
+    st["h"] = K.rmsnorm(f["x"], f["scale"], 1.0e-6)
+    st["agg"] = K.segment_attention(f["logit"], f["value"], st["offsets"])
+
+
+def chain_zonal(f, st):
+    from bysj_b200 import kernels as K
+
+    g = f["g"]
+    st["z"] = K.zonal_scatter(f["zonal"], f["radial"], g.dst, f["slot"], f["inv"])
+
+
+def chain_forces(f, st):
+    from bysj_b200 import kernels as K
+
+    g = f["g"]
+    order, soff = K.group_by_source(g.src, f["n"])
+    st["force"] = K.force_assembly(f["grad"], g.unit, g.src, g.dst, st["offsets"], soff, order)
+
+
+def chain_pipelined(frames, streams):
+    """Frames on alternating streams, their stages interleaved so that every
+    host wait has the other stream's kernels queued: offsets and node
+    operators of frame i, then the grouping and forces of frame i-1, then the
+    GIE of frame i."""
+    main = torch.cuda.current_stream()
+    for s in streams:
+        s.wait_stream(main)
+    pending = None
+    for i, f in enumerate(frames):
+        s, st = streams[i % len(streams)], {}
+        with torch.cuda.stream(s):
+            chain_offsets(f, st)
+            chain_node_ops(f, st)
+        if pending is not None:
+            with torch.cuda.stream(pending[0]):
+                chain_forces(pending[1], pending[2])
+        with torch.cuda.stream(s):
+            chain_zonal(f, st)
+        pending = (s, f, st)
+    if pending is not None:
+        with torch.cuda.stream(pending[0]):
+            chain_forces(pending[1], pending[2])
+    for s in streams:
+        main.wait_stream(s)
+
+
 def chain_bytes(e, n, c=CHAIN_CHANNELS):
     """Algorithmic bytes of one chain frame (each input read once, each output
     written once, per operator)."""
@@ -1002,9 +1065,14 @@ def run_chain(args, dist):
         seed = args.seed + 1000 * dist.rank + 97 * k
         sets.append(chain_inputs(W.c3_box(device=device, seed=seed), seed + 5, device))
 
+    streams = [torch.cuda.Stream(device=device) for _ in range(max(1, args.chain_streams))]
+
     def step():
-        for i, _ in enumerate(frames):
-            chain_frame(sets[i % 2])
+        if len(streams) == 1:
+            for i, _ in enumerate(frames):
+                chain_frame(sets[i % 2])
+        else:
+            chain_pipelined([sets[i % 2] for i, _ in enumerate(frames)], streams)
 
     for _ in range(args.warmup):
         step()
@@ -1043,6 +1111,9 @@ def run_chain(args, dist):
                        "frames_per_step": frames_total, "n_atoms": n,
                        "n_edges_per_frame": int(e_mean), "channels": CHAIN_CHANNELS,
                        "parallelism": f"frame-sharded x{dist.world} (no collective)",
+                       "streams": (f"{len(streams)} CUDA streams per rank, consecutive "
+                                   "frames alternating, their stages interleaved"
+                                   if len(streams) > 1 else "one stream"),
                        "l2": "each frame's inputs (~5.9 GB) exceed L2; no flush"},
             "edges_per_s": frames_total * e_mean / step_max,
             "ms_per_frame": frame_s * 1e3,
