@@ -192,9 +192,23 @@ __global__ void __launch_bounds__(kBlock, 2) gie_fwd_kernel(GieArgs a) {
 // the row -> slot choice is resolved at compile time.  The R zonal
 // coefficients of an edge are the same for its LPE lanes: each warp stages
 // them for 32 edges at a time in shared memory with coalesced loads, and the
-// lanes read them back as broadcasts.  With L = 3 the 15 x 4 accumulators
-// take 60 registers, so two CTAs per SM (also for L = 2); three for L = 1.
+// lanes read them back as broadcasts.  The radial quads go through a ring of
+// kFwdStages step buffers in shared memory (cp.async): step j (EG edges, one
+// per edge group) is computed while steps j+1 .. j+kFwdAhead are in flight,
+// so the loads of several steps overlap without registers for them (C3 op
+// with its CSR view, C = 32: 257 -> 231 us, C = 64: 362 -> 346 us; the
+// register form kept two edges per lane in flight and was latency-bound, 8
+// long-scoreboard stalls per issued instruction).  With
+// L = 3 the 15 x 4 accumulators take 60 registers, so two CTAs per SM (also
+// for L = 2); three for L = 1.
 constexpr int kZonalChunk = 32;  // edges whose zonal rows a warp stages at once
+constexpr int kFwdStages = 4;    // radial step buffers per warp
+constexpr int kFwdAhead = kFwdStages - 1;
+
+template <int L>
+constexpr size_t gie_fwd_smem_bytes() {
+  return static_cast<size_t>(kWarpsPerBlock) * kFwdStages * kWarp * L * sizeof(float4);
+}
 
 template <int LPE, int L>
 __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
@@ -202,11 +216,14 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
   if (a.gate != nullptr && *a.gate != 0) return;  // the CSR view was not built
   constexpr int R = (L + 1) * (L + 1) - 1;
   constexpr int EG = kWarp / LPE;
+  constexpr int kStepQuads = kWarp * L;  // EG edges x L degrees x LPE lanes
   __shared__ float zstage[kWarpsPerBlock][kZonalChunk * R];
+  extern __shared__ float4 gie_fwd_ring[];
   const int64_t p = global_warp();
   if (p >= a.mp.parts) return;
   if (slot_base == kSlotBaseOnDevice && !degree_table(a.slot, L, a.n_radial, slot_base)) return;
   float* zb = zstage[threadIdx.x >> 5];
+  float4* ring = gie_fwd_ring + (threadIdx.x >> 5) * kFwdStages * kStepQuads;
   const int lane = lane_id();
   const int eg = lane / LPE;
   const int c4 = lane % LPE;
@@ -221,6 +238,25 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[r][i] = 0.0f;
+    // The radial quads of the step whose first edge is `base` into ring slot
+    // b; a lane past the piece's end copies the step's first edge (in range),
+    // so the quads it never uses are finite.  Each lane reads back only the
+    // quads it copied itself.
+    const auto radial_issue = [&](int64_t base, int b) {
+      const int64_t k = base + eg < cur.hi ? base + eg : base;
+      const int64_t e = a.order ? __ldg(a.order + k) : k;
+      const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
+      float4* dst = ring + b * kStepQuads + eg * L * LPE + c4;
+#pragma unroll
+      for (int l = 1; l <= L; ++l) cp_async16(dst + (l - 1) * LPE, rr + l * C);
+    };
+    __syncwarp();  // the previous piece's reads of the ring are done
+#pragma unroll
+    for (int j = 0; j < kFwdAhead; ++j) {
+      if (cur.lo + j * EG < cur.hi) radial_issue(cur.lo + j * EG, j);
+      cp_async_commit();
+    }
+    int slot = 0;  // ring slot of the step being computed
     for (int64_t lo = cur.lo; lo < cur.hi; lo += kZonalChunk) {  // warp-uniform
       const int rows = static_cast<int>(cur.hi - lo < kZonalChunk ? cur.hi - lo : kZonalChunk);
       __syncwarp();  // the previous chunk's reads are done
@@ -234,67 +270,32 @@ __global__ void __launch_bounds__(kBlock, L >= 2 ? 2 : 3)
         }
       }
       __syncwarp();
-      int k = eg;
-      for (; k + EG < rows; k += 2 * EG) {
-        // The next step's radial rows (degrees 1..L of each of its edges,
-        // one contiguous L*C*4-byte run per edge) are requested into L2
-        // now, so they are in flight while this step's loads are (C = 64:
-        // 351 -> 335 us).  With four or more edges side by side (C <= 32)
-        // a step already has enough rows in flight and the extra requests
-        // only cost issue slots (C = 32: 226 us without, 233 us with).
-        if (EG <= 2 && c4 == 0) {
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int64_t t = lo + k + 2 * EG + u * EG;
-            if (t < cur.r.b1)
-              prefetch_l2_bulk(a.radial + (a.order ? __ldg(a.order + t) : t) * radial_row +
-                                   (slot_base + 1) * C,
-                               static_cast<uint32_t>(L * C * sizeof(float)));
-          }
-        }
-        float4 rad[2][L];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int64_t slot = lo + k + u * EG;
-          const int64_t e = a.order ? __ldg(a.order + slot) : slot;
-          const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
-#pragma unroll
-          for (int l = 1; l <= L; ++l) rad[u][l - 1] = ld_stream_f4(rr + l * C);
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const float* z = zb + (k + u * EG) * R;
-#pragma unroll
-          for (int l = 1; l <= L; ++l)
-#pragma unroll
-            for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
-              const float zr = z[r];
-              acc[r][0] = fmaf(zr, rad[u][l - 1].x, acc[r][0]);
-              acc[r][1] = fmaf(zr, rad[u][l - 1].y, acc[r][1]);
-              acc[r][2] = fmaf(zr, rad[u][l - 1].z, acc[r][2]);
-              acc[r][3] = fmaf(zr, rad[u][l - 1].w, acc[r][3]);
-            }
-        }
-      }
-      if (k < rows) {
-        const int64_t slot = lo + k;
-        const int64_t e = a.order ? __ldg(a.order + slot) : slot;
-        const float* rr = a.radial + e * radial_row + slot_base * C + 4 * c4;
-        const float* z = zb + k * R;
+      for (int k0 = 0; k0 < rows; k0 += EG) {  // warp-uniform
+        const int64_t next = lo + k0 + kFwdAhead * EG;
+        const int refill = slot == 0 ? kFwdStages - 1 : slot - 1;  // read one step ago
+        if (next < cur.hi) radial_issue(next, refill);
+        cp_async_commit();
+        cp_async_wait<kFwdAhead>();  // this step's quads have landed
+        const int k = k0 + eg;
+        const bool valid = k < rows;
+        const float* z = zb + (valid ? k : 0) * R;
+        const float4* qs = ring + slot * kStepQuads + eg * L * LPE + c4;
 #pragma unroll
         for (int l = 1; l <= L; ++l) {
-          const float4 q = ld_stream_f4(rr + l * C);
+          const float4 q = qs[(l - 1) * LPE];
 #pragma unroll
           for (int r = l * l - 1; r < (l + 1) * (l + 1) - 1; ++r) {
-            const float zr = z[r];
+            const float zr = valid ? z[r] : 0.0f;
             acc[r][0] = fmaf(zr, q.x, acc[r][0]);
             acc[r][1] = fmaf(zr, q.y, acc[r][1]);
             acc[r][2] = fmaf(zr, q.z, acc[r][2]);
             acc[r][3] = fmaf(zr, q.w, acc[r][3]);
           }
         }
+        slot = slot == kFwdStages - 1 ? 0 : slot + 1;
       }
     }
+    cp_async_wait<0>();  // no copy of this piece is left in flight
     if constexpr (EG > 1) {
 #pragma unroll
       for (int r = 0; r < R; ++r)
@@ -734,7 +735,7 @@ struct GieDegreeLayout {
   GieDegreeKernel kernel = nullptr;
   PartitionPlan plan;
   size_t bytes = 0;
-  size_t smem = 0;  // dynamic shared memory per CTA (backward)
+  size_t smem = 0;  // dynamic shared memory per CTA
   int smem_status = BYSJ_OK;
   SplitSlots ss{};
 };
@@ -757,16 +758,22 @@ size_t gie_bwd_smem_size(int64_t degrees, int64_t channels) {
   return gie_bwd_smem_bytes<3>(lpe);
 }
 
+size_t gie_fwd_smem_size(int64_t degrees) {
+  switch (degrees) {
+    case 1: return gie_fwd_smem_bytes<1>();
+    case 2: return gie_fwd_smem_bytes<2>();
+    default: return gie_fwd_smem_bytes<3>();
+  }
+}
+
 GieDegreeLayout gie_degree_layout(int64_t n_edges, int64_t n_nodes, int64_t degrees,
                                   int64_t channels, void* ws, bool backward = false) {
   GieDegreeLayout L;
   L.kernel = gie_degree_kernel(degrees, channels, backward);
   if (L.kernel == nullptr) return L;
   const int64_t rows = (degrees + 1) * (degrees + 1) - 1;
-  if (backward) {
-    L.smem = gie_bwd_smem_size(degrees, channels);
-    L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.kernel), L.smem);
-  }
+  L.smem = backward ? gie_bwd_smem_size(degrees, channels) : gie_fwd_smem_size(degrees);
+  L.smem_status = allow_dynamic_smem(reinterpret_cast<const void*>(L.kernel), L.smem);
   const DeviceInfo& dev = current_device_info();
   const int64_t resident = static_cast<int64_t>(dev.sm_count) *
                            resident_blocks(reinterpret_cast<const void*>(L.kernel), L.smem) *
@@ -863,6 +870,7 @@ int gie_forward_impl(const float* zonal, const float* radial, const int64_t* off
     D = gie_degree_layout(n_edges, n_nodes, degrees, channels,
                           workspace ? static_cast<char*>(workspace) + after256(L.bytes) : nullptr);
     need = after256(L.bytes) + D.bytes;
+    if (D.smem_status != BYSJ_OK) return D.smem_status;
   }
   if (workspace == nullptr || workspace_bytes < need)
     return fail(BYSJ_ERR_WORKSPACE,
@@ -896,7 +904,7 @@ int gie_forward_impl(const float* zonal, const float* radial, const int64_t* off
     d.lv = 0;
     d.mp = MergePath{offsets, n_nodes, n_edges, D.plan.ipc, D.plan.parts};
     d.ss = D.ss;
-    D.kernel<<<D.plan.blocks, kBlock, 0, s>>>(d, kSlotBaseOnDevice);
+    D.kernel<<<D.plan.blocks, kBlock, D.smem, s>>>(d, kSlotBaseOnDevice);
     st = launch_check("gie_fwd_degree_kernel");
     if (st) return st;
     a.skip_degrees = degrees;
@@ -984,7 +992,8 @@ int bysj_gie_zonal_scatter_forward_degree(const float* zonal, const float* radia
   a.channels = channels;
   a.mp = MergePath{offsets, n_nodes, n_edges, L.plan.ipc, L.plan.parts};
   a.ss = L.ss;
-  L.kernel<<<L.plan.blocks, kBlock, 0, s>>>(a, slot_base);
+  if (L.smem_status != BYSJ_OK) return L.smem_status;
+  L.kernel<<<L.plan.blocks, kBlock, L.smem, s>>>(a, slot_base);
   return launch_check("gie_fwd_degree_kernel");
 }
 

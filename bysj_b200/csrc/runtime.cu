@@ -81,16 +81,21 @@ const DeviceInfo& current_device_info() {
 }
 
 int allow_dynamic_smem(const void* kernel, size_t bytes) {
-  if (bytes <= 48 * 1024) return BYSJ_OK;
+  if (bytes == 0) return BYSJ_OK;
   static std::mutex m;
   static std::set<std::tuple<const void*, int, size_t>> done;
   const DeviceInfo& info = current_device_info();
   std::lock_guard<std::mutex> lock(m);
   const auto key = std::make_tuple(kernel, info.device, bytes);
   if (done.count(key)) return BYSJ_OK;
-  const int st = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(bytes)),
-                            "opt in to dynamic shared memory");
+  // The default limit is 48 KB of static and dynamic shared memory together.
+  cudaFuncAttributes attr{};
+  int st = cuda_check(cudaFuncGetAttributes(&attr, kernel), "kernel attributes");
+  if (st != BYSJ_OK) return st;
+  if (attr.sharedSizeBytes + bytes > 48 * 1024)
+    st = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(bytes)),
+                    "opt in to dynamic shared memory");
   if (st == BYSJ_OK) done.insert(key);
   return st;
 }
