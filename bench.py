@@ -43,6 +43,7 @@ frame every step and reports the same metric and config.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -1328,9 +1329,15 @@ def main():
             line = run_ours(args, dist)
             if not args.no_extra and not args.profile_small:
                 # the two other multi-GPU workloads, same ranks, same
-                # collective order on every rank; their own timings and checks
+                # collective order on every rank; their own timings and checks.
+                # They run after the headline and the per-op lines, which are
+                # measured on a fresh allocator: run first, the partition's
+                # ~130 GB left the op lines measurably slower later in the
+                # same process (the GIE forward 345 -> 357 us).
+                gc.collect()
                 torch.cuda.empty_cache()
                 chain = run_chain(extra_args(args), dist)
+                gc.collect()
                 torch.cuda.empty_cache()
                 part = run_partition(extra_args(args), dist)
                 if line is not None:
