@@ -955,16 +955,17 @@ def chain_frame(f):
     offsets = K.segment_offsets(g.dst, f["n"])
     h = K.rmsnorm(f["x"], f["scale"], 1.0e-6)
     agg = K.segment_attention(f["logit"], f["value"], offsets)
-    z = K.zonal_scatter(f["zonal"], f["radial"], g.dst, f["slot"], f["inv"])
+    z = K.zonal_scatter(f["zonal"], f["radial"], g.dst, f["slot"], f["inv"], dst_offsets=offsets)
     order, soff = K.group_by_source(g.src, f["n"])
     force, virial = K.force_assembly(f["grad"], g.unit, g.src, g.dst, offsets, soff, order)
     return h, agg, z, force, virial
 
 
 # The same calls in stages, for the two-stream pipeline of run_chain: the
-# read-backs of the public API (the offsets flags, the GIE CSR view's flags,
-# the grouping range flag) wait on their own stream only, so a frame's wait
-# overlaps the other stream's kernels.
+# read-backs of the public API (the offsets flags, the grouping range flag)
+# wait on their own stream only, so a frame's wait overlaps the other
+# stream's kernels.  The GIE takes the frame's destination CSR from the
+# offsets stage, so it reads nothing back.
 def chain_offsets(f, st):
     from bysj_b200 import kernels as K
 
@@ -982,7 +983,8 @@ def chain_zonal(f, st):
     from bysj_b200 import kernels as K
 
     g = f["g"]
-    st["z"] = K.zonal_scatter(f["zonal"], f["radial"], g.dst, f["slot"], f["inv"])
+    st["z"] = K.zonal_scatter(f["zonal"], f["radial"], g.dst, f["slot"], f["inv"],
+                              dst_offsets=st["offsets"])
 
 
 def chain_forces(f, st):
@@ -1179,7 +1181,8 @@ def run_partition(args, dist):
         out = _C.segment_attention_forward(logit, value, part.dst_offsets)
         if events is not None:
             events[1].record()
-        z = K.zonal_scatter(zonal, radial, dst_local, slot, inv_local)
+        z = K.zonal_scatter(zonal, radial, dst_local, slot, inv_local,
+                            dst_offsets=part.dst_offsets)
         return h, out, z
 
     def step(events=None):
@@ -1196,20 +1199,33 @@ def run_partition(args, dist):
     launches = dist.sum(float(local_kernels + 2)) if local_kernels is not None else None
     pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
              for _ in range(args.steps)]
+    # one event after each step: this rank's step durations, to tell a uniform
+    # slowdown from a few slow steps; the allocator's counters over the same
+    # region show whether a step had to return cached blocks and map new ones
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     clocks = ClockSampler(device)
     clocks.start()
     dist.barrier()
     torch.cuda.synchronize()
+    stats0 = torch.cuda.memory_stats(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for i in range(args.steps):
         _, (force, virial) = step(pairs[i])
+        marks[i].record()
     end.record()
     torch.cuda.synchronize()
     dist.barrier()
     clock_info = clocks.stop()
+    stats1 = torch.cuda.memory_stats(device)
+    free_b, total_b = torch.cuda.mem_get_info(device)
     step_max = dist.max(start.elapsed_time(end) / 1e3 / args.steps)
     kernel_s = statistics.mean(a.elapsed_time(b) for a, b in pairs) / 1e3
+    step_ms = [a.elapsed_time(b) for a, b in zip([start] + marks[:-1], marks)]
+    allocator = {key: int(stats1.get(key, 0) - stats0.get(key, 0))
+                 for key in ("num_alloc_retries", "num_device_alloc", "num_device_free")}
+    allocator.update(reserved_gb=round(torch.cuda.memory_reserved(device) / 1e9, 2),
+                     free_gb=round(free_b / 1e9, 2), total_gb=round(total_b / 1e9, 2))
 
     # check: repeated steps give bit-identical forces (fixed reduction orders
     # on every rank and in the collective) ...
@@ -1220,6 +1236,12 @@ def run_partition(args, dist):
     same = float(torch.equal(force, force2) and torch.equal(virial, virial2))
     repeat_same = dist.sum(same) == float(dist.world)
     del force2, virial2
+    # the GIE was given the partition's destination CSR: the same output as
+    # deriving it from dst_local (the public API's own path)
+    z_given = local_ops()[2]
+    z_derived = K.zonal_scatter(zonal, radial, dst_local, slot, inv_local)
+    csr_same = dist.sum(float(torch.equal(z_given, z_derived))) == float(dist.world)
+    del z_given, z_derived
     # ... and this rank's forces match the single-device assembly of the whole box
     order, soff = K.group_by_source(g.src, n)
     f_ref, v_ref = _C.force_assembly(grad_all, vec_all, offsets, soff, order)
@@ -1276,12 +1298,17 @@ def run_partition(args, dist):
                          "kernel_ms": kernel_s * 1e3, "peak_source": peak_src},
             "check": {"max_abs_err_vs_single_device": err, "max_abs_force": force_scale,
                       "bit_identical_repeat": repeat_same,
+                      "zonal_given_csr_equal": csr_same,
                       "exchange": "float64 source partials, NCCL reduce-scatter (sum)",
                       "nccl_algo": os.environ.get("NCCL_ALGO", "default"),
                       "nccl_proto": os.environ.get("NCCL_PROTO", "default")},
             "breakdown": {"exchange_ms": exchange_s * 1e3, "local_ms": local_s * 1e3,
                           "note": "each part timed alone (max over ranks); the timed step "
                                   "overlaps the exchange with the local operators"},
+            "steps_rank0_ms": {"min": round(min(step_ms), 3),
+                               "median": round(statistics.median(step_ms), 3),
+                               "max": round(max(step_ms), 3)},
+            "allocator_rank0": allocator,
             "clocks": clock_info,
             "gpu_launches": None if launches is None else int(launches) * args.steps,
         }
@@ -1320,6 +1347,11 @@ def main():
     if args.impl == "reference":
         run_reference(args, dist)
         return
+    # No automatic garbage collection while measuring (as timeit does): a
+    # full collection pauses the host for tens of ms, and a step whose host
+    # waits on the device once per step (a public-API read-back) turns that
+    # pause into device idle time.  Collected explicitly between lines.
+    gc.disable()
     if args.only:
         run_only(args)
         return
@@ -1328,8 +1360,9 @@ def main():
         if args.mode == "frames":
             line = run_ours(args, dist)
             if not args.no_extra and not args.profile_small:
-                # the two other multi-GPU workloads, same ranks, same
-                # collective order on every rank; their own timings and checks.
+                # the two other multi-GPU workloads (the 64-frame chain and the
+                # partitioned box), same ranks, same collective order on every
+                # rank; their own timings and checks.
                 # They run after the headline and the per-op lines, which are
                 # measured on a fresh allocator: run first, the partition's
                 # ~130 GB left the op lines measurably slower later in the

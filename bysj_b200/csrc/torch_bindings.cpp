@@ -670,14 +670,38 @@ void check_gie(const Tensor& zonal, const Tensor& radial, const Tensor& dst,
               "GIE inv_sqrt_deg must have shape (n_nodes,) or (n_nodes, 1, 1)");
 }
 
+// dst_offsets: the caller's CSR of an already grouped dst (offsets[n] =
+// number of edges with dst < n), taken as given: no derivation kernel and no
+// flags read back, so the host does not wait for the device.
+void check_dst_offsets(const Tensor& zonal, const Tensor& dst_offsets, int64_t nodes) {
+  i64(dst_offsets, "GIE dst_offsets");
+  same_device(zonal, dst_offsets, "GIE dst_offsets");
+  TORCH_CHECK(dst_offsets.dim() == 1 && dst_offsets.size(0) == nodes + 1,
+              "GIE dst_offsets must have shape (n_nodes + 1,)");
+}
+
 Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor radial_slot,
-                                 Tensor inv_sqrt_deg) {
+                                 Tensor inv_sqrt_deg, OptTensor dst_offsets) {
   check_gie(zonal, radial, dst, radial_slot, inv_sqrt_deg);
   c10::cuda::CUDAGuard guard(zonal.device());
   const int64_t edges = zonal.size(0), rows = zonal.size(1);
   const int64_t n_radial = radial.size(1), channels = radial.size(2);
   const int64_t nodes = inv_sqrt_deg.size(0);
+  if (dst_offsets) check_dst_offsets(zonal, *dst_offsets, nodes);
   if (nodes == 0) return torch::empty({nodes, rows + 1, channels}, zonal.options());
+  if (dst_offsets) {
+    Tensor out = torch::empty({nodes, rows + 1, channels}, zonal.options());
+    Tensor ws =
+        workspace(zonal, bysj_gie_zonal_scatter_workspace_size(edges, nodes, rows, channels));
+    check(bysj_gie_zonal_scatter_forward(
+              zonal.data_ptr<float>(), radial.data_ptr<float>(),
+              dst_offsets->data_ptr<int64_t>(), nullptr, radial_slot.data_ptr<int64_t>(),
+              inv_sqrt_deg.data_ptr<float>(), edges, nodes, rows, n_radial, channels,
+              out.data_ptr<float>(), ws.data_ptr(), static_cast<size_t>(ws.numel()),
+              stream_of(zonal)),
+          "gie_zonal_scatter_forward");
+    return out;
+  }
   // The slot table stays on the device: for the degree-grouped shape the
   // library launches the degree kernel and the generic one, and each checks
   // the table itself (no read back here).
@@ -717,7 +741,8 @@ Tensor gie_zonal_scatter_forward(Tensor zonal, Tensor radial, Tensor dst, Tensor
 std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output, Tensor zonal,
                                                               Tensor radial, Tensor dst,
                                                               Tensor radial_slot,
-                                                              Tensor inv_sqrt_deg) {
+                                                              Tensor inv_sqrt_deg,
+                                                              OptTensor dst_offsets) {
   check_gie(zonal, radial, dst, radial_slot, inv_sqrt_deg);
   f32(grad_output, "GIE grad_output");
   const int64_t edges = zonal.size(0), rows = zonal.size(1);
@@ -727,8 +752,25 @@ std::tuple<Tensor, Tensor, Tensor> gie_zonal_scatter_backward(Tensor grad_output
                   grad_output.size(1) == rows + 1 && grad_output.size(2) == channels,
               "GIE grad_output must have shape (n_nodes, n_rows + 1, channels)");
   c10::cuda::CUDAGuard guard(zonal.device());
+  if (dst_offsets) check_dst_offsets(zonal, *dst_offsets, nodes);
   if (nodes == 0)
     return {torch::empty_like(zonal), torch::empty_like(radial), torch::empty_like(inv_sqrt_deg)};
+  if (dst_offsets) {
+    Tensor gz = torch::empty_like(zonal);
+    Tensor gr = torch::empty_like(radial);
+    Tensor gi = torch::empty_like(inv_sqrt_deg);
+    Tensor ws = workspace(
+        zonal, bysj_gie_zonal_scatter_backward_workspace_size(edges, nodes, rows, channels));
+    check(bysj_gie_zonal_scatter_backward(
+              grad_output.data_ptr<float>(), zonal.data_ptr<float>(), radial.data_ptr<float>(),
+              dst.data_ptr<int64_t>(), dst_offsets->data_ptr<int64_t>(), nullptr,
+              radial_slot.data_ptr<int64_t>(), inv_sqrt_deg.data_ptr<float>(), edges, nodes,
+              rows, n_radial, channels, gz.data_ptr<float>(), gr.data_ptr<float>(),
+              gi.data_ptr<float>(), ws.data_ptr(), static_cast<size_t>(ws.numel()),
+              stream_of(zonal)),
+          "gie_zonal_scatter_backward");
+    return {gz, gr, gi};
+  }
   // As the forward: gated on the sorted-path flags, read early; the CSR
   // kernel is queued before the outputs and the workspace are allocated.
   auto [offsets, flags] = csr_view_launch(dst, nodes);
@@ -769,8 +811,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200 (sm_100a) segmented operators: thin shim over libbysj_b200";
   m.def("rmsnorm_forward", &rmsnorm_forward);
   m.def("rmsnorm_backward", &rmsnorm_backward);
-  m.def("gie_zonal_scatter_forward", &gie_zonal_scatter_forward);
-  m.def("gie_zonal_scatter_backward", &gie_zonal_scatter_backward);
+  m.def("gie_zonal_scatter_forward", &gie_zonal_scatter_forward, py::arg("zonal"),
+        py::arg("radial"), py::arg("dst"), py::arg("radial_slot"), py::arg("inv_sqrt_deg"),
+        py::arg("dst_offsets") = py::none());
+  m.def("gie_zonal_scatter_backward", &gie_zonal_scatter_backward, py::arg("grad_output"),
+        py::arg("zonal"), py::arg("radial"), py::arg("dst"), py::arg("radial_slot"),
+        py::arg("inv_sqrt_deg"), py::arg("dst_offsets") = py::none());
   m.def("segment_sum_forward", &segment_sum_forward, py::arg("src"), py::arg("offsets"),
         py::arg("edge_scale") = py::none(), py::arg("node_scale") = py::none(),
         py::arg("order") = py::none());

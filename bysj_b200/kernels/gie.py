@@ -55,20 +55,20 @@ def _validate(zonal, radial, dst, radial_slot, inv_sqrt_deg):
 
 class _GIEZonalScatterFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, zonal, radial, dst, radial_slot, inv_sqrt_deg):
+    def forward(ctx, zonal, radial, dst, radial_slot, inv_sqrt_deg, dst_offsets):
         output = _extension("gie_zonal_scatter_forward").gie_zonal_scatter_forward(
-            zonal, radial, dst, radial_slot, inv_sqrt_deg
+            zonal, radial, dst, radial_slot, inv_sqrt_deg, dst_offsets
         )
-        ctx.save_for_backward(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+        ctx.save_for_backward(zonal, radial, dst, radial_slot, inv_sqrt_deg, dst_offsets)
         return output
 
     @staticmethod
     def backward(ctx, grad_output):
-        zonal, radial, dst, radial_slot, inv_sqrt_deg = ctx.saved_tensors
+        zonal, radial, dst, radial_slot, inv_sqrt_deg, dst_offsets = ctx.saved_tensors
         grad_zonal, grad_radial, grad_inv = _extension(
             "gie_zonal_scatter_backward"
         ).gie_zonal_scatter_backward(
-            grad_output.contiguous(), zonal, radial, dst, radial_slot, inv_sqrt_deg
+            grad_output.contiguous(), zonal, radial, dst, radial_slot, inv_sqrt_deg, dst_offsets
         )
         needs = ctx.needs_input_grad
         return (
@@ -77,29 +77,62 @@ class _GIEZonalScatterFunction(torch.autograd.Function):
             None,
             None,
             grad_inv if needs[4] else None,
+            None,
         )
 
 
-def zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg):
+def _validate_dst_offsets(dst_offsets, dst, n_nodes):
+    if not isinstance(dst_offsets, torch.Tensor):
+        raise TypeError("GIE dst_offsets must be a tensor")
+    if dst_offsets.dtype != torch.int64:
+        raise TypeError("GIE dst_offsets must be int64")
+    if tuple(dst_offsets.shape) != (n_nodes + 1,):
+        raise ValueError("GIE dst_offsets must have shape (n_nodes + 1,)")
+    if not dst_offsets.is_contiguous():
+        raise ValueError("GIE inputs must be contiguous")
+    if dst_offsets.device != dst.device:
+        raise ValueError("all GIE inputs must share a device")
+
+
+def zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg, *, dst_offsets=None):
     """DPA4 geometric-initial-embedding zonal scatter on a B200.
 
     ``out[n, r+1, c] = inv[n] * sum_{dst[e]=n} zonal[e, r] * radial[e,
     radial_slot[r], c]``; row zero is reserved (zero).  Value tensors are
     contiguous float32, indices contiguous int64 and in range.  Gradients are
     defined for zonal, radial and the inverse degree, not for the indices.
+
+    ``dst_offsets`` (an addition to the reference signature): when ``dst`` is
+    already grouped (non-decreasing) and its CSR is at hand -- ``[n_nodes +
+    1]`` int64, ``dst_offsets[n]`` = the number of edges with ``dst < n``, as
+    ``segment_offsets(dst, n_nodes)`` returns -- pass it, and the operator
+    uses it as given instead of deriving the CSR on the device and reading
+    its flags back (no host wait; the same kernels and bits).  It is trusted
+    like the other indices; with grouping checks on, it is compared with the
+    CSR of ``dst``.
     """
     _validate(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+    if dst_offsets is not None:
+        _validate_dst_offsets(dst_offsets, dst, inv_sqrt_deg.shape[0])
     require_dcu(zonal, radial, dst, radial_slot, inv_sqrt_deg)
     if _segment._should_check(None):
         _segment.check_indices(values=radial_slot, value_limit=radial.shape[1],
                                name="GIE radial_slot")
         _segment.check_indices(values=dst, value_limit=inv_sqrt_deg.shape[0], name="GIE dst")
-    return _GIEZonalScatterFunction.apply(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+        if dst_offsets is not None:
+            _segment.check_indices(dst_offsets, dst.shape[0], name="GIE dst_offsets")
+            derived, flags = _extension("segment_offsets").segment_offsets(
+                dst, inv_sqrt_deg.shape[0])
+            if flags & _segment._FLAG_UNSORTED or not torch.equal(derived, dst_offsets):
+                raise ValueError("GIE dst_offsets: not the CSR of a grouped dst")
+    return _GIEZonalScatterFunction.apply(zonal, radial, dst, radial_slot, inv_sqrt_deg,
+                                          dst_offsets)
 
 
-def gie_zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg):
+def gie_zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg, *, dst_offsets=None):
     """Alias naming the DPA4 stage this primitive belongs to."""
-    return zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg)
+    return zonal_scatter(zonal, radial, dst, radial_slot, inv_sqrt_deg,
+                         dst_offsets=dst_offsets)
 
 
 def gie_available() -> bool:

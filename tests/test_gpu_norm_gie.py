@@ -279,3 +279,57 @@ def test_gie_degree_backward_inverse_gradient_sums_first(cuda):
     up[0, 1, :] = 0.3
     (grad,) = torch.autograd.grad(out, (inverse,), up)
     assert abs(grad.item() - 4 * 0.3 * 9.0) < 1e-4
+
+
+@pytest.mark.parametrize("rows,n_radial,channels,slot_kind",
+                         [(15, 4, 64, "degree"), (15, 4, 32, "degree"), (3, 2, 8, "generic")])
+def test_gie_dst_offsets_takes_the_given_csr(cuda, rows, n_radial, channels, slot_kind):
+    # With the CSR of a grouped dst passed in, the operator skips its own
+    # derivation and read-back: the same kernels, so the same bits as the
+    # dst-only call, forward and backward (empty nodes and a split hub in).
+    gen = torch.Generator().manual_seed(rows * channels)
+    sizes = torch.randint(0, 9, (400,), generator=gen)
+    sizes[::7] = 0
+    sizes[123] = 4000
+    dst = torch.repeat_interleave(torch.arange(400), sizes).cuda()
+    e = dst.numel()
+    off = K.segment_offsets(dst, 400)
+    zonal = torch.randn(e, rows, generator=gen).cuda().requires_grad_(True)
+    radial = torch.randn(e, n_radial, channels, generator=gen).cuda().requires_grad_(True)
+    inv = (torch.rand(400, generator=gen) + 0.2).cuda().requires_grad_(True)
+    slot = (W.degree_slots() if slot_kind == "degree" else torch.tensor([0, 1, 1])).cuda()
+    up = torch.randn(400, rows + 1, channels, generator=gen).cuda()
+    base = K.zonal_scatter(zonal, radial, dst, slot, inv)
+    given = K.zonal_scatter(zonal, radial, dst, slot, inv, dst_offsets=off)
+    assert torch.equal(base, given)
+    gb = torch.autograd.grad(base, (zonal, radial, inv), up)
+    gg = torch.autograd.grad(given, (zonal, radial, inv), up)
+    assert all(torch.equal(a, b) for a, b in zip(gb, gg))
+    empty = K.zonal_scatter(zonal[:0], radial[:0], dst[:0], slot, inv,
+                            dst_offsets=torch.zeros(401, dtype=torch.int64, device="cuda"))
+    assert empty.count_nonzero() == 0
+
+
+def test_gie_dst_offsets_arguments_and_grouping_check(cuda, monkeypatch):
+    from bysj_b200.kernels import segment as S
+
+    zonal, radial, dst, slot, inv = _small()
+    dst = torch.tensor([0, 1, 1, 1], device="cuda")
+    off = torch.tensor([0, 1, 4], device="cuda")
+    want = K.zonal_scatter(zonal, radial, dst, slot, inv)
+    assert torch.equal(K.zonal_scatter(zonal, radial, dst, slot, inv, dst_offsets=off), want)
+    with pytest.raises(TypeError, match="dst_offsets must be int64"):
+        K.zonal_scatter(zonal, radial, dst, slot, inv, dst_offsets=off.int())
+    with pytest.raises(ValueError, match=r"shape \(n_nodes \+ 1,\)"):
+        K.zonal_scatter(zonal, radial, dst, slot, inv, dst_offsets=off[:2])
+    monkeypatch.setattr(S, "_CHECK_GROUPING", True)
+    assert torch.equal(K.zonal_scatter(zonal, radial, dst, slot, inv, dst_offsets=off), want)
+    with pytest.raises(ValueError, match="GIE dst_offsets: offsets"):
+        K.zonal_scatter(zonal, radial, dst, slot, inv,
+                        dst_offsets=torch.tensor([0, 1, 5], device="cuda"))
+    with pytest.raises(ValueError, match="not the CSR of a grouped dst"):
+        K.zonal_scatter(zonal, radial, dst, slot, inv,
+                        dst_offsets=torch.tensor([0, 2, 4], device="cuda"))
+    unsorted = torch.tensor([1, 0, 1, 1], device="cuda")
+    with pytest.raises(ValueError, match="not the CSR of a grouped dst"):
+        K.zonal_scatter(zonal, radial, unsorted, slot, inv, dst_offsets=off)

@@ -315,14 +315,23 @@ def test_gie_validation_and_dispatch():
         kernels.zonal_scatter(valid[0], torch.ones(4, 2), *valid[2:])
     with pytest.raises(TypeError, match="dst and radial_slot must be int64"):
         kernels.zonal_scatter(valid[0], valid[1], valid[2].int(), valid[3], valid[4])
+    with pytest.raises(TypeError, match="dst_offsets must be a tensor"):
+        kernels.zonal_scatter(*valid, dst_offsets=[0, 1, 4])
+    with pytest.raises(TypeError, match="dst_offsets must be int64"):
+        kernels.zonal_scatter(*valid, dst_offsets=torch.tensor([0, 1, 4], dtype=torch.int32))
+    with pytest.raises(ValueError, match=r"dst_offsets must have shape \(n_nodes \+ 1,\)"):
+        kernels.zonal_scatter(*valid, dst_offsets=torch.tensor([0, 4]))
+    with pytest.raises(ValueError, match="must be contiguous"):
+        kernels.zonal_scatter(*valid, dst_offsets=torch.tensor([0, 9, 1, 9, 4, 9])[::2])
 
     class Fake:
         @staticmethod
         def gie_zonal_scatter_forward(*args):
-            return zonal_scatter_reference(*args)
+            assert args[5] is None
+            return zonal_scatter_reference(*args[:5])
 
         @staticmethod
-        def gie_zonal_scatter_backward(g, zonal, radial, dst, slot, inv):
+        def gie_zonal_scatter_backward(g, zonal, radial, dst, slot, inv, dst_offsets):
             with torch.enable_grad():
                 z, r, i = (t.detach().requires_grad_(True) for t in (zonal, radial, inv))
                 return torch.autograd.grad(zonal_scatter_reference(z, r, dst, slot, i), (z, r, i), g)
