@@ -1307,7 +1307,8 @@ def run_partition(args, dist):
                                   "overlaps the exchange with the local operators"},
             "steps_rank0_ms": {"min": round(min(step_ms), 3),
                                "median": round(statistics.median(step_ms), 3),
-                               "max": round(max(step_ms), 3)},
+                               "max": round(max(step_ms), 3),
+                               "each": [round(t, 2) for t in step_ms]},
             "allocator_rank0": allocator,
             "clocks": clock_info,
             "gpu_launches": None if launches is None else int(launches) * args.steps,
