@@ -365,3 +365,38 @@ def test_attention_validation():
             return_value=SimpleNamespace(segment_attention_forward=lambda *a: calls.append(a) or 7)):
         assert kernels.segment_attention(torch.randn(5, 2), torch.randn(5, 2, 4), offsets) == 7
     assert len(calls) == 1
+
+
+def test_gie_given_csr_reaches_both_directions():
+    # dst_offsets is handed to the forward and, saved with the inputs, to the
+    # backward entry point; the gradients keep the reference's contract.
+    zonal, radial, _, slot, inv = _gie_inputs()
+    dst = torch.tensor([0, 1, 1, 1])
+    off = torch.tensor([0, 1, 4])
+    seen = []
+
+    class Fake:
+        @staticmethod
+        def gie_zonal_scatter_forward(zonal, radial, dst, slot, inv, dst_offsets):
+            seen.append(("fwd", dst_offsets))
+            return zonal_scatter_reference(zonal, radial, dst, slot, inv)
+
+        @staticmethod
+        def gie_zonal_scatter_backward(g, zonal, radial, dst, slot, inv, dst_offsets):
+            seen.append(("bwd", dst_offsets))
+            with torch.enable_grad():
+                z, r, i = (t.detach().requires_grad_(True) for t in (zonal, radial, inv))
+                return torch.autograd.grad(zonal_scatter_reference(z, r, dst, slot, i), (z, r, i), g)
+
+    z, r, i = (t.clone().requires_grad_(True) for t in (zonal, radial, inv))
+    up = torch.randn(2, 4, 3)
+    with patch.object(gie_mod, "require_dcu"), patch.object(gie_mod, "_extension",
+                                                            return_value=Fake()):
+        out = kernels.zonal_scatter(z, r, dst, slot, i, dst_offsets=off)
+        got = torch.autograd.grad(out, (z, r, i), up)
+    assert [kind for kind, _ in seen] == ["fwd", "bwd"]
+    assert all(t is not None and torch.equal(t, off) for _, t in seen)
+    rz, rr, ri = (t.detach().clone().requires_grad_(True) for t in (zonal, radial, inv))
+    want = torch.autograd.grad(zonal_scatter_reference(rz, rr, dst, slot, ri), (rz, rr, ri), up)
+    for a, b in zip(got, want):
+        torch.testing.assert_close(a, b)
