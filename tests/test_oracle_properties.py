@@ -21,6 +21,7 @@ from oracle import truth
 from reference import (
     force_assembly_reference,
     rmsnorm,
+    rotate_back_aggregate_reference,
     rmsnorm_per_degree,
     segment_attention_reference,
     segment_softmax_reference,
@@ -233,3 +234,65 @@ def test_rmsnorm_has_unit_rms_and_no_scale(rows, degree, width, factor, seed):
     np.testing.assert_allclose(rmsnorm_per_degree(_t(x32), _t(weight)).numpy(),
                                truth.rmsnorm(x32, weight, 1e-6, per_degree=True)[0],
                                rtol=1e-5, atol=1e-6)
+
+
+def _orthogonal(rng, e, m):
+    """e random orthogonal m x m matrices (QR with the signs fixed)."""
+    q, r = np.linalg.qr(rng.normal(size=(e, m, m)))
+    return q * np.sign(np.diagonal(r, axis1=1, axis2=2))[:, None, :]
+
+
+@PROPS
+@given(graphs(max_edges=24), st.integers(0, 3), st.integers(1, 3), st.integers(1, 3), st.booleans())
+@example(NO_EDGES, 2, 2, 2, True)
+@example(LONE_NODE, 3, 2, 1, False)
+def test_rotate_back_undoes_orthogonal_rotations(g, lmax, heads, dh, rescaled):
+    # x_local = D x_global per degree block with D orthogonal: the rotate-back
+    # returns the weighted destination sum of x_global itself.
+    n, dst, _, seed = g
+    rng = np.random.default_rng(seed)
+    e, comps, channels = dst.size, (lmax + 1) ** 2, heads * dh
+    x_global = rng.normal(size=(e, comps, channels))
+    x_local = np.empty_like(x_global)
+    packed = []
+    for l in range(lmax + 1):
+        m = 2 * l + 1
+        d = _orthogonal(rng, e, m)
+        x_local[:, l * l:(l + 1) ** 2, :] = d @ x_global[:, l * l:(l + 1) ** 2, :]
+        packed.append(d.reshape(e, m * m))
+    rotation = np.concatenate(packed, axis=1) if e else np.zeros((0, truth.rotation_block_offsets(lmax)[-1]))
+    alpha = rng.uniform(0.0, 1.0, size=(e, heads))
+    rescale = rng.uniform(0.5, 2.0, size=e) if rescaled else None
+    weight = np.repeat(alpha, dh, axis=1)[:, None, :] * (1.0 if rescale is None else rescale[:, None, None])
+    want = truth.segment_sum((x_global * weight).reshape(e, comps * channels), dst, n)
+    want = want.reshape(n, comps, channels)
+    got = truth.rotate_back_aggregate(x_local, rotation, rescale, alpha, dst, n, lmax, heads)
+    np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-9)
+    f32 = [a.astype(np.float32) for a in (x_local, rotation, alpha)]
+    r32 = None if rescale is None else rescale.astype(np.float32)
+    ref = rotate_back_aggregate_reference(_t(f32[0]), _t(f32[1]), _t(r32), _t(f32[2]), None,
+                                          _t(truth.segment_offsets(dst, n)), _t(dst), lmax, heads)
+    np.testing.assert_allclose(ref.numpy(),
+                               truth.rotate_back_aggregate(*f32[:2], r32, f32[2], dst, n, lmax, heads),
+                               rtol=1e-5, atol=1e-5)
+
+
+@PROPS
+@given(st.integers(0, 6), st.integers(1, 4), st.integers(1, 5), st.integers(1, 4),
+       st.integers(0, 2**32 - 1))
+def test_edge_chain_adds_terms_and_applies_the_activation_last(e, comps, channels, n_terms, seed):
+    rng = np.random.default_rng(seed)
+    shape = (e, comps, channels)
+    kinds = [shape, (e, 1, channels), (1, comps, 1), (e, comps, 1)]
+    terms = []
+    for t in range(n_terms):
+        a = rng.normal(size=kinds[t % 4])
+        coef = float(rng.uniform(-2, 2))
+        terms.append((coef, a) if t % 2 else (coef, a, rng.normal(size=kinds[(t + 1) % 4])))
+    lin = truth.edge_chain(terms, shape)
+    np.testing.assert_allclose(lin, sum(truth.edge_chain([t], shape) for t in terms) + 0 * lin,
+                               rtol=1e-12, atol=1e-12)
+    doubled = [(2.0 * t[0],) + tuple(t[1:]) for t in terms]
+    np.testing.assert_allclose(truth.edge_chain(doubled, shape), 2.0 * lin, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(truth.edge_chain(terms, shape, "silu"),
+                               lin * truth.edge_chain(terms, shape, "sigmoid"), rtol=1e-12, atol=1e-12)
